@@ -1,0 +1,516 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE-layer hot path (one JSON line on rank 0).
+
+Default workload (config 1 of the build's configs): a 16-layer OLMoE-1B-7B-shaped MoE stack in
+decode: H=2048, 64 SwiGLU experts of I=1024, top-8, softmax without renormalisation, router
+weights and experts N(0, 0.02), every expert resident in HBM both as fp16 and as int4 gs64 (mse
+scales), per-(token, expert) precision by the threshold rule (fp16 if the router probability is
+>= 0.1, else int4), activations fp16, T tokens per step (default 64; 1/8/32 are swept too).
+A step is the hot path of all 16 layers for T tokens: router -> precision mask -> dispatch ->
+grouped gate/up GEMV -> grouped down GEMV + weighted combine, with a residual add between layers
+standing in for the dense part (out of scope). Weights are random (no checkpoint), inputs seeded.
+
+value: tokens/s with inputs resident in HBM, the step replayed as one CUDA graph.
+e2e:   tokens/s through the public modules (B200Router + B200Experts per layer), copying the step's
+       input from pinned host memory and reading its output back every step.
+--impl reference: the reference's CPU expert path (materialise to fp32 + expert_ffn + weighted
+       index_add, moelab/runtime.py:681-702) restated by the oracle, on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "moe-offload-lab_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/s"
+CFG1 = dict(name="c1", layers=16, H=2048, I=1024, E=64, k=8, renorm=False, precs=["fp16", "int4"],
+            policy=dict(mode="threshold", thr=0.1), act="fp16")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--sweep", default="1,8,32", help="extra batch sizes reported beside the headline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---- distributed plumbing ---------------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- clocks ------------------------------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi sampled every 100 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        busy = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- workload ---------------------------------------------------------------------------------------------------
+class Stack:
+    """The 16-layer MoE stack of config 1 with every record resident on the device."""
+
+    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0):
+        import moeb200
+        from moeb200 import format as F
+        from moeb200 import ops
+
+        self.cfg = cfg
+        self.dev = dev
+        L, H, I, E = cfg["layers"], cfg["H"], cfg["I"], cfg["E"]
+        self.act = {"fp16": torch.float16, "bf16": torch.bfloat16}[cfg["act"]]
+        self.lays = {p: F.record_layout(p, H, I) for p in cfg["precs"]}
+        self.policy = ops.PolicySpec(**cfg["policy"])
+        self.rt = moeb200.B200Runtime(cfg["precs"], self.lays, E, dev, self.policy, layers=range(L))
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.wr = []
+        for li in range(L):
+            self.wr.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(self.act))
+            for e in range(E):
+                gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
+                dn = torch.randn(H, I, generator=g, device=dev) * 0.02
+                for p in cfg["precs"]:
+                    self.rt.add_record(li, e, p, F.encode_record(self.lays[p], gu, dn))
+        self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"]) for w in self.wr]
+        self.experts = [moeb200.B200Experts(self.rt, li, torch.nn.SiLU(), E) for li in range(L)]
+        self.record_bytes = {p: self.lays[p]["record_bytes"] for p in cfg["precs"]}
+
+    # device-resident step: fused router (+ mask) -> experts, residual between layers
+    def make_device_step(self, T: int):
+        from moeb200 import ops
+
+        cfg, dev = self.cfg, self.dev
+        L, k, H = cfg["layers"], cfg["k"], cfg["H"]
+        self.bufs = [dict(w=torch.empty(T, k, device=dev), idx=torch.empty(T, k, dtype=torch.int64, device=dev),
+                          level=torch.empty(T, k, dtype=torch.uint8, device=dev),
+                          skip=torch.empty(T, k, dtype=torch.uint8, device=dev)) for _ in range(L)]
+        self.xs = [torch.empty(T, H, dtype=self.act, device=dev) for _ in range(L + 1)]
+        self.outs = [torch.empty(T, H, dtype=self.act, device=dev) for _ in range(L)]
+        pols = [self.policy.to_c(li) for li in range(L)]
+        tables = [self.rt._ctables[li] for li in range(L)]
+        miss = self.rt.miss
+
+        def step():
+            for li in range(L):
+                b = self.bufs[li]
+                x = self.xs[li]
+                ops.router(x, self.wr[li], k, cfg["renorm"], None, pols[li], want_probs=False, out=b)
+                ops.experts_forward(tables[li], x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li],
+                                    miss=miss)
+                torch.add(x, self.outs[li], out=self.xs[li + 1])
+        return step
+
+    def launches_per_step(self) -> int:
+        # per layer: router logits, router top-k (+ levels), dispatch (count, scan, scatter),
+        # gate/up GEMV, down GEMV, finalize
+        return self.cfg["layers"] * 8
+
+    def e2e_step(self, x_host: torch.Tensor, x_dev: torch.Tensor, y_host: torch.Tensor):
+        x_dev.copy_(x_host, non_blocking=True)
+        x = x_dev
+        for li in range(self.cfg["layers"]):
+            _, w, idx = self.routers[li](x)
+            x = x + self.experts[li](x, idx, w)
+        y_host.copy_(x, non_blocking=True)
+
+    def routing_bytes(self) -> dict:
+        """Algorithmic bytes of the last device step per layer: distinct (expert, precision)
+        records used, split into the gate/up and down matrices, plus activations."""
+        from moeb200.format import field_offsets
+
+        cfg = self.cfg
+        P = len(cfg["precs"])
+        out = {"up": 0, "down": 0, "records": 0, "pairs": 0}
+        gu_bytes, dn_bytes = {}, {}
+        for p in cfg["precs"]:
+            lay = self.lays[p]
+            f = {n: (s, d) for n, s, d, _ in lay["fields"]}
+            el = {"float16": 2, "bfloat16": 2, "float32": 4, "int8": 1, "uint8": 1}
+
+            def nb(name):
+                s, d = f[name]
+                return int(np.prod(s)) * el[d]
+
+            if "gate_up" in f:
+                gu_bytes[p], dn_bytes[p] = nb("gate_up"), nb("down")
+            else:
+                gu_bytes[p] = nb("gate_up.q") + nb("gate_up.s")
+                dn_bytes[p] = nb("down.q") + nb("down.s")
+        T, H, I = self.xs[0].shape[0], cfg["H"], cfg["I"]
+        for li in range(cfg["layers"]):
+            b = self.bufs[li]
+            idx = b["idx"].cpu().numpy()
+            lvl = b["level"].cpu().numpy()
+            skip = b["skip"].cpu().numpy().astype(bool)
+            used = set()
+            for t in range(idx.shape[0]):
+                for j in range(idx.shape[1]):
+                    if skip[t, j]:
+                        continue
+                    lv = int(lvl[t, j])
+                    slot = min(lv, P - 1) if P >= 3 else (0 if lv == 0 else P - 1)
+                    used.add((int(idx[t, j]), slot))
+                    out["pairs"] += 1
+            for (_, s) in used:
+                p = cfg["precs"][s]
+                out["up"] += gu_bytes[p]
+                out["down"] += dn_bytes[p]
+            out["records"] += len(used)
+        n_pairs = out["pairs"]
+        out["up_total"] = out["up"] + cfg["layers"] * T * H * 2 + n_pairs * I * 2
+        out["down_total"] = out["down"] + n_pairs * I * 2 + cfg["layers"] * T * H * 4
+        return out
+
+
+def time_graph(step, K: int, W: int, world: int):
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(max(3, W)):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = a.elapsed_time(b) / K
+    return g, ms
+
+
+def phase_times(stack: Stack, T: int, reps: int = 5):
+    """Average duration of the gate/up and down GEMV launches over the step, from CUDA events
+    recorded by libmoeb200 around its phases on the launching stream."""
+    import ctypes as C
+
+    from moeb200 import _lib
+
+    L = stack.cfg["layers"]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L * reps)]
+    lib = _lib.lib()
+    step = stack.make_device_step(T)
+    step()
+    torch.cuda.synchronize()
+    n = 0
+    from moeb200 import ops
+
+    cfg = stack.cfg
+    pols = [stack.policy.to_c(li) for li in range(L)]
+    for r in range(reps):
+        for li in range(L):
+            bb = stack.bufs[li]
+            x = stack.xs[li]
+            ops.router(x, stack.wr[li], cfg["k"], cfg["renorm"], None, pols[li], want_probs=False, out=bb)
+            e = evs[n]
+            for ev in e:
+                ev.record()  # materialise the events on this stream before handing them over
+            _lib.check(lib.moeb200_trace_events(C.c_void_p(e[0].cuda_event), C.c_void_p(e[1].cuda_event),
+                                                C.c_void_p(e[2].cuda_event)))
+            ops.experts_forward(stack.rt._ctables[li], x, bb["idx"], bb["w"], bb["level"], bb["skip"],
+                                out=stack.outs[li], miss=stack.rt.miss)
+            _lib.check(lib.moeb200_trace_events(None, None, None))
+            torch.add(x, stack.outs[li], out=stack.xs[li + 1])
+            n += 1
+    torch.cuda.synchronize()
+    up = [e[0].elapsed_time(e[1]) for e in evs]
+    dn = [e[1].elapsed_time(e[2]) for e in evs]
+    return float(np.mean(up)), float(np.mean(dn))
+
+
+# ---- CPU baseline (oracle restatement of the reference's CPU expert path) ---------------------------------------
+def cpu_layer_sample(stack: Stack, T: int, layer: int = 0):
+    """One layer of the workload on the host cores: returns (seconds, sample description)."""
+    from oracle import moe_oracle as O
+
+    cfg = stack.cfg
+    P = len(cfg["precs"])
+    b = stack.bufs[layer]
+    x = stack.xs[layer].float().cpu().numpy()
+    idx = b["idx"].cpu().numpy()
+    w = b["w"].cpu().numpy()
+    lvl = b["level"].cpu().numpy().astype(np.int64)
+    skip = b["skip"].cpu().numpy().astype(bool)
+    slot = np.vectorize(lambda v: O.level_to_slot(int(v), P))(lvl)
+    recs = [[stack.rt._records[(layer, e, p)].cpu().numpy() for e in range(cfg["E"])] for p in cfg["precs"]]
+    lays = [stack.lays[p] for p in cfg["precs"]]
+    t0 = time.perf_counter()
+    O.moe_layer(x, idx, w, slot, skip, recs, lays, cfg["E"])
+    dt = time.perf_counter() - t0
+    return dt, f"layer {layer} of the step at T={T} (all its routed pairs), scaled x{cfg['layers']} layers"
+
+
+def reference_arm(args, world, rank):
+    """--impl reference: the oracle port of the reference's CPU expert path on the host cores,
+    rank 0 only. Nothing of this build's CUDA library runs here: the records are built with torch
+    ops (the moelab quantiser restated in moeb200.format), routing and masks by the oracle."""
+    if rank != 0:
+        return
+    from moeb200 import format as F
+    from oracle import moe_oracle as O
+
+    cfg = CFG1
+    H, I, E, k, T = cfg["H"], cfg["I"], cfg["E"], cfg["k"], args.batch
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    g = torch.Generator(device=dev).manual_seed(0)
+    lays = [F.record_layout(p, H, I) for p in cfg["precs"]]
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).half()
+    recs = [[] for _ in cfg["precs"]]
+    for e in range(E):
+        gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
+        dn = torch.randn(H, I, generator=g, device=dev) * 0.02
+        for s_, lay in enumerate(lays):
+            recs[s_].append(F.encode_record(lay, gu, dn).cpu().numpy())
+    torch.manual_seed(1234)
+    x = torch.randn(T, H).half().float().numpy()
+    probs, w, idx, _ = O.router(x, wr.float().cpu().numpy(), k, cfg["renorm"], "float16")
+    lvl, skip = O.threshold_levels(w, cfg["policy"]["thr"])
+    slot = np.vectorize(lambda v: O.level_to_slot(int(v), len(lays)))(lvl.astype(np.int64))
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.moe_layer(x, idx, w, slot, skip, recs, lays, E)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    step_s = float(np.mean(times)) * cfg["layers"]
+    v = T / step_s
+    cores = os.cpu_count()
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"c1 OLMoE 16-layer MoE stack decode T={T}, fp16/int4 threshold 0.1",
+                       "global_batch": T, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "each step: one MoE layer of the workload (all T*k routed pairs, "
+                                       "records materialised to fp32 per call) on the host cores with numpy, "
+                                       "scaled to 16 layers"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
+    dev = torch.device("cuda", local)
+    stack = Stack(CFG1, dev, seed=0)
+    T = args.batch
+    H = CFG1["H"]
+    torch.manual_seed(1234 + rank)
+    x0 = torch.randn(T, H, device=dev).to(stack.act)
+
+    # headline: device-resident step replayed as a CUDA graph
+    step = stack.make_device_step(T)
+    stack.xs[0].copy_(x0)
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    graph, ms = time_graph(step, args.steps, args.warmup, world)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world)
+    value = T * world / (ms / 1e3)
+    rb = stack.routing_bytes()
+    miss = int(stack.rt.miss.item())
+    del graph
+
+    # roofline of the dominant kernel (gate/up GEMV) from CUDA events on its stream
+    try:
+        up_ms, dn_ms = phase_times(stack, T)
+    except Exception as exc:  # the measurement hook failed: report no roofline rather than guess
+        print(f"phase timing unavailable: {exc}", file=sys.stderr)
+        up_ms = dn_ms = float("nan")
+    L = CFG1["layers"]
+    up_bytes_launch = rb["up_total"] / L
+    dn_bytes_launch = rb["down_total"] / L
+    up_gbs = up_bytes_launch / (up_ms / 1e3) / 1e9
+    dn_gbs = dn_bytes_launch / (dn_ms / 1e3) / 1e9
+
+    # sweep of other decode batches (device-resident value only)
+    sweep = {}
+    for Ts in [int(s) for s in args.sweep.split(",") if s.strip()]:
+        st = stack.make_device_step(Ts)
+        stack.xs[0].copy_(torch.randn(Ts, H, device=dev).to(stack.act))
+        g2, ms2 = time_graph(st, max(5, args.steps // 2), 3, world)
+        del g2
+        ms2 = max_over_ranks(ms2, world)
+        rb2 = stack.routing_bytes()
+        sweep[str(Ts)] = {"tokens_per_s": Ts * world / (ms2 / 1e3), "ms_per_step": ms2,
+                          "record_gbs": (rb2["up"] + rb2["down"]) / (ms2 / 1e3) / 1e9}
+
+    # end to end through the public modules, host copies inside the timed region
+    x_host = x0.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x0)
+    for _ in range(args.warmup):
+        stack.e2e_step(x_host, x_dev, y_host)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        stack.e2e_step(x_host, x_dev, y_host)
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    e2e = T * world / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        stack.make_device_step(T)
+        stack.xs[0].copy_(x0)
+        st = stack.make_device_step(T)
+        stack.xs[0].copy_(x0)
+        st()
+        torch.cuda.synchronize()
+        dt, sample = cpu_layer_sample(stack, T, layer=0)
+        cpu = {"value": T / (dt * L), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 activations, fp16+int4 gs64 records, f32 accumulation",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) random-init experts and routers)",
+            "config": {"workload": f"c1 OLMoE-1B-7B 16-layer MoE stack decode, T={T}/GPU, "
+                                   "fp16/int4 by router prob >= 0.1, all experts resident",
+                       "global_batch": T * world, "layers": L, "experts": CFG1["E"], "top_k": CFG1["k"],
+                       "hidden": H, "inter": CFG1["I"], "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+                       "l2": "no flush: each step streams ~%.1f GB of records (> 126 MB L2)" % (
+                           (rb["up"] + rb["down"]) / 1e9),
+                       "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks"},
+            "int4_fp16_record_gbs": (rb["up"] + rb["down"]) / (ms / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "gemv up (gate/up dequant GEMV + SwiGLU)",
+                         "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": up_gbs / hbm_peak,
+                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": up_bytes_launch,
+                         "launch_ms": up_ms, "down_achieved": dn_gbs, "down_launch_ms": dn_ms},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+            "gpu_launches": stack.launches_per_step() * args.steps,
+            "clocks": clk,
+            "sweep": sweep,
+            "missing_pairs": miss,
+            "records_per_step": rb["records"], "pairs_per_step": rb["pairs"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

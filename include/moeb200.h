@@ -1,0 +1,163 @@
+/*
+ * moeb200 -- C ABI of the B200-native MoE-layer hot path.
+ *
+ * A drop-in for the compute behind moelab's `OffloadedExperts` module (moelab/runtime.py:1094-1112)
+ * and for the transformers router it keeps (`parent.gate`, moelab/loader.py:222-223). Every entry
+ * point takes plain device pointers, sizes and a cudaStream_t passed as void*; none allocates, and
+ * apart from moeb200_check_workspace none synchronises or reads device memory on the host, so those
+ * calls can be recorded in a CUDA graph.
+ * Every entry point returns a status (0 = OK); moeb200_last_error() gives the message of the last
+ * failure on the calling thread.
+ *
+ * Data formats follow moelab exactly:
+ *  - expert records: one uint8 blob per (layer, expert, precision) with the field table of
+ *    moelab/store.py:76-115 (gate_up [2I,H] then down [H,I]; int8/int4 add fp16 scales per group
+ *    of gs input columns; int4 packs two values per byte, low nibble = even column, stored +8).
+ *  - routing: top_k_index int64 [T,k], top_k_weights float32 [T,k] (transformers TopKRouter).
+ *  - precision levels: uint8 [T,k], 0 = most precise precision of the store (moelab/policy.py).
+ */
+#ifndef MOEB200_H
+#define MOEB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+enum {
+  MOEB200_OK = 0,
+  MOEB200_ERR_INVALID = 1,     /* bad argument: shape, type, alignment or null pointer        */
+  MOEB200_ERR_UNSUPPORTED = 2, /* valid for moelab, not handled by these kernels (message says) */
+  MOEB200_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed                 */
+  MOEB200_ERR_WORKSPACE = 4    /* workspace smaller than the *_workspace() query returned      */
+};
+
+/* ---- element types ------------------------------------------------------------------------ */
+enum { MOEB200_F32 = 0, MOEB200_F16 = 1, MOEB200_BF16 = 2, MOEB200_I8 = 3, MOEB200_I4 = 4 };
+
+/* Field table of one expert record (mirror of moelab/store.py:76-115 `record_layout`).
+ * wtype: F32/F16/BF16 for float records, I8/I4 for quantised ones.
+ * Float records: off_gu_q = offset of gate_up, off_dn_q = offset of down, *_s = -1, gs_* = 0. */
+typedef struct {
+  int32_t wtype;
+  int32_t hidden;
+  int32_t inter;
+  int32_t gs_up;
+  int32_t gs_dn;
+  int32_t _pad;
+  int64_t off_gu_q;
+  int64_t off_gu_s;
+  int64_t off_dn_q;
+  int64_t off_dn_s;
+  int64_t record_bytes;
+} moeb200_layout;
+
+/* Precision policy (mirror of moelab/policy.py:20-58 PrecisionPolicy, plus the build's threshold
+ * rule). mode: 0 "hi" (every pair level 0), 1 "lo" (every pair level 2), 2 "hobbit",
+ * 3 "threshold" (level 0 if the pair's router weight >= thr, else level 2).
+ * t_mid / t2 < 0 mean "unset" (None in the reference). */
+typedef struct {
+  int32_t mode;
+  float t1;
+  float t_mid;
+  float t2;
+  float thr;
+} moeb200_policy;
+
+/* Device table of resident expert records for one layer (mirror of moelab/fullgraph.py:43-98
+ * DeviceTable): table[p * E + e] = device address of expert e's record at precision slot p
+ * (0 = not resident). Precision slots are ordered most precise first, as moelab's store lists. */
+typedef struct {
+  int32_t n_prec;
+  int32_t num_experts;
+  moeb200_layout layout[4];
+  const int64_t* table;
+} moeb200_expert_table;
+
+const char* moeb200_version(void);
+
+/* Copies the last error message of the calling thread into buf (always NUL-terminated).
+ * Returns the status of that failure. */
+int moeb200_last_error(char* buf, size_t n);
+
+/* Number of SMs of the current device (cached per device). */
+int moeb200_num_sms(void);
+
+/* Measurement hook (no reference counterpart): CUDA events (cudaEvent_t) that the grouped-expert
+ * entry points of the calling thread record on their stream before the gate/up GEMV, between the
+ * two GEMVs and after the down GEMV. NULLs switch it off. */
+int moeb200_trace_events(void* up_begin, void* up_end, void* down_end);
+
+/* ---- router --------------------------------------------------------------------------------
+ * Replaces transformers OlmoeTopKRouter / Qwen3MoeTopKRouter / Qwen3NextTopKRouter.forward
+ * (olmoe/modeling_olmoe.py:350-359, qwen3_moe/modeling_qwen3_moe.py:254-272,
+ *  qwen3_next/modeling_qwen3_next.py:761-779): logits = h . Wr^T accumulated in fp32 and rounded
+ * to the model dtype, + bias[e] (fp32, optional synthetic skew), probs = softmax in fp32 over all
+ * E, top-k with ties broken by the lower expert index, optional renormalisation of the k weights.
+ * h [T,H] and wr [E,H] are act_type (F16/BF16/F32). probs [T,E] may be NULL.
+ * If policy != NULL the HOBBIT / threshold levels of each pair are also written to level [T,k]
+ * and skip [T,k] (uint8, 1 = skipped). */
+int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H,
+                   int32_t E, int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx,
+                   const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
+                   void* stream);
+size_t moeb200_router_workspace(int32_t T, int32_t E);
+
+/* ---- precision levels ----------------------------------------------------------------------
+ * Replaces PrecisionPolicy.levels / levels_one (moelab/policy.py:110-137) and the device version
+ * gpu_levels (moelab/fullgraph.py:101-114): w [T,k] fp32 -> level [T,k] uint8 in {0,1,2},
+ * skip [T,k] uint8 (may be NULL). */
+int moeb200_levels(const float* w, int32_t T, int32_t k, const moeb200_policy* policy, uint8_t* level,
+                   uint8_t* skip, void* stream);
+
+/* ---- dispatch --------------------------------------------------------------------------------
+ * Replaces the routing part of MoERuntime._decide_general (moelab/runtime.py:459-492): pairs
+ * (t, j) not skipped are flattened to p = t*k + j and sorted stably
+ *   - by expert:                counts_e [E], pos_e [T*k]   (= flat_pos[order], counts of
+ *                               unique_consecutive with zeros kept),
+ *   - by (expert, slot):        counts_k [E*P], pos_k [T*k],
+ * where slot = level_to_precision(level) (moelab/policy.py:188-192) over P precisions.
+ * n_kept [1] receives the number of kept pairs. level/skip may be NULL (all level 0 / none). */
+int moeb200_dispatch(const int64_t* idx, const uint8_t* level, const uint8_t* skip, int32_t T, int32_t k,
+                     int32_t E, int32_t P, int32_t* counts_e, int32_t* pos_e, int32_t* counts_k,
+                     int32_t* pos_k, int32_t* n_kept, void* ws, size_t ws_bytes, void* stream);
+size_t moeb200_dispatch_workspace(int32_t T, int32_t k, int32_t E, int32_t P);
+
+/* ---- grouped expert products for one token --------------------------------------------------
+ * Replaces grouped_ffn_int4 (moelab/kernels.py:834-872), grouped_ffn_int8 (kernels.py:747-769) and
+ * grouped_ffn_float (kernels.py:875-891): out[H] += sum_e w[e] * down_e(silu(gate_e x) * up_e x)
+ * for n experts sharing one layout. tab [n,4] (device) holds per expert the field addresses
+ * [gate_up.q, gate_up.s, down.q, down.s] (float records: [gate_up, gate_up, down, down]), exactly
+ * the pointer table of kernels.py:230-244. A row whose weight is 0 is a no-op (fixed-size tables,
+ * kernels.py:903-905). x [H] and out [H] are act_type; accumulation is fp32. */
+int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const float* w, int32_t n,
+                        const void* x, int32_t act_type, void* out, void* ws, size_t ws_bytes, void* stream);
+size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n);
+
+/* ---- the experts module ------------------------------------------------------------------------
+ * Replaces OffloadedExperts.forward -> MoERuntime.run_layer for experts resident on this GPU
+ * (moelab/runtime.py:522-770 with every request a VRAM hit; fullgraph.py:149-188 on device):
+ * out[T,H] = sum over kept pairs (t,j) of w[t,j] * expert_{idx[t,j]}(x[t]) evaluated at the pair's
+ * precision slot (level_to_precision of level[t,j]). out is overwritten (act_type).
+ * level/skip may be NULL (every pair at slot 0). A pair whose expert has no resident record at its
+ * slot is skipped and counted in miss [1] (fullgraph.py `flag`); miss may be NULL. */
+int moeb200_experts_forward(const moeb200_expert_table* experts, const void* x, int32_t act_type, int32_t T,
+                            const int64_t* idx, const float* w, int32_t k, const uint8_t* level,
+                            const uint8_t* skip, void* out, int32_t* miss, void* ws, size_t ws_bytes,
+                            void* stream);
+size_t moeb200_experts_workspace(const moeb200_expert_table* experts, int32_t T, int32_t k);
+
+/* Every workspace starts with a device status word that kernels set instead of hanging or
+ * faulting (0 = OK, 1 = a bounded wait gave up, 2 = an expert index outside [0, E) reached
+ * dispatch). This call copies it to *status and clears it; it is the one entry point that
+ * synchronises the stream, so keep it out of captured graphs. */
+int moeb200_check_workspace(void* ws, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOEB200_H */

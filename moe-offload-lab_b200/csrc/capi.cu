@@ -1,0 +1,489 @@
+// extern "C" entry points of libmoeb200 (declared in include/moeb200.h).
+//
+// Host-side validation, workspace carving and kernel sequencing. Nothing here allocates device
+// memory, synchronises a stream (except moeb200_check_workspace) or reads device data, so every
+// entry point can be recorded in a CUDA graph.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "route.cuh"
+
+namespace moeb200 {
+int gemv_occupancy(int act_type, int nb, bool up, int smem);
+}
+
+using namespace moeb200;
+
+namespace {
+
+thread_local std::string g_err;
+thread_local int g_err_code = MOEB200_OK;
+// Optional CUDA events recorded around the GEMV phases of the next expert calls (measurement).
+thread_local cudaEvent_t g_trace[3] = {nullptr, nullptr, nullptr};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  g_err_code = code;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                       \
+  do {                                                                                       \
+    cudaError_t e_ = (expr);                                                                 \
+    if (e_ != cudaSuccess) return fail(MOEB200_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr size_t kAlign = 256;
+
+// Workspace carving: the same walk sizes (base == nullptr) and hands out sub-buffers.
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + kAlign - 1) / kAlign * kAlign;
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+// Header of every workspace: status word and small device counters.
+struct WsHeader {
+  int32_t status;
+  int32_t n_items;
+  int32_t n_kept;
+  int32_t miss;
+};
+
+int act_bytes(int act) { return act == MOEB200_F32 ? 4 : 2; }
+
+int num_sms_cached() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+bool is_int(int wt) { return wt == MOEB200_I4 || wt == MOEB200_I8; }
+
+// Host mirror of the device chunk-kind choice (gemv.cu kind_of): returns false if unsupported.
+bool matrix_supported(int wt, int K, int gs, const char* name, std::string& why) {
+  char b[256];
+  switch (wt) {
+    case MOEB200_I4:
+      if (gs > 0 && gs % 32 == 0 && K % 32 == 0 && K % gs == 0) return true;
+      snprintf(b, sizeof b, "%s: int4 needs a group size multiple of 32 dividing K (K=%d, gs=%d)", name, K, gs);
+      break;
+    case MOEB200_I8:
+      if (gs > 0 && gs % 16 == 0 && K % 16 == 0 && K % gs == 0) return true;
+      snprintf(b, sizeof b, "%s: int8 needs a group size multiple of 16 dividing K (K=%d, gs=%d)", name, K, gs);
+      break;
+    case MOEB200_F16:
+    case MOEB200_BF16:
+    case MOEB200_F32:
+      if (K % 16 == 0) return true;
+      snprintf(b, sizeof b, "%s: float records need K %% 16 == 0 (K=%d)", name, K);
+      break;
+    default:
+      snprintf(b, sizeof b, "%s: unknown record element type %d", name, wt);
+  }
+  why = b;
+  return false;
+}
+
+int check_layout(const moeb200_layout& L, int H, int I) {
+  if (L.hidden != H || L.inter != I)
+    return fail(MOEB200_ERR_INVALID, "layouts disagree on shapes (%d,%d) vs (%d,%d)", L.hidden, L.inter, H, I);
+  std::string why;
+  if (!matrix_supported(L.wtype, H, L.gs_up, "gate_up", why)) return fail(MOEB200_ERR_UNSUPPORTED, "%s", why.c_str());
+  if (!matrix_supported(L.wtype, I, L.gs_dn, "down", why)) return fail(MOEB200_ERR_UNSUPPORTED, "%s", why.c_str());
+  if (L.off_gu_q < 0 || L.off_dn_q < 0 || (L.off_gu_q % 16) || (L.off_dn_q % 16))
+    return fail(MOEB200_ERR_INVALID, "record field offsets must be 16-byte aligned");
+  if (is_int(L.wtype) && (L.off_gu_s < 0 || L.off_dn_s < 0 || (L.off_gu_s % 16) || (L.off_dn_s % 16)))
+    return fail(MOEB200_ERR_INVALID, "scale field offsets must be 16-byte aligned");
+  return MOEB200_OK;
+}
+
+int check_shapes(int H, int I) {
+  if (H <= 0 || I <= 0 || H % 32 != 0 || I % 16 != 0)
+    return fail(MOEB200_ERR_UNSUPPORTED, "hidden must be a multiple of 32 and inter of 16 (H=%d, I=%d)", H, I);
+  if (H % 8 || I % 8) return fail(MOEB200_ERR_UNSUPPORTED, "H and I must be multiples of 8");
+  return MOEB200_OK;
+}
+
+int scale_slot_bytes(const moeb200_layout* L, int n) {
+  int ng = 1;
+  for (int i = 0; i < n; ++i)
+    if (is_int(L[i].wtype)) {
+      ng = std::max(ng, L[i].hidden / L[i].gs_up);
+      ng = std::max(ng, L[i].inter / L[i].gs_dn);
+    }
+  return 64 * ng;
+}
+
+struct ForwardWs {
+  WsHeader* hdr;
+  int32_t *pos_e, *pos_k, *counts_e, *counts_k, *offs_k, *blk_k, *blk_e, *rank_k, *rank_e;
+  Item* items;
+  uint8_t* h;
+  float* acc;
+  float* logits;
+  size_t bytes;
+};
+
+ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, int act) {
+  Carve c(base);
+  ForwardWs w{};
+  const int n = T * k;
+  const int keys = E * P;
+  const int nblk = (n + kDispBlock - 1) / kDispBlock;
+  w.hdr = c.take<WsHeader>(1);
+  w.pos_e = c.take<int32_t>(n);
+  w.pos_k = c.take<int32_t>(n);
+  w.counts_e = c.take<int32_t>(E);
+  w.counts_k = c.take<int32_t>(keys);
+  w.offs_k = c.take<int32_t>(keys);
+  w.blk_k = c.take<int32_t>((size_t)nblk * keys);
+  w.blk_e = c.take<int32_t>((size_t)nblk * E);
+  w.rank_k = c.take<int32_t>(n);
+  w.rank_e = c.take<int32_t>(n);
+  w.items = c.take<Item>(n);
+  w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
+  w.acc = c.take<float>((size_t)T * H);
+  w.bytes = c.off;
+  return w;
+}
+
+LayoutDev to_dev(const moeb200_layout& L) {
+  LayoutDev d{};
+  d.wtype = L.wtype;
+  d.gs_up = L.gs_up;
+  d.gs_dn = L.gs_dn;
+  return d;
+}
+
+int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int act, int max_items, int nt,
+                      cudaStream_t s, void* out, int add) {
+  gp.scale_slot_bytes = scale_slot_bytes(lays, nlay);
+  const int smem = gemv_smem_bytes(gp.scale_slot_bytes);
+  if (smem > 227 * 1024) return fail(MOEB200_ERR_UNSUPPORTED, "too many scale groups per row for the GEMV stages");
+  const int nb = nt > 8 ? 2 : 1;
+  const int sms = num_sms_cached();
+  const int occ_up = std::max(1, gemv_occupancy(act, nb, true, smem));
+  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, smem));
+  const int64_t tiles_up = (int64_t)max_items * (gp.I / 16);
+  const int64_t tiles_dn = (int64_t)max_items * (gp.H / 32);
+  const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + kGemvWarps - 1) / kGemvWarps));
+  const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + kGemvWarps - 1) / kGemvWarps));
+  if (g_trace[0]) CUDA_TRY(cudaEventRecord(g_trace[0], s));
+  CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, s));
+  if (g_trace[1]) CUDA_TRY(cudaEventRecord(g_trace[1], s));
+  CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, s));
+  if (g_trace[2]) CUDA_TRY(cudaEventRecord(g_trace[2], s));
+  CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
+  return MOEB200_OK;
+}
+
+__global__ void table_items_kernel(const int64_t* __restrict__ tab, const float* __restrict__ w, int n,
+                                   Item* __restrict__ items, int32_t* __restrict__ n_items, int32_t* __restrict__ pos) {
+  // one block: compact the rows whose weight is non-zero into one-token items
+  __shared__ int32_t base;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    const bool on = i < n && w[i] != 0.f;
+    const uint32_t bal = __ballot_sync(0xffffffffu, on);
+    const int lane = threadIdx.x & 31;
+    int wbase = 0;
+    if (lane == 0 && bal) wbase = atomicAdd(&base, __popc(bal));
+    wbase = __shfl_sync(0xffffffffu, wbase, 0);
+    if (on) {
+      const int j = wbase + __popc(bal & ((1u << lane) - 1u));
+      Item it;
+      it.p_guq = tab[4 * (int64_t)i + 0];
+      it.p_gus = tab[4 * (int64_t)i + 1];
+      it.p_dnq = tab[4 * (int64_t)i + 2];
+      it.p_dns = tab[4 * (int64_t)i + 3];
+      it.slot = 0;
+      it.start = j;
+      it.ntok = 1;
+      it._pad = i;
+      items[j] = it;
+      pos[j] = i;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_items = base;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* moeb200_version(void) { return "moeb200 0.1 (sm_100a)"; }
+
+int moeb200_last_error(char* buf, size_t n) {
+  if (buf && n) {
+    strncpy(buf, g_err.c_str(), n - 1);
+    buf[n - 1] = '\0';
+  }
+  return g_err_code;
+}
+
+int moeb200_num_sms(void) { return num_sms_cached(); }
+
+int moeb200_trace_events(void* up_begin, void* up_end, void* down_end) {
+  g_trace[0] = static_cast<cudaEvent_t>(up_begin);
+  g_trace[1] = static_cast<cudaEvent_t>(up_end);
+  g_trace[2] = static_cast<cudaEvent_t>(down_end);
+  return MOEB200_OK;
+}
+
+size_t moeb200_router_workspace(int32_t T, int32_t E) {
+  Carve c(nullptr);
+  c.take<WsHeader>(1);
+  c.take<float>((size_t)T * E);
+  return c.off;
+}
+
+int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H, int32_t E,
+                   int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, const moeb200_policy* policy,
+                   uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes, void* stream) {
+  if (!h || !wr || !w || !idx) return fail(MOEB200_ERR_INVALID, "router: null pointer");
+  if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 1024)
+    return fail(MOEB200_ERR_INVALID, "router: bad sizes T=%d H=%d E=%d k=%d (k <= 32, E <= 1024)", T, H, E, k);
+  if (act_type != MOEB200_F16 && act_type != MOEB200_BF16 && act_type != MOEB200_F32)
+    return fail(MOEB200_ERR_INVALID, "router: activation type must be F16, BF16 or F32");
+  if (H % (act_type == MOEB200_F32 ? 4 : 8)) return fail(MOEB200_ERR_UNSUPPORTED, "router: H must be a multiple of 8");
+  if (policy && !level) return fail(MOEB200_ERR_INVALID, "router: policy given without a level output");
+  if (ws_bytes < moeb200_router_workspace(T, E)) return fail(MOEB200_ERR_WORKSPACE, "router: workspace too small");
+  Carve c(ws);
+  WsHeader* hdr = c.take<WsHeader>(1);
+  (void)hdr;
+  float* logits = c.take<float>((size_t)T * E);
+  PolicyDev pd{};
+  if (policy) pd = {policy->mode, policy->t1, policy->t_mid, policy->t2, policy->thr};
+  CUDA_TRY(launch_router(h, wr, bias, act_type, T, H, E, k, renorm, logits, probs, w, idx, policy ? &pd : nullptr,
+                         level, skip, static_cast<cudaStream_t>(stream)));
+  return MOEB200_OK;
+}
+
+int moeb200_levels(const float* w, int32_t T, int32_t k, const moeb200_policy* policy, uint8_t* level, uint8_t* skip,
+                   void* stream) {
+  if (!w || !policy || !level) return fail(MOEB200_ERR_INVALID, "levels: null pointer");
+  if (T <= 0 || k <= 0 || k > 32) return fail(MOEB200_ERR_INVALID, "levels: bad sizes T=%d k=%d", T, k);
+  if (policy->mode < 0 || policy->mode > 3) return fail(MOEB200_ERR_INVALID, "levels: unknown mode %d", policy->mode);
+  PolicyDev pd{policy->mode, policy->t1, policy->t_mid, policy->t2, policy->thr};
+  CUDA_TRY(launch_levels(w, T, k, pd, level, skip, static_cast<cudaStream_t>(stream)));
+  return MOEB200_OK;
+}
+
+size_t moeb200_dispatch_workspace(int32_t T, int32_t k, int32_t E, int32_t P) {
+  const int n = T * k;
+  const int nblk = (n + kDispBlock - 1) / kDispBlock;
+  Carve c(nullptr);
+  c.take<WsHeader>(1);
+  c.take<int32_t>((size_t)nblk * E * P);
+  c.take<int32_t>((size_t)nblk * E);
+  c.take<int32_t>(n);
+  c.take<int32_t>(n);
+  c.take<int32_t>((size_t)E * P);
+  return c.off;
+}
+
+int moeb200_dispatch(const int64_t* idx, const uint8_t* level, const uint8_t* skip, int32_t T, int32_t k, int32_t E,
+                     int32_t P, int32_t* counts_e, int32_t* pos_e, int32_t* counts_k, int32_t* pos_k, int32_t* n_kept,
+                     void* ws, size_t ws_bytes, void* stream) {
+  if (!idx || !counts_e || !pos_e || !counts_k || !pos_k) return fail(MOEB200_ERR_INVALID, "dispatch: null pointer");
+  if (T <= 0 || k <= 0 || E <= 0 || P <= 0 || P > 4 || (int64_t)E * P > kMaxKeys || (int64_t)T * k >= (1ll << 30))
+    return fail(MOEB200_ERR_INVALID, "dispatch: bad sizes T=%d k=%d E=%d P=%d (E*P <= %d)", T, k, E, P, kMaxKeys);
+  if (ws_bytes < moeb200_dispatch_workspace(T, k, E, P)) return fail(MOEB200_ERR_WORKSPACE, "dispatch: workspace too small");
+  const int n = T * k;
+  DispatchParams dp{};
+  Carve c(ws);
+  WsHeader* hdr = c.take<WsHeader>(1);
+  dp.nblk = (n + kDispBlock - 1) / kDispBlock;
+  dp.blk_k = c.take<int32_t>((size_t)dp.nblk * E * P);
+  dp.blk_e = c.take<int32_t>((size_t)dp.nblk * E);
+  dp.rank_k = c.take<int32_t>(n);
+  dp.rank_e = c.take<int32_t>(n);
+  dp.offs_k = c.take<int32_t>((size_t)E * P);
+  dp.idx = idx;
+  dp.level = level;
+  dp.skip = skip;
+  dp.T = T;
+  dp.k = k;
+  dp.E = E;
+  dp.P = P;
+  dp.nt = 8;
+  dp.counts_e = counts_e;
+  dp.pos_e = pos_e;
+  dp.counts_k = counts_k;
+  dp.pos_k = pos_k;
+  dp.n_kept = n_kept;
+  dp.status = &hdr->status;
+  CUDA_TRY(launch_dispatch(dp, static_cast<cudaStream_t>(stream)));
+  return MOEB200_OK;
+}
+
+size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
+  if (!layout || n <= 0) return 0;
+  Carve c(nullptr);
+  c.take<WsHeader>(1);
+  c.take<Item>(n);
+  c.take<int32_t>(n);
+  c.take<uint8_t>((size_t)n * layout->inter * 2);
+  c.take<float>((size_t)layout->hidden);
+  return c.off;
+}
+
+int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const float* w, int32_t n, const void* x,
+                        int32_t act_type, void* out, void* ws, size_t ws_bytes, void* stream) {
+  if (!layout || !tab || !w || !x || !out || !ws) return fail(MOEB200_ERR_INVALID, "grouped_ffn: null pointer");
+  if (n <= 0 || n > 4096) return fail(MOEB200_ERR_INVALID, "grouped_ffn: n=%d out of range", n);
+  if (act_type != MOEB200_F16 && act_type != MOEB200_BF16)
+    return fail(MOEB200_ERR_UNSUPPORTED, "grouped_ffn: activations must be F16 or BF16 (tensor-core operands)");
+  const int H = layout->hidden, I = layout->inter;
+  int rc = check_shapes(H, I);
+  if (rc) return rc;
+  rc = check_layout(*layout, H, I);
+  if (rc) return rc;
+  if (ws_bytes < moeb200_grouped_ffn_workspace(layout, n))
+    return fail(MOEB200_ERR_WORKSPACE, "grouped_ffn: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carve c(ws);
+  WsHeader* hdr = c.take<WsHeader>(1);
+  Item* items = c.take<Item>(n);
+  int32_t* pos = c.take<int32_t>(n);
+  uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
+  float* acc = c.take<float>((size_t)H);
+  table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
+  CUDA_TRY(cudaGetLastError());
+  GemvParams gp{};
+  gp.items = items;
+  gp.n_items = &hdr->n_items;
+  gp.pos = pos;
+  gp.wflat = w;
+  gp.k = n;
+  gp.H = H;
+  gp.I = I;
+  gp.T = 1;
+  gp.x = x;
+  gp.h = hbuf;
+  gp.acc = acc;
+  gp.status = &hdr->status;
+  gp.lay[0] = to_dev(*layout);
+  gp.zero_acc = 1;
+  return run_expert_phases(gp, layout, 1, act_type, n, 8, s, out, /*add=*/1);
+}
+
+size_t moeb200_experts_workspace(const moeb200_expert_table* ex, int32_t T, int32_t k) {
+  if (!ex || ex->n_prec <= 0) return 0;
+  return carve_forward(nullptr, T, k, ex->num_experts, ex->n_prec, ex->layout[0].hidden, ex->layout[0].inter, MOEB200_F16)
+      .bytes;
+}
+
+int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32_t act_type, int32_t T,
+                            const int64_t* idx, const float* w, int32_t k, const uint8_t* level, const uint8_t* skip,
+                            void* out, int32_t* miss, void* ws, size_t ws_bytes, void* stream) {
+  if (!ex || !ex->table || !x || !idx || !w || !out || !ws) return fail(MOEB200_ERR_INVALID, "experts_forward: null pointer");
+  const int P = ex->n_prec, E = ex->num_experts;
+  if (P <= 0 || P > 4 || E <= 0 || (int64_t)E * P > kMaxKeys)
+    return fail(MOEB200_ERR_INVALID, "experts_forward: bad table (P=%d, E=%d, E*P <= %d)", P, E, kMaxKeys);
+  if (T <= 0 || k <= 0 || k > 32 || (int64_t)T * k >= (1ll << 30))
+    return fail(MOEB200_ERR_INVALID, "experts_forward: bad sizes T=%d k=%d", T, k);
+  if (act_type != MOEB200_F16 && act_type != MOEB200_BF16)
+    return fail(MOEB200_ERR_UNSUPPORTED, "experts_forward: activations must be F16 or BF16");
+  const int H = ex->layout[0].hidden, I = ex->layout[0].inter;
+  int rc = check_shapes(H, I);
+  if (rc) return rc;
+  for (int p = 0; p < P; ++p) {
+    rc = check_layout(ex->layout[p], H, I);
+    if (rc) return rc;
+  }
+  ForwardWs fw = carve_forward(nullptr, T, k, E, P, H, I, act_type);
+  if (ws_bytes < fw.bytes) return fail(MOEB200_ERR_WORKSPACE, "experts_forward: workspace too small (%zu < %zu)", ws_bytes, fw.bytes);
+  fw = carve_forward(ws, T, k, E, P, H, I, act_type);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n = T * k;
+  const int nt = T >= 128 ? 16 : 8;
+  DispatchParams dp{};
+  dp.idx = idx;
+  dp.level = level;
+  dp.skip = skip;
+  dp.T = T;
+  dp.k = k;
+  dp.E = E;
+  dp.P = P;
+  dp.nblk = (n + kDispBlock - 1) / kDispBlock;
+  dp.nt = nt;
+  dp.counts_e = fw.counts_e;
+  dp.pos_e = fw.pos_e;
+  dp.counts_k = fw.counts_k;
+  dp.offs_k = fw.offs_k;
+  dp.pos_k = fw.pos_k;
+  dp.n_kept = &fw.hdr->n_kept;
+  dp.blk_k = fw.blk_k;
+  dp.blk_e = fw.blk_e;
+  dp.rank_k = fw.rank_k;
+  dp.rank_e = fw.rank_e;
+  dp.items = fw.items;
+  dp.n_items = &fw.hdr->n_items;
+  dp.table = ex->table;
+  for (int p = 0; p < P; ++p) {
+    const moeb200_layout& L = ex->layout[p];
+    dp.offs[p] = {L.off_gu_q, is_int(L.wtype) ? L.off_gu_s : 0, L.off_dn_q, is_int(L.wtype) ? L.off_dn_s : 0};
+  }
+  dp.miss = miss ? miss : &fw.hdr->miss;
+  dp.status = &fw.hdr->status;
+  CUDA_TRY(launch_dispatch(dp, s));
+  GemvParams gp{};
+  gp.items = fw.items;
+  gp.n_items = &fw.hdr->n_items;
+  gp.pos = fw.pos_k;
+  gp.wflat = w;
+  gp.k = k;
+  gp.H = H;
+  gp.I = I;
+  gp.T = T;
+  gp.x = x;
+  gp.h = fw.h;
+  gp.acc = fw.acc;
+  gp.status = &fw.hdr->status;
+  for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
+  gp.zero_acc = 1;
+  // upper bound on items: every key splits into ceil(c / nt) items
+  const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)E * P);
+  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, nt, s, out, /*add=*/0);
+}
+
+int moeb200_check_workspace(void* ws, int32_t* status, void* stream) {
+  if (!ws || !status) return fail(MOEB200_ERR_INVALID, "check_workspace: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  WsHeader* hdr = static_cast<WsHeader*>(ws);
+  CUDA_TRY(cudaMemcpyAsync(status, &hdr->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  CUDA_TRY(cudaMemsetAsync(&hdr->status, 0, sizeof(int32_t), s));
+  return MOEB200_OK;
+}
+
+}  // extern "C"

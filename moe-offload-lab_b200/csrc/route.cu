@@ -1,0 +1,481 @@
+// Router, precision levels and dispatch for the MoE layer on B200.
+//
+//  router_logits : logits[t, e] = round_to_model_dtype(sum_c h[t, c] * Wr[e, c]) (fp32 FMA chain per
+//                  lane, fixed xor-tree across the warp), one warp per expert, tokens streamed.
+//  router_topk   : one warp per token: + bias, fp32 softmax over all E, top-k by repeated warp
+//                  arg-max (ties -> lower expert index), optional renormalisation, and the
+//                  HOBBIT / threshold level of every pair (moelab/policy.py:77-137).
+//  dispatch      : stable counting sort of the kept pairs by expert and by (expert, precision
+//                  slot): per-block warp-aggregated histograms and in-order ranks (__match_any_sync),
+//                  one scan over (key, block), then a scatter. Reproduces the reference's stable
+//                  argsort + unique_consecutive (moelab/runtime.py:471-482) bit for bit, and emits the
+//                  grouped-GEMV work items (<= 8*NB pairs of one (expert, slot) each).
+#include "route.cuh"
+
+namespace moeb200 {
+
+namespace {
+
+template <typename AT>
+__device__ __forceinline__ float round_act(float v) {
+  return to_f32<AT>(from_f32<AT>(v));
+}
+
+// ---- router logits --------------------------------------------------------------------------------
+template <typename AT>
+__global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict__ h, const AT* __restrict__ wr,
+                                                            int T, int H, int E, int tok_per_block,
+                                                            float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  if (e >= E) return;
+  const int t0 = blockIdx.y * tok_per_block;
+  const int t1 = min(T, t0 + tok_per_block);
+  const AT* wrow = wr + (int64_t)e * H;
+  for (int t = t0; t < t1; ++t) {
+    const AT* xrow = h + (int64_t)t * H;
+    float acc = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      uint4 wv = *reinterpret_cast<const uint4*>(wrow + c);
+      uint4 xv = *reinterpret_cast<const uint4*>(xrow + c);
+      const AT* wa = reinterpret_cast<const AT*>(&wv);
+      const AT* xa = reinterpret_cast<const AT*>(&xv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<AT>(xa[i]), to_f32<AT>(wa[i]), acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) logits[(int64_t)t * E + e] = round_act<AT>(acc);
+  }
+}
+
+// fp32 activations: 4 values per 16-byte load
+__global__ void __launch_bounds__(256) router_logits_f32_kernel(const float* __restrict__ h,
+                                                                const float* __restrict__ wr, int T, int H, int E,
+                                                                int tok_per_block, float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  if (e >= E) return;
+  const int t0 = blockIdx.y * tok_per_block;
+  const int t1 = min(T, t0 + tok_per_block);
+  const float* wrow = wr + (int64_t)e * H;
+  for (int t = t0; t < t1; ++t) {
+    const float* xrow = h + (int64_t)t * H;
+    float acc = 0.f;
+    for (int c = lane * 4; c < H; c += 128) {
+      float4 wv = *reinterpret_cast<const float4*>(wrow + c);
+      float4 xv = *reinterpret_cast<const float4*>(xrow + c);
+      acc = fmaf(xv.x, wv.x, acc);
+      acc = fmaf(xv.y, wv.y, acc);
+      acc = fmaf(xv.z, wv.z, acc);
+      acc = fmaf(xv.w, wv.w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) logits[(int64_t)t * E + e] = acc;
+  }
+}
+
+// ---- precision levels of one token (one thread, k <= 32) ------------------------------------------
+// Same operation order as the oracle restatement of PrecisionPolicy.unimportance/levels: the k
+// weights are summed in index order, divided, ranked by descending weight (stable), and s is the
+// running sum in rank order; the comparisons carry the reference's +1e-6 slack.
+__device__ void token_levels(const float* w, int k, const PolicyDev& pol, uint8_t* level, uint8_t* skip) {
+  if (pol.mode == 0 || pol.mode == 1) {
+    for (int j = 0; j < k; ++j) {
+      level[j] = pol.mode == 0 ? 0 : 2;
+      if (skip) skip[j] = 0;
+    }
+    return;
+  }
+  if (pol.mode == 3) {
+    for (int j = 0; j < k; ++j) {
+      level[j] = w[j] >= pol.thr ? 0 : 2;
+      if (skip) skip[j] = 0;
+    }
+    return;
+  }
+  float wn[32];
+  float tot = 0.f;
+  for (int j = 0; j < k; ++j) tot = __fadd_rn(tot, w[j]);
+  tot = fmaxf(tot, 1e-12f);
+  for (int j = 0; j < k; ++j) wn[j] = __fdiv_rn(w[j], tot);
+  uint32_t used = 0;
+  float acc = 0.f;
+  const float t1 = pol.t1 + 1e-6f;
+  const float tm = pol.t_mid + 1e-6f;
+  const float t2 = pol.t2 + 1e-6f;
+  for (int r = 0; r < k; ++r) {
+    int best = -1;
+    for (int j = 0; j < k; ++j)
+      if (!(used >> j & 1u) && (best < 0 || wn[j] > wn[best])) best = j;
+    used |= 1u << best;
+    const float s = acc;
+    acc = __fadd_rn(acc, wn[best]);
+    uint8_t lv = 2;
+    if (pol.t_mid >= 0.f && s <= tm) lv = 1;
+    if (s <= t1) lv = 0;
+    level[best] = lv;
+    if (skip) skip[best] = (pol.t2 >= 0.f && s > t2 && lv != 0) ? 1 : 0;
+  }
+}
+
+__global__ void levels_kernel(const float* __restrict__ w, int T, int k, PolicyDev pol, uint8_t* __restrict__ level,
+                              uint8_t* __restrict__ skip) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  token_levels(w + (int64_t)t * k, k, pol, level + (int64_t)t * k, skip ? skip + (int64_t)t * k : nullptr);
+}
+
+// ---- softmax + top-k: one warp per token ------------------------------------------------------------
+constexpr int kMaxEPerLane = 32;  // E <= 1024
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
+                                                          const float* __restrict__ bias, int T, int E, int k,
+                                                          int renorm, float* __restrict__ probs,
+                                                          float* __restrict__ w, int64_t* __restrict__ idx,
+                                                          PolicyDev pol, int with_levels,
+                                                          uint8_t* __restrict__ level, uint8_t* __restrict__ skip) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const int per = (E + 31) / 32;
+  float v[kMaxEPerLane];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxEPerLane; ++i) {
+    if (i >= per) break;
+    const int e = lane + 32 * i;
+    float l = -INFINITY;
+    if (e < E) {
+      l = logits[(int64_t)t * E + e];
+      if (bias) l = __fadd_rn(l, bias[e]);
+    }
+    v[i] = l;
+    m = fmaxf(m, l);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float ex[kMaxEPerLane];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxEPerLane; ++i) {
+    if (i >= per) break;
+    const int e = lane + 32 * i;
+    ex[i] = e < E ? expf(v[i] - m) : 0.f;
+    s += ex[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  // top-k on the logits (softmax is strictly increasing in the logit): arg-max rounds with the
+  // lower index winning ties.
+  uint32_t taken = 0;
+  float wsel = 0.f;  // lane j < k holds the j-th selected probability
+  int isel = 0;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxEPerLane; ++i) {
+      if (i >= per) break;
+      const int e = lane + 32 * i;
+      if (e < E && !(taken >> i & 1u) && (v[i] > bv || (v[i] == bv && e < bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const int owner = bi & 31;
+    // fetch the owner's exp value for expert bi
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxEPerLane; ++i) {
+      if (i >= per) break;
+      if (lane + 32 * i == bi) mine = ex[i];
+    }
+    const float ebi = __shfl_sync(0xffffffffu, mine, owner);
+    if (lane == r) {
+      wsel = __fdiv_rn(ebi, s);
+      isel = bi;
+    }
+  }
+  if (probs) {
+#pragma unroll
+    for (int i = 0; i < kMaxEPerLane; ++i) {
+      if (i >= per) break;
+      const int e = lane + 32 * i;
+      if (e < E) probs[(int64_t)t * E + e] = __fdiv_rn(ex[i], s);
+    }
+  }
+  if (renorm) {
+    float tot = 0.f;
+    for (int j = 0; j < k; ++j) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, wsel, j));
+    wsel = __fdiv_rn(wsel, tot);
+  }
+  if (lane < k) {
+    w[(int64_t)t * k + lane] = wsel;
+    idx[(int64_t)t * k + lane] = isel;
+  }
+  if (with_levels) {
+    __syncwarp();
+    if (lane == 0) {
+      float wl[32];
+      for (int j = 0; j < k; ++j) wl[j] = w[(int64_t)t * k + j];
+      token_levels(wl, k, pol, level + (int64_t)t * k, skip ? skip + (int64_t)t * k : nullptr);
+    }
+  }
+}
+
+// ---- dispatch ----------------------------------------------------------------------------------------
+__device__ __forceinline__ int slot_of(int level, int P) {
+  if (P >= 3) return min(level, P - 1);
+  return level == 0 ? 0 : P - 1;
+}
+
+// D1: one warp per block of kDispBlock pairs, processed in order 32 at a time. Each pair gets its
+// rank among the earlier pairs of the block with the same key (expert, and expert*P + slot).
+__global__ void __launch_bounds__(32) dispatch_count_kernel(DispatchParams p) {
+  extern __shared__ int32_t sh[];
+  int32_t* cnt_k = sh;               // [E*P]
+  int32_t* cnt_e = sh + p.E * p.P;   // [E]
+  const int lane = threadIdx.x;
+  const int keys = p.E * p.P;
+  for (int i = lane; i < keys + p.E; i += 32) sh[i] = 0;
+  __syncwarp();
+  const int n = p.T * p.k;
+  const int b = blockIdx.x;
+  const int base = b * kDispBlock;
+  const int end = min(n, base + kDispBlock);
+  for (int c = base; c < end; c += 32) {
+    const int i = c + lane;
+    int key = -1, e = -1;
+    if (i < end) {
+      const bool skipped = p.skip && p.skip[i];
+      const int64_t ev = p.idx[i];
+      if (ev < 0 || ev >= p.E) {
+        if (p.status) atomicExch(p.status, kDevBadIndex);
+      } else if (!skipped) {
+        e = (int)ev;
+        const int lv = p.level ? p.level[i] : 0;
+        key = e * p.P + slot_of(lv, p.P);
+      }
+    }
+    const uint32_t lt = (1u << lane) - 1u;
+    const uint32_t mk = __match_any_sync(0xffffffffu, key);
+    const uint32_t me = __match_any_sync(0xffffffffu, e);
+    int rk = 0, re = 0;
+    if (key >= 0) {
+      rk = cnt_k[key] + __popc(mk & lt);
+      re = cnt_e[e] + __popc(me & lt);
+    }
+    __syncwarp();
+    // the highest lane of each group publishes the new count
+    if (key >= 0 && (mk >> lane) == 1u) cnt_k[key] = rk + 1;
+    if (e >= 0 && (me >> lane) == 1u) cnt_e[e] = re + 1;
+    __syncwarp();
+    if (i < end) {
+      p.rank_k[i] = key >= 0 ? rk : -1;
+      p.rank_e[i] = re;
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < keys; i += 32) p.blk_k[(int64_t)b * keys + i] = cnt_k[i];
+  for (int i = lane; i < p.E; i += 32) p.blk_e[(int64_t)b * p.E + i] = cnt_e[i];
+}
+
+// Block-wide exclusive scan of up to 1024 * kScanPer values (one block of 1024 threads).
+template <int PER>
+__device__ int32_t block_exclusive_scan(int32_t (&v)[PER], int32_t* sh_warp) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int32_t loc = 0;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int32_t x = v[i];
+    v[i] = loc;
+    loc += x;
+  }
+  int32_t inc = loc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sh_warp[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t s = lane < (int)(blockDim.x >> 5) ? sh_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    sh_warp[lane] = s;
+  }
+  __syncthreads();
+  const int32_t before = (warp > 0 ? sh_warp[warp - 1] : 0) + inc - loc;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) v[i] += before;
+  const int32_t total = sh_warp[31];
+  __syncthreads();
+  return total;
+}
+
+// D2: one block of 1024 threads. Turns per-block counts into per-(block, key) bases, writes the
+// per-key counts, and builds the work items.
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
+  __shared__ int32_t sh_warp[32];
+  const int keys = p.E * p.P;
+  const int tid = threadIdx.x;
+  if (tid == 0 && p.miss) *p.miss = 0;
+  __syncthreads();
+  constexpr int PER = kMaxKeys / 1024;
+  // per key: running prefix over blocks; totals
+  int32_t tot_k[PER], tot_e[PER], nit[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int key = tid * PER + i;
+    int32_t run = 0;
+    if (key < keys)
+      for (int b = 0; b < p.nblk; ++b) {
+        const int32_t c = p.blk_k[(int64_t)b * keys + key];
+        p.blk_k[(int64_t)b * keys + key] = run;
+        run += c;
+      }
+    tot_k[i] = key < keys ? run : 0;
+    int32_t rune = 0;
+    const int e = tid * PER + i;
+    if (e < p.E)
+      for (int b = 0; b < p.nblk; ++b) {
+        const int32_t c = p.blk_e[(int64_t)b * p.E + e];
+        p.blk_e[(int64_t)b * p.E + e] = rune;
+        rune += c;
+      }
+    tot_e[i] = e < p.E ? rune : 0;
+    // work items: only for keys whose expert record is resident
+    int32_t ni = 0;
+    if (p.items != nullptr && key < keys && run > 0) {
+      const int ex = key / p.P, sl = key % p.P;
+      const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 1;
+      if (rec != 0) ni = (run + p.nt - 1) / p.nt;
+      else if (p.miss) atomicAdd(p.miss, run);
+    }
+    nit[i] = ni;
+  }
+  int32_t off_k[PER], off_e[PER], off_i[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    off_k[i] = tot_k[i];
+    off_e[i] = tot_e[i];
+    off_i[i] = nit[i];
+  }
+  const int32_t n_kept = block_exclusive_scan<PER>(off_k, sh_warp);
+  block_exclusive_scan<PER>(off_e, sh_warp);
+  const int32_t n_items = block_exclusive_scan<PER>(off_i, sh_warp);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int key = tid * PER + i;
+    if (key < keys) {
+      p.counts_k[key] = tot_k[i];
+      p.offs_k[key] = off_k[i];
+      for (int b = 0; b < p.nblk; ++b) p.blk_k[(int64_t)b * keys + key] += off_k[i];
+      if (nit[i] > 0) {
+        const int ex = key / p.P, sl = key % p.P;
+        const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
+        const LayoutOffs lo = p.offs[sl];
+        for (int m = 0; m < nit[i]; ++m) {
+          Item it;
+          it.p_guq = rec + lo.gu_q;
+          it.p_gus = rec + lo.gu_s;
+          it.p_dnq = rec + lo.dn_q;
+          it.p_dns = rec + lo.dn_s;
+          it.slot = sl;
+          it.start = off_k[i] + m * p.nt;
+          it.ntok = min(p.nt, tot_k[i] - m * p.nt);
+          it._pad = ex;
+          p.items[off_i[i] + m] = it;
+        }
+      }
+    }
+    const int e = tid * PER + i;
+    if (e < p.E) {
+      p.counts_e[e] = tot_e[i];
+      for (int b = 0; b < p.nblk; ++b) p.blk_e[(int64_t)b * p.E + e] += off_e[i];
+    }
+  }
+  if (tid == 0) {
+    if (p.n_items) *p.n_items = n_items;
+    if (p.n_kept) *p.n_kept = n_kept;
+  }
+}
+
+// D3: scatter each kept pair to its sorted positions.
+__global__ void dispatch_scatter_kernel(DispatchParams p) {
+  const int n = p.T * p.k;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int rk = p.rank_k[i];
+  if (rk < 0) return;
+  const int b = i / kDispBlock;
+  const int e = (int)p.idx[i];
+  const int lv = p.level ? p.level[i] : 0;
+  const int key = e * p.P + slot_of(lv, p.P);
+  p.pos_k[p.blk_k[(int64_t)b * p.E * p.P + key] + rk] = i;
+  p.pos_e[p.blk_e[(int64_t)b * p.E + e] + p.rank_e[i]] = i;
+}
+
+}  // namespace
+
+cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,
+                          int renorm, float* logits, float* probs, float* w, int64_t* idx, const PolicyDev* pol,
+                          uint8_t* level, uint8_t* skip, cudaStream_t s) {
+  const int tpb = T <= 8 ? T : 8;
+  dim3 grid((E + 7) / 8, (T + tpb - 1) / tpb);
+  if (act_type == MOEB200_F16)
+    router_logits_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(h), static_cast<const __half*>(wr),
+                                                      T, H, E, tpb, logits);
+  else if (act_type == MOEB200_BF16)
+    router_logits_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h),
+                                                             static_cast<const __nv_bfloat16*>(wr), T, H, E, tpb,
+                                                             logits);
+  else
+    router_logits_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(h), static_cast<const float*>(wr), T, H,
+                                                  E, tpb, logits);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  PolicyDev pd{};
+  if (pol) pd = *pol;
+  router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, bias, T, E, k, renorm, probs, w, idx, pd, pol != nullptr,
+                                                 level, skip);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, uint8_t* level, uint8_t* skip,
+                          cudaStream_t s) {
+  levels_kernel<<<(T + 127) / 128, 128, 0, s>>>(w, T, k, pol, level, skip);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
+  const int keys = p.E * p.P;
+  const size_t sh = (size_t)(keys + p.E) * sizeof(int32_t);
+  dispatch_count_kernel<<<p.nblk, 32, sh, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dispatch_scan_kernel<<<1, 1024, 0, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int n = p.T * p.k;
+  dispatch_scatter_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace moeb200

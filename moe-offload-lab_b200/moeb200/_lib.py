@@ -1,0 +1,94 @@
+"""ctypes binding of libmoeb200.so (the C ABI declared in include/moeb200.h).
+
+The library is built in-tree (moeb200/build.py) and loaded from next to this file. There is no
+fallback: if the library is missing or a call fails, an exception is raised.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libmoeb200.so"
+
+F32, F16, BF16, I8, I4 = 0, 1, 2, 3, 4
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3, 4
+
+
+class MoeB200Error(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"moeb200 error {code}: {msg}")
+        self.code = code
+
+
+class Layout(C.Structure):
+    _fields_ = [("wtype", C.c_int32), ("hidden", C.c_int32), ("inter", C.c_int32), ("gs_up", C.c_int32),
+                ("gs_dn", C.c_int32), ("_pad", C.c_int32), ("off_gu_q", C.c_int64), ("off_gu_s", C.c_int64),
+                ("off_dn_q", C.c_int64), ("off_dn_s", C.c_int64), ("record_bytes", C.c_int64)]
+
+
+class Policy(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("t1", C.c_float), ("t_mid", C.c_float), ("t2", C.c_float),
+                ("thr", C.c_float)]
+
+
+class ExpertTable(C.Structure):
+    _fields_ = [("n_prec", C.c_int32), ("num_experts", C.c_int32), ("layout", Layout * 4),
+                ("table", C.c_void_p)]
+
+
+_P = C.c_void_p
+_SIGS = {
+    "moeb200_version": (C.c_char_p, []),
+    "moeb200_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
+    "moeb200_num_sms": (C.c_int, []),
+    "moeb200_trace_events": (C.c_int, [_P, _P, _P]),
+    "moeb200_router": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                 _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
+    "moeb200_router_workspace": (C.c_size_t, [C.c_int32, C.c_int32]),
+    "moeb200_levels": (C.c_int, [_P, C.c_int32, C.c_int32, C.POINTER(Policy), _P, _P, _P]),
+    "moeb200_dispatch": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, _P,
+                                   _P, C.c_size_t, _P]),
+    "moeb200_dispatch_workspace": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "moeb200_grouped_ffn": (C.c_int, [C.POINTER(Layout), _P, _P, C.c_int32, _P, C.c_int32, _P, _P, C.c_size_t,
+                                      _P]),
+    "moeb200_grouped_ffn_workspace": (C.c_size_t, [C.POINTER(Layout), C.c_int32]),
+    "moeb200_experts_forward": (C.c_int, [C.POINTER(ExpertTable), _P, C.c_int32, C.c_int32, _P, _P, C.c_int32,
+                                          _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "moeb200_experts_workspace": (C.c_size_t, [C.POINTER(ExpertTable), C.c_int32, C.c_int32]),
+    "moeb200_check_workspace": (C.c_int, [_P, C.POINTER(C.c_int32), _P]),
+}
+
+_lib: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise MoeB200Error(ERR_INVALID, f"{LIB_PATH} is missing: build it with moeb200/build.py "
+                                            "(there is no fallback implementation)")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> tuple[int, str]:
+    buf = C.create_string_buffer(1024)
+    code = lib().moeb200_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        code, msg = last_error()
+        raise MoeB200Error(rc, msg)
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)

@@ -1,0 +1,187 @@
+"""torch-tensor wrappers of the C ABI: device pointers, the current stream and cached workspaces.
+
+Every function here launches CUDA kernels of libmoeb200 on ``torch.cuda.current_stream()`` and
+returns without synchronising. Inputs must already be CUDA tensors; nothing is computed on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .format import ACT_TYPE
+
+_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(nbytes: int, device: torch.device, slot: int = 0) -> torch.Tensor:
+    """A cached uint8 device buffer of at least nbytes (one per device and slot).
+
+    Slots let callers that run concurrently (or that are captured in different graphs) keep
+    separate scratch. The buffer only grows; growing outside graph capture keeps captures valid.
+    """
+    dev = torch.device(device)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), slot)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def _stream(device=None) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("moeb200 kernels take CUDA tensors only (there is no CPU path)")
+
+
+def _act(dtype: torch.dtype) -> int:
+    if dtype not in ACT_TYPE:
+        raise ValueError(f"unsupported activation dtype {dtype}")
+    return ACT_TYPE[dtype]
+
+
+@dataclass
+class PolicySpec:
+    """Precision rule of the experts module (moelab/policy.py:20-58 PrecisionPolicy, plus the
+    threshold rule of the build's configs). mode: "hi", "lo", "hobbit" or "threshold"."""
+
+    mode: str = "hobbit"
+    t1: float = 0.6
+    t_mid: float | None = None
+    t2: float | None = None
+    thr: float = 0.1
+    protect_layers: frozenset = frozenset()
+
+    def to_c(self, layer: int | None = None) -> _lib.Policy:
+        mode = self.mode
+        if layer is not None and layer in self.protect_layers:
+            mode = "hi"
+        p = _lib.Policy()
+        p.mode = {"hi": 0, "lo": 1, "hobbit": 2, "threshold": 3}[mode]
+        p.t1 = self.t1
+        p.t_mid = -1.0 if self.t_mid is None else self.t_mid
+        p.t2 = -1.0 if self.t2 is None else self.t2
+        p.thr = self.thr
+        return p
+
+
+def router(h: torch.Tensor, wr: torch.Tensor, k: int, renorm: bool, bias: torch.Tensor | None = None,
+           policy: _lib.Policy | None = None, want_probs: bool = True, out: dict | None = None):
+    """Fused router: (probs [T,E] f32 | None, w [T,k] f32, idx [T,k] i64, level [T,k] u8 | None,
+    skip [T,k] u8 | None)."""
+    _need_cuda(h, wr, bias)
+    T, H = h.shape
+    E = wr.shape[0]
+    dev = h.device
+    o = out or {}
+    probs = o.get("probs") if want_probs else None
+    if want_probs and probs is None:
+        probs = torch.empty(T, E, dtype=torch.float32, device=dev)
+    w = o.get("w")
+    if w is None:
+        w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    idx = o.get("idx")
+    if idx is None:
+        idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    level = skip = None
+    if policy is not None:
+        level = o.get("level")
+        if level is None:
+            level = torch.empty(T, k, dtype=torch.uint8, device=dev)
+        skip = o.get("skip")
+        if skip is None:
+            skip = torch.empty(T, k, dtype=torch.uint8, device=dev)
+    L = _lib.lib()
+    nbytes = L.moeb200_router_workspace(T, E)
+    ws = workspace(nbytes, dev, slot=1)
+    _lib.check(L.moeb200_router(_ptr(h), _ptr(wr), _ptr(bias), _act(h.dtype), T, H, E, k, int(bool(renorm)),
+                                _ptr(probs), _ptr(w), _ptr(idx), C.byref(policy) if policy is not None else None,
+                                _ptr(level), _ptr(skip), _ptr(ws), ws.numel(), _stream(dev)))
+    return probs, w, idx, level, skip
+
+
+def levels(w: torch.Tensor, policy: _lib.Policy, level: torch.Tensor | None = None,
+           skip: torch.Tensor | None = None):
+    _need_cuda(w)
+    T, k = w.shape
+    if level is None:
+        level = torch.empty(T, k, dtype=torch.uint8, device=w.device)
+    if skip is None:
+        skip = torch.empty(T, k, dtype=torch.uint8, device=w.device)
+    _lib.check(_lib.lib().moeb200_levels(_ptr(w), T, k, C.byref(policy), _ptr(level), _ptr(skip),
+                                         _stream(w.device)))
+    return level, skip
+
+
+def dispatch(idx: torch.Tensor, level: torch.Tensor | None, skip: torch.Tensor | None, E: int, P: int):
+    """Stable dispatch: dict(counts_e [E], pos_e [T*k], counts_k [E*P], pos_k [T*k], n_kept [1])."""
+    _need_cuda(idx, level, skip)
+    T, k = idx.shape
+    dev = idx.device
+    n = T * k
+    counts_e = torch.empty(E, dtype=torch.int32, device=dev)
+    counts_k = torch.empty(E * P, dtype=torch.int32, device=dev)
+    pos_e = torch.full((n,), -1, dtype=torch.int32, device=dev)
+    pos_k = torch.full((n,), -1, dtype=torch.int32, device=dev)
+    n_kept = torch.empty(1, dtype=torch.int32, device=dev)
+    L = _lib.lib()
+    ws = workspace(L.moeb200_dispatch_workspace(T, k, E, P), dev, slot=2)
+    _lib.check(L.moeb200_dispatch(_ptr(idx.contiguous()), _ptr(level), _ptr(skip), T, k, E, P, _ptr(counts_e),
+                                  _ptr(pos_e), _ptr(counts_k), _ptr(pos_k), _ptr(n_kept), _ptr(ws), ws.numel(),
+                                  _stream(dev)))
+    return {"counts_e": counts_e, "pos_e": pos_e, "counts_k": counts_k, "pos_k": pos_k, "n_kept": n_kept}
+
+
+def grouped_ffn_table(layout_c: _lib.Layout, tab: torch.Tensor, w: torch.Tensor, x_row: torch.Tensor,
+                      out: torch.Tensor, ws: torch.Tensor | None = None) -> None:
+    """out[H] += sum_e w[e] * expert_e(x) with a device pointer table tab [n, 4] (int64)."""
+    _need_cuda(tab, w, x_row, out)
+    n = tab.shape[0]
+    L = _lib.lib()
+    nbytes = L.moeb200_grouped_ffn_workspace(C.byref(layout_c), n)
+    if ws is None:
+        ws = workspace(nbytes, x_row.device, slot=3)
+    elif ws.numel() < nbytes:
+        raise ValueError("workspace too small")
+    _lib.check(L.moeb200_grouped_ffn(C.byref(layout_c), _ptr(tab), _ptr(w), n, _ptr(x_row), _act(x_row.dtype),
+                                     _ptr(out), _ptr(ws), ws.numel(), _stream(x_row.device)))
+
+
+def experts_forward(table: _lib.ExpertTable, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+                    level: torch.Tensor | None, skip: torch.Tensor | None, out: torch.Tensor | None = None,
+                    miss: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """out[T,H] = sum over kept pairs of w * expert(x) at each pair's precision slot."""
+    _need_cuda(x, idx, w, level, skip)
+    T = x.shape[0]
+    k = idx.shape[1]
+    if out is None:
+        out = torch.empty_like(x)
+    L = _lib.lib()
+    nbytes = L.moeb200_experts_workspace(C.byref(table), T, k)
+    if ws is None:
+        ws = workspace(nbytes, x.device, slot=0)
+    elif ws.numel() < nbytes:
+        raise ValueError("workspace too small")
+    _lib.check(L.moeb200_experts_forward(C.byref(table), _ptr(x), _act(x.dtype), T, _ptr(idx), _ptr(w), k,
+                                         _ptr(level), _ptr(skip), _ptr(out), _ptr(miss), _ptr(ws), ws.numel(),
+                                         _stream(x.device)))
+    return out
+
+
+def check_workspace(ws: torch.Tensor) -> int:
+    """Device status word of a workspace (0 = OK); synchronises the current stream."""
+    st = C.c_int32(0)
+    _lib.check(_lib.lib().moeb200_check_workspace(_ptr(ws), C.byref(st), _stream(ws.device)))
+    return st.value

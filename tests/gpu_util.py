@@ -1,0 +1,42 @@
+"""Helpers shared by the GPU parity tests: seeded records on the device, oracle views of them."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from moeb200 import format as F
+from oracle import moe_oracle as O
+
+TOL = 1e-2  # max |got - ref| / max |ref| for layer outputs (fp32 accumulation), per the spec
+
+
+def act_np(x: torch.Tensor) -> np.ndarray:
+    """Activations as the float32 values the kernels see."""
+    return x.float().cpu().numpy()
+
+
+def make_records(prec: str, H: int, I: int, n: int, seed: int, device, std: float = 0.02, scale: str | None = None):
+    """n records of one precision built on the device from N(0, std) weights.
+    Returns (layout, [uint8 CUDA tensors], [uint8 numpy copies])."""
+    lay = F.record_layout(prec, H, I, scale=scale)
+    g = torch.Generator(device=device).manual_seed(seed)
+    blobs = []
+    for _ in range(n):
+        gu = torch.randn(2 * I, H, generator=g, device=device) * std
+        dn = torch.randn(H, I, generator=g, device=device) * std
+        blobs.append(F.encode_record(lay, gu, dn))
+    return lay, blobs, [b.cpu().numpy() for b in blobs]
+
+
+def layer_records(precs, H, I, E, seed, device, std=0.02):
+    """Per precision, E records of the SAME float experts (like a store with several precisions)."""
+    lays = {p: F.record_layout(p, H, I) for p in precs}
+    g = torch.Generator(device=device).manual_seed(seed)
+    recs = {p: [] for p in precs}
+    for _ in range(E):
+        gu = torch.randn(2 * I, H, generator=g, device=device) * std
+        dn = torch.randn(H, I, generator=g, device=device) * std
+        for p in precs:
+            recs[p].append(F.encode_record(lays[p], gu, dn))
+    return lays, recs
