@@ -51,6 +51,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--sweep", default="1,8,32", help="extra batch sizes reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
     return ap.parse_args()
 
 
@@ -283,43 +287,22 @@ def time_graph(step, K: int, W: int, world: int):
     return g, ms
 
 
-def phase_times(stack: Stack, T: int, reps: int = 5):
-    """Average duration of the gate/up and down GEMV launches over the step, from CUDA events
-    recorded by libmoeb200 around its phases on the launching stream."""
+def phase_times(step, reps: int = 5):
+    """Average duration (ms) of the gate/up and down expert kernels over the step, from CUDA events
+    that libmoeb200 records on the launching stream around its phases (eager replay of the step)."""
     import ctypes as C
 
     from moeb200 import _lib
 
-    L = stack.cfg["layers"]
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L * reps)]
     lib = _lib.lib()
-    step = stack.make_device_step(T)
     step()
     torch.cuda.synchronize()
-    n = 0
-    from moeb200 import ops
-
-    cfg = stack.cfg
-    pols = [stack.policy.to_c(li) for li in range(L)]
-    for r in range(reps):
-        for li in range(L):
-            bb = stack.bufs[li]
-            x = stack.xs[li]
-            ops.router(x, stack.wr[li], cfg["k"], cfg["renorm"], None, pols[li], want_probs=False, out=bb)
-            e = evs[n]
-            for ev in e:
-                ev.record()  # materialise the events on this stream before handing them over
-            _lib.check(lib.moeb200_trace_events(C.c_void_p(e[0].cuda_event), C.c_void_p(e[1].cuda_event),
-                                                C.c_void_p(e[2].cuda_event)))
-            ops.experts_forward(stack.rt._ctables[li], x, bb["idx"], bb["w"], bb["level"], bb["skip"],
-                                out=stack.outs[li], miss=stack.rt.miss)
-            _lib.check(lib.moeb200_trace_events(None, None, None))
-            torch.add(x, stack.outs[li], out=stack.xs[li + 1])
-            n += 1
-    torch.cuda.synchronize()
-    up = [e[0].elapsed_time(e[1]) for e in evs]
-    dn = [e[1].elapsed_time(e[2]) for e in evs]
-    return float(np.mean(up)), float(np.mean(dn))
+    _lib.check(lib.moeb200_trace_begin())
+    for _ in range(reps):
+        step()
+    up, dn, n = C.c_float(), C.c_float(), C.c_int32()
+    _lib.check(lib.moeb200_trace_end(C.byref(up), C.byref(dn), C.byref(n)))
+    return up.value / max(n.value, 1), dn.value / max(n.value, 1)
 
 
 # ---- CPU baseline (oracle restatement of the reference's CPU expert path) ---------------------------------------
@@ -405,8 +388,25 @@ def main():
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
     dev = torch.device("cuda", local)
-    stack = Stack(CFG1, dev, seed=0)
+    cfg = dict(CFG1)
+    if args.layers:
+        cfg["layers"] = args.layers
+    from moeb200 import ops as _ops
+
+    _ops.set_path(args.path)
+    stack = Stack(cfg, dev, seed=0)
     T = args.batch
+    if args.ncu:
+        step = stack.make_device_step(T)
+        stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({"ncu_step_done": True, "layers": cfg["layers"], "T": T}))
+        return
     H = CFG1["H"]
     torch.manual_seed(1234 + rank)
     x0 = torch.randn(T, H, device=dev).to(stack.act)
@@ -426,11 +426,11 @@ def main():
 
     # roofline of the dominant kernel (gate/up GEMV) from CUDA events on its stream
     try:
-        up_ms, dn_ms = phase_times(stack, T)
+        up_ms, dn_ms = phase_times(step)
     except Exception as exc:  # the measurement hook failed: report no roofline rather than guess
         print(f"phase timing unavailable: {exc}", file=sys.stderr)
         up_ms = dn_ms = float("nan")
-    L = CFG1["layers"]
+    L = cfg["layers"]
     up_bytes_launch = rb["up_total"] / L
     dn_bytes_launch = rb["down_total"] / L
     up_gbs = up_bytes_launch / (up_ms / 1e3) / 1e9

@@ -86,10 +86,18 @@ int moeb200_last_error(char* buf, size_t n);
 /* Number of SMs of the current device (cached per device). */
 int moeb200_num_sms(void);
 
-/* Measurement hook (no reference counterpart): CUDA events (cudaEvent_t) that the grouped-expert
- * entry points of the calling thread record on their stream before the gate/up GEMV, between the
- * two GEMVs and after the down GEMV. NULLs switch it off. */
-int moeb200_trace_events(void* up_begin, void* up_end, void* down_end);
+/* Expert-product path of the following moeb200_experts_forward calls on the calling thread
+ * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 16*E, grouped GEMV
+ * otherwise), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128). */
+int moeb200_set_path(int32_t path);
+
+/* Measurement hooks (no reference counterpart). Between trace_begin and trace_end, every
+ * grouped-expert call of the calling thread records CUDA events (owned by the library) on its
+ * stream before the gate/up phase, between the two phases and after the down phase.
+ * trace_end synchronises on them and returns the summed phase times (ms) and the call count;
+ * it is for benchmarks, not for captured graphs. */
+int moeb200_trace_begin(void);
+int moeb200_trace_end(float* up_ms, float* down_ms, int32_t* calls);
 
 /* ---- router --------------------------------------------------------------------------------
  * Replaces transformers OlmoeTopKRouter / Qwen3MoeTopKRouter / Qwen3NextTopKRouter.forward
@@ -97,11 +105,12 @@ int moeb200_trace_events(void* up_begin, void* up_end, void* down_end);
  *  qwen3_next/modeling_qwen3_next.py:761-779): logits = h . Wr^T accumulated in fp32 and rounded
  * to the model dtype, + bias[e] (fp32, optional synthetic skew), probs = softmax in fp32 over all
  * E, top-k with ties broken by the lower expert index, optional renormalisation of the k weights.
- * h [T,H] and wr [E,H] are act_type (F16/BF16/F32). probs [T,E] may be NULL.
+ * h [T,H] and wr [E,H] are act_type (F16/BF16/F32). probs [T,E] may be NULL. logits [T,E] (may be
+ * NULL) receives the model-dtype-rounded logits before the bias, as float32.
  * If policy != NULL the HOBBIT / threshold levels of each pair are also written to level [T,k]
  * and skip [T,k] (uint8, 1 = skipped). */
 int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H,
-                   int32_t E, int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx,
+                   int32_t E, int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, float* logits,
                    const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
                    void* stream);
 size_t moeb200_router_workspace(int32_t T, int32_t E);

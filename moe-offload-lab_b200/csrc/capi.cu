@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "route.cuh"
 
@@ -22,8 +23,32 @@ namespace {
 
 thread_local std::string g_err;
 thread_local int g_err_code = MOEB200_OK;
-// Optional CUDA events recorded around the GEMV phases of the next expert calls (measurement).
-thread_local cudaEvent_t g_trace[3] = {nullptr, nullptr, nullptr};
+// Phase tracing (measurement): while on, every grouped-expert call records library-owned CUDA
+// events before the gate/up phase, between the phases and after the down phase.
+struct TraceRec {
+  cudaEvent_t ev[3];
+};
+thread_local bool g_tracing = false;
+thread_local std::vector<TraceRec> g_trace_pool;
+thread_local size_t g_trace_used = 0;
+
+cudaError_t trace_mark(int which, cudaStream_t s) {
+  if (!g_tracing) return cudaSuccess;
+  if (which == 0) {
+    if (g_trace_used == g_trace_pool.size()) {
+      TraceRec r{};
+      for (auto& e : r.ev) {
+        cudaError_t err = cudaEventCreate(&e);
+        if (err != cudaSuccess) return err;
+      }
+      g_trace_pool.push_back(r);
+    }
+    ++g_trace_used;
+  }
+  return cudaEventRecord(g_trace_pool[g_trace_used - 1].ev[which], s);
+}
+// Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM.
+thread_local int g_path = 0;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -181,7 +206,21 @@ LayoutDev to_dev(const moeb200_layout& L) {
 }
 
 int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int act, int max_items, int nt,
-                      cudaStream_t s, void* out, int add) {
+                      cudaStream_t s, void* out, int add, bool gemm = false) {
+  if (gemm) {
+    const int sms = num_sms_cached();
+    const int64_t tiles = (int64_t)max_items * (gp.I / 128);
+    const int64_t tiles_dn = (int64_t)max_items * (gp.H / 128);
+    const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>(sms, tiles));
+    const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>(sms, tiles_dn));
+    CUDA_TRY(trace_mark(0, s));
+    CUDA_TRY(launch_gemm_up(gp, act, grid_up, s));
+    CUDA_TRY(trace_mark(1, s));
+    CUDA_TRY(launch_gemm_down(gp, act, grid_dn, s));
+    CUDA_TRY(trace_mark(2, s));
+    CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
+    return MOEB200_OK;
+  }
   gp.scale_slot_bytes = scale_slot_bytes(lays, nlay);
   const int smem = gemv_smem_bytes(gp.scale_slot_bytes);
   if (smem > 227 * 1024) return fail(MOEB200_ERR_UNSUPPORTED, "too many scale groups per row for the GEMV stages");
@@ -193,11 +232,11 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
   const int64_t tiles_dn = (int64_t)max_items * (gp.H / 32);
   const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + kGemvWarps - 1) / kGemvWarps));
   const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + kGemvWarps - 1) / kGemvWarps));
-  if (g_trace[0]) CUDA_TRY(cudaEventRecord(g_trace[0], s));
+  CUDA_TRY(trace_mark(0, s));
   CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, s));
-  if (g_trace[1]) CUDA_TRY(cudaEventRecord(g_trace[1], s));
+  CUDA_TRY(trace_mark(1, s));
   CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, s));
-  if (g_trace[2]) CUDA_TRY(cudaEventRecord(g_trace[2], s));
+  CUDA_TRY(trace_mark(2, s));
   CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
   return MOEB200_OK;
 }
@@ -251,10 +290,34 @@ int moeb200_last_error(char* buf, size_t n) {
 
 int moeb200_num_sms(void) { return num_sms_cached(); }
 
-int moeb200_trace_events(void* up_begin, void* up_end, void* down_end) {
-  g_trace[0] = static_cast<cudaEvent_t>(up_begin);
-  g_trace[1] = static_cast<cudaEvent_t>(up_end);
-  g_trace[2] = static_cast<cudaEvent_t>(down_end);
+int moeb200_set_path(int32_t path) {
+  if (path < 0 || path > 2) return fail(MOEB200_ERR_INVALID, "set_path: path must be 0 (auto), 1 (GEMV) or 2 (GEMM)");
+  g_path = path;
+  return MOEB200_OK;
+}
+
+int moeb200_trace_begin(void) {
+  g_tracing = true;
+  g_trace_used = 0;
+  return MOEB200_OK;
+}
+
+int moeb200_trace_end(float* up_ms, float* down_ms, int32_t* calls) {
+  g_tracing = false;
+  float up = 0.f, dn = 0.f;
+  for (size_t i = 0; i < g_trace_used; ++i) {
+    const TraceRec& r = g_trace_pool[i];
+    CUDA_TRY(cudaEventSynchronize(r.ev[2]));
+    float a = 0.f, b = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&a, r.ev[0], r.ev[1]));
+    CUDA_TRY(cudaEventElapsedTime(&b, r.ev[1], r.ev[2]));
+    up += a;
+    dn += b;
+  }
+  if (up_ms) *up_ms = up;
+  if (down_ms) *down_ms = dn;
+  if (calls) *calls = (int32_t)g_trace_used;
+  g_trace_used = 0;
   return MOEB200_OK;
 }
 
@@ -266,8 +329,9 @@ size_t moeb200_router_workspace(int32_t T, int32_t E) {
 }
 
 int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H, int32_t E,
-                   int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, const moeb200_policy* policy,
-                   uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes, void* stream) {
+                   int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, float* logits_out,
+                   const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
+                   void* stream) {
   if (!h || !wr || !w || !idx) return fail(MOEB200_ERR_INVALID, "router: null pointer");
   if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 1024)
     return fail(MOEB200_ERR_INVALID, "router: bad sizes T=%d H=%d E=%d k=%d (k <= 32, E <= 1024)", T, H, E, k);
@@ -280,6 +344,7 @@ int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act
   WsHeader* hdr = c.take<WsHeader>(1);
   (void)hdr;
   float* logits = c.take<float>((size_t)T * E);
+  if (logits_out) logits = logits_out;
   PolicyDev pd{};
   if (policy) pd = {policy->mode, policy->t1, policy->t_mid, policy->t2, policy->thr};
   CUDA_TRY(launch_router(h, wr, bias, act_type, T, H, E, k, renorm, logits, probs, w, idx, policy ? &pd : nullptr,
@@ -425,7 +490,14 @@ int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32
   fw = carve_forward(ws, T, k, E, P, H, I, act_type);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n = T * k;
-  const int nt = T >= 128 ? 16 : 8;
+  // tcgen05 GEMM when experts see many tokens (prefill), warp GEMV otherwise (decode)
+  const bool gemm_ok = (H % 128 == 0) && (I % 128 == 0);
+  bool gemm = g_path == 2 || (g_path == 0 && (int64_t)n >= 16ll * E);
+  if (gemm && !gemm_ok) {
+    if (g_path == 2) return fail(MOEB200_ERR_UNSUPPORTED, "GEMM path needs H and I multiples of 128 (H=%d, I=%d)", H, I);
+    gemm = false;
+  }
+  const int nt = gemm ? 128 : (T >= 128 ? 16 : 8);
   DispatchParams dp{};
   dp.idx = idx;
   dp.level = level;
@@ -473,7 +545,7 @@ int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32
   gp.zero_acc = 1;
   // upper bound on items: every key splits into ceil(c / nt) items
   const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)E * P);
-  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, nt, s, out, /*add=*/0);
+  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, nt, s, out, /*add=*/0, gemm);
 }
 
 int moeb200_check_workspace(void* ws, int32_t* status, void* stream) {

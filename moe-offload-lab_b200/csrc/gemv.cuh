@@ -59,6 +59,9 @@ __host__ __device__ inline int gemv_warp_smem(int scale_slot_bytes) {
 cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, cudaStream_t s);
 cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, cudaStream_t s);
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s);
+// tcgen05 grouped GEMM (gemm_tc.cu): items of up to 128 pairs, I and H multiples of 128
+cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s);
+cudaError_t launch_gemm_down(const GemvParams& p, int act_type, int grid, cudaStream_t s);
 int gemv_smem_bytes(int scale_slot_bytes);
 
 }  // namespace moeb200

@@ -42,9 +42,11 @@ _SIGS = {
     "moeb200_version": (C.c_char_p, []),
     "moeb200_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
     "moeb200_num_sms": (C.c_int, []),
-    "moeb200_trace_events": (C.c_int, [_P, _P, _P]),
+    "moeb200_trace_begin": (C.c_int, []),
+    "moeb200_trace_end": (C.c_int, [C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "moeb200_router": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
-                                 _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
+                                 _P, _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
+    "moeb200_set_path": (C.c_int, [C.c_int32]),
     "moeb200_router_workspace": (C.c_size_t, [C.c_int32, C.c_int32]),
     "moeb200_levels": (C.c_int, [_P, C.c_int32, C.c_int32, C.POINTER(Policy), _P, _P, _P]),
     "moeb200_dispatch": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, _P,

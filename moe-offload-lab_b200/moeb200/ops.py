@@ -78,7 +78,8 @@ class PolicySpec:
 
 
 def router(h: torch.Tensor, wr: torch.Tensor, k: int, renorm: bool, bias: torch.Tensor | None = None,
-           policy: _lib.Policy | None = None, want_probs: bool = True, out: dict | None = None):
+           policy: _lib.Policy | None = None, want_probs: bool = True, out: dict | None = None,
+           logits: torch.Tensor | None = None):
     """Fused router: (probs [T,E] f32 | None, w [T,k] f32, idx [T,k] i64, level [T,k] u8 | None,
     skip [T,k] u8 | None)."""
     _need_cuda(h, wr, bias)
@@ -107,7 +108,8 @@ def router(h: torch.Tensor, wr: torch.Tensor, k: int, renorm: bool, bias: torch.
     nbytes = L.moeb200_router_workspace(T, E)
     ws = workspace(nbytes, dev, slot=1)
     _lib.check(L.moeb200_router(_ptr(h), _ptr(wr), _ptr(bias), _act(h.dtype), T, H, E, k, int(bool(renorm)),
-                                _ptr(probs), _ptr(w), _ptr(idx), C.byref(policy) if policy is not None else None,
+                                _ptr(probs), _ptr(w), _ptr(idx), _ptr(logits),
+                                C.byref(policy) if policy is not None else None,
                                 _ptr(level), _ptr(skip), _ptr(ws), ws.numel(), _stream(dev)))
     return probs, w, idx, level, skip
 
@@ -178,6 +180,11 @@ def experts_forward(table: _lib.ExpertTable, x: torch.Tensor, idx: torch.Tensor,
                                          _ptr(level), _ptr(skip), _ptr(out), _ptr(miss), _ptr(ws), ws.numel(),
                                          _stream(x.device)))
     return out
+
+
+def set_path(path: str) -> None:
+    """Expert-product path for this thread's next experts_forward calls: "auto", "gemv" or "gemm"."""
+    _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2}[path]))
 
 
 def check_workspace(ws: torch.Tensor) -> int:

@@ -40,3 +40,25 @@ def layer_records(precs, H, I, E, seed, device, std=0.02):
         for p in precs:
             recs[p].append(F.encode_record(lays[p], gu, dn))
     return lays, recs
+
+
+def emulate_router_logits(h: np.ndarray, wr: np.ndarray, dtype: str) -> np.ndarray:
+    """Bit-exact emulation of the router-logit kernel's fp32 arithmetic: lane l of a warp takes the
+    columns l*8 + 256*i + j (i over H/256, j over 8) in that order with fused multiply-adds (the
+    product of two 16-bit values is exact in fp64, and one fp64 add of it to an fp32 partial
+    rounded once to fp32 is the FMA), then an xor butterfly over offsets 16, 8, 4, 2, 1, then one
+    rounding to the model dtype."""
+    from oracle import moe_oracle as O
+
+    T, H = h.shape
+    E = wr.shape[0]
+    hf = h.astype(np.float64).reshape(T, 1, H // 256, 32, 8)
+    wf = wr.astype(np.float64).reshape(1, E, H // 256, 32, 8)
+    acc = np.zeros((T, E, 32), np.float32)
+    for i in range(H // 256):
+        for j in range(8):
+            prod = hf[:, :, i, :, j] * wf[:, :, i, :, j]  # (T, E, 32), exact
+            acc = (acc.astype(np.float64) + prod).astype(np.float32)
+    for o in (16, 8, 4, 2, 1):
+        acc = (acc + acc[:, :, np.arange(32) ^ o]).astype(np.float32)
+    return O.round_to(acc[:, :, 0], dtype)

@@ -99,8 +99,8 @@ def test_invalid_arguments_refused_without_cuda():
     rc = L.moeb200_grouped_ffn(C.byref(lay), fake, fake, 2, fake, _lib.F16, fake, fake, 16, None)
     assert rc == _lib.ERR_WORKSPACE
     # router: k > E
-    rc = L.moeb200_router(fake, fake, None, _lib.F16, 1, 2048, 4, 8, 0, None, fake, fake, None, None, None, fake,
-                          1 << 20, None)
+    rc = L.moeb200_router(fake, fake, None, _lib.F16, 1, 2048, 4, 8, 0, None, fake, fake, None, None, None, None,
+                          fake, 1 << 20, None)
     assert rc == _lib.ERR_INVALID
 
 
