@@ -146,6 +146,20 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
                         const void* x, int32_t act_type, void* out, void* ws, size_t ws_bytes, void* stream);
 size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n);
 
+/* Workspace-free variant of moeb200_grouped_ffn (no counterpart in the reference).
+ * For callers that cannot provide device scratch: a host binding the C ABI directly with no device
+ * allocator of its own, or code that must not call cudaMalloc (it can synchronise the device, or the
+ * GPU memory is already budgeted by another framework's allocator). The scratch is one static device
+ * array of MOEB200_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits; the call allocates
+ * nothing. The first call on a device looks up that array's address with the device current, so make
+ * it before any stream capture. Calls share the array: sequential calls are independent (what must
+ * start at zero is cleared), calls that overlap on the GPU race. A call whose scratch would exceed
+ * the array (moeb200_grouped_ffn_workspace(layout, n) > MOEB200_NOALLOC_SCRATCH_BYTES) returns
+ * MOEB200_ERR_UNSUPPORTED without launching anything. */
+#define MOEB200_NOALLOC_SCRATCH_BYTES (1u << 20)
+int moeb200_grouped_ffn_noalloc(const moeb200_layout* layout, const int64_t* tab, const float* w, int32_t n,
+                                const void* x, int32_t act_type, void* out, void* stream);
+
 /* ---- the experts module ------------------------------------------------------------------------
  * Replaces OffloadedExperts.forward -> MoERuntime.run_layer for experts resident on this GPU
  * (moelab/runtime.py:522-770 with every request a VRAM hit; fullgraph.py:149-188 on device):

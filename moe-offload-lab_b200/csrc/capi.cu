@@ -276,6 +276,20 @@ __global__ void table_items_kernel(const int64_t* __restrict__ tab, const float*
 
 }  // namespace
 
+namespace moeb200 {
+// Records an error message for moeb200_last_error from other translation units of the library.
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  g_err_code = code;
+  return code;
+}
+}  // namespace moeb200
+
 extern "C" {
 
 const char* moeb200_version(void) { return "moeb200 0.1 (sm_100a)"; }

@@ -55,6 +55,7 @@ _SIGS = {
     "moeb200_grouped_ffn": (C.c_int, [C.POINTER(Layout), _P, _P, C.c_int32, _P, C.c_int32, _P, _P, C.c_size_t,
                                       _P]),
     "moeb200_grouped_ffn_workspace": (C.c_size_t, [C.POINTER(Layout), C.c_int32]),
+    "moeb200_grouped_ffn_noalloc": (C.c_int, [C.POINTER(Layout), _P, _P, C.c_int32, _P, C.c_int32, _P, _P]),
     "moeb200_experts_forward": (C.c_int, [C.POINTER(ExpertTable), _P, C.c_int32, C.c_int32, _P, _P, C.c_int32,
                                           _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "moeb200_experts_workspace": (C.c_size_t, [C.POINTER(ExpertTable), C.c_int32, C.c_int32]),
