@@ -39,7 +39,12 @@ import torch  # noqa: E402
 
 METRIC = "MoE-layer tokens/s"
 CFG1 = dict(name="c1", layers=16, H=2048, I=1024, E=64, k=8, renorm=False, precs=["fp16", "int4"],
-            policy=dict(mode="threshold", thr=0.1), act="fp16")
+            policy=dict(mode="threshold", thr=0.1), act="fp16", bias=False, T=64)
+# single-layer configurations reported beside the headline (BASELINE.json configs 0 and 2)
+CFG0 = dict(name="c0", layers=1, H=2048, I=1024, E=64, k=8, renorm=False, precs=["int4"],
+            policy=dict(mode="lo"), act="fp16", bias=False, T=1)
+CFG2 = dict(name="c2", layers=1, H=2048, I=768, E=128, k=8, renorm=True, precs=["int4"],
+            policy=dict(mode="lo"), act="bf16", bias=True, T=2048)
 
 
 def parse():
@@ -52,9 +57,11 @@ def parse():
     ap.add_argument("--sweep", default="1,8,32", help="extra batch sizes reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
+    ap.add_argument("--config", default="c1", choices=["c0", "c1", "c2"], help="workload of --ncu mode")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
+    ap.add_argument("--extra", default="c0,c2", help="single-layer configs measured beside the headline")
     return ap.parse_args()
 
 
@@ -160,6 +167,7 @@ class Stack:
         self.rt = moeb200.B200Runtime(cfg["precs"], self.lays, E, dev, self.policy, layers=range(L))
         g = torch.Generator(device=dev).manual_seed(seed)
         self.wr = []
+        self.bias = (torch.randn(E, generator=g, device=dev) if cfg.get("bias") else None)
         for li in range(L):
             self.wr.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(self.act))
             for e in range(E):
@@ -167,7 +175,7 @@ class Stack:
                 dn = torch.randn(H, I, generator=g, device=dev) * 0.02
                 for p in cfg["precs"]:
                     self.rt.add_record(li, e, p, F.encode_record(self.lays[p], gu, dn))
-        self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"]) for w in self.wr]
+        self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"], self.bias) for w in self.wr]
         self.experts = [moeb200.B200Experts(self.rt, li, torch.nn.SiLU(), E) for li in range(L)]
         self.record_bytes = {p: self.lays[p]["record_bytes"] for p in cfg["precs"]}
 
@@ -190,7 +198,7 @@ class Stack:
             for li in range(L):
                 b = self.bufs[li]
                 x = self.xs[li]
-                ops.router(x, self.wr[li], k, cfg["renorm"], None, pols[li], want_probs=False, out=b)
+                ops.router(x, self.wr[li], k, cfg["renorm"], self.bias, pols[li], want_probs=False, out=b)
                 ops.experts_forward(tables[li], x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li],
                                     miss=miss)
                 torch.add(x, self.outs[li], out=self.xs[li + 1])
@@ -305,6 +313,41 @@ def phase_times(step, reps: int = 5):
     return up.value / max(n.value, 1), dn.value / max(n.value, 1)
 
 
+def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: dict) -> dict:
+    """Tokens/s of one MoE layer of `cfg` (CUDA-graph replay, inputs resident) and the roofline of
+    its expert kernels: HBM bytes for decode, tensor flops for prefill (tcgen05 path)."""
+    stack = Stack(cfg, dev, seed=1)
+    T = cfg["T"]
+    step = stack.make_device_step(T)
+    stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
+    g, ms = time_graph(step, steps, warmup, world)
+    del g
+    ms = max_over_ranks(ms, world)
+    rb = stack.routing_bytes()
+    up_ms, dn_ms = phase_times(step)
+    pairs = rb["pairs"]
+    out = {"workload": cfg["name"], "T": T, "tokens_per_s": T * world / (ms / 1e3), "ms_per_layer": ms,
+           "experts_ms": up_ms + dn_ms, "records": rb["records"], "pairs": pairs}
+    prefill = T * cfg["k"] >= 16 * cfg["E"]
+    if prefill:
+        flops = 6.0 * cfg["H"] * cfg["I"] * pairs
+        tf = flops / ((up_ms + dn_ms) / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops", 1590.0)
+        out["roofline"] = {"bound": "tensor", "kernel": "tcgen05 grouped GEMM (up + down)", "achieved": tf,
+                           "peak": peak, "unit": "TFLOP/s", "frac": tf / peak, "flops_per_layer": flops,
+                           "up_ms": up_ms, "down_ms": dn_ms}
+    else:
+        byts = rb["up_total"] + rb["down_total"]
+        gbs = byts / ((up_ms + dn_ms) / 1e3) / 1e9
+        peak = peaks.get("hbm_gbs", 6650.0)
+        out["roofline"] = {"bound": "hbm", "kernel": "grouped GEMV (up + down)", "achieved": gbs, "peak": peak,
+                           "unit": "GB/s", "frac": gbs / peak, "bytes_per_layer": byts, "up_ms": up_ms,
+                           "down_ms": dn_ms}
+    del stack
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---- CPU baseline (oracle restatement of the reference's CPU expert path) ---------------------------------------
 def cpu_layer_sample(stack: Stack, T: int, layer: int = 0):
     """One layer of the workload on the host cores: returns (seconds, sample description)."""
@@ -388,14 +431,14 @@ def main():
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
     dev = torch.device("cuda", local)
-    cfg = dict(CFG1)
+    cfg = dict({"c0": CFG0, "c1": CFG1, "c2": CFG2}[args.config] if args.ncu else CFG1)
     if args.layers:
         cfg["layers"] = args.layers
     from moeb200 import ops as _ops
 
     _ops.set_path(args.path)
     stack = Stack(cfg, dev, seed=0)
-    T = args.batch
+    T = args.batch if not args.ncu or args.config == "c1" else cfg["T"]
     if args.ncu:
         step = stack.make_device_step(T)
         stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
@@ -478,6 +521,11 @@ def main():
         cpu = {"value": T / (dt * L), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                "sample": sample}
 
+    extra = {}
+    for name in [c for c in args.extra.split(",") if c]:
+        cfgx = {"c0": CFG0, "c2": CFG2}[name]
+        extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -503,6 +551,7 @@ def main():
             "clocks": clk,
             "sweep": sweep,
             "missing_pairs": miss,
+            "extra_configs": extra,
             "records_per_step": rb["records"], "pairs_per_step": rb["pairs"],
         }
         print(json.dumps(line), flush=True)

@@ -13,10 +13,6 @@
 
 #include "route.cuh"
 
-namespace moeb200 {
-int gemv_occupancy(int act_type, int nb, bool up, int smem);
-}
-
 using namespace moeb200;
 
 namespace {
@@ -154,14 +150,19 @@ int check_shapes(int H, int I) {
   return MOEB200_OK;
 }
 
-int scale_slot_bytes(const moeb200_layout* L, int n) {
-  int ng = 1;
-  for (int i = 0; i < n; ++i)
-    if (is_int(L[i].wtype)) {
-      ng = std::max(ng, L[i].hidden / L[i].gs_up);
-      ng = std::max(ng, L[i].inter / L[i].gs_dn);
-    }
-  return 64 * ng;
+// Split-K planning of the GEMV phases: a split covers a multiple of kSplitCols input columns (a
+// multiple of every group size and pipeline step), and is only used for small pair counts (the
+// pre-activation buffer is sized for kMaxSplitPairs pairs).
+constexpr int kMaxSplitPairs = 256;
+
+bool split_ok(const moeb200_layout* L, int nlay, bool up, int ks) {
+  if (ks == 1) return true;
+  for (int i = 0; i < nlay; ++i) {
+    const int K = up ? L[i].hidden : L[i].inter;
+    if (K < ks * kSplitCols / 2) return false;
+    if (is_int(L[i].wtype) && kSplitCols % (up ? L[i].gs_up : L[i].gs_dn)) return false;
+  }
+  return true;
 }
 
 struct ForwardWs {
@@ -169,6 +170,7 @@ struct ForwardWs {
   int32_t *pos_e, *pos_k, *counts_e, *counts_k, *offs_k, *blk_k, *blk_e, *rank_k, *rank_e;
   Item* items;
   uint8_t* h;
+  float* pre;
   float* acc;
   float* logits;
   size_t bytes;
@@ -192,6 +194,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.rank_e = c.take<int32_t>(n);
   w.items = c.take<Item>(n);
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
+  w.pre = c.take<float>((size_t)std::min(n, kMaxSplitPairs) * 2 * I);
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
   return w;
@@ -205,8 +208,8 @@ LayoutDev to_dev(const moeb200_layout& L) {
   return d;
 }
 
-int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int act, int max_items, int nt,
-                      cudaStream_t s, void* out, int add, bool gemm = false) {
+int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int act, int max_items, int n_pairs,
+                      int nt, cudaStream_t s, void* out, int add, bool gemm = false) {
   if (gemm) {
     const int sms = num_sms_cached();
     const int64_t tiles = (int64_t)max_items * (gp.I / 128);
@@ -221,21 +224,36 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
     CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
     return MOEB200_OK;
   }
-  gp.scale_slot_bytes = scale_slot_bytes(lays, nlay);
-  const int smem = gemv_smem_bytes(gp.scale_slot_bytes);
-  if (smem > 227 * 1024) return fail(MOEB200_ERR_UNSUPPORTED, "too many scale groups per row for the GEMV stages");
-  const int nb = nt > 8 ? 2 : 1;
   const int sms = num_sms_cached();
-  const int occ_up = std::max(1, gemv_occupancy(act, nb, true, smem));
-  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, smem));
-  const int64_t tiles_up = (int64_t)max_items * (gp.I / 16);
-  const int64_t tiles_dn = (int64_t)max_items * (gp.H / 32);
-  const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + kGemvWarps - 1) / kGemvWarps));
-  const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + kGemvWarps - 1) / kGemvWarps));
+  const int nb = nt > 8 ? 2 : 1;
+  // split K while the tiles would not give every resident warp two of them
+  const int64_t rb_up = gp.I / 16, rb_dn = gp.H / 32;
+  int ks_up = 1, ks_dn = 1;
+  const int64_t want = 2ll * sms * kGemvMaxWarps;
+  const bool can_split = max_items <= kMaxSplitPairs && n_pairs <= kMaxSplitPairs && gp.pre != nullptr;
+  while (can_split && ks_up < 4 && (int64_t)max_items * rb_up * ks_up < want && split_ok(lays, nlay, true, ks_up * 2))
+    ks_up *= 2;
+  while (ks_dn < 4 && (int64_t)max_items * rb_dn * ks_dn < want && split_ok(lays, nlay, false, ks_dn * 2)) ks_dn *= 2;
+  gp.ksplit_up = ks_up;
+  gp.ksplit_dn = ks_dn;
+  int rstride = 0;
+  for (int i = 0; i < nlay; ++i) rstride = std::max(rstride, gemv_row_stride(lays[i].wtype));
+  gp.stage_bytes = 32 * rstride;
+  int warps = kGemvMaxWarps;
+  while (warps > 1 && gemv_smem_bytes(gp.stage_bytes, warps) > 227 * 1024) --warps;
+  const int smem = gemv_smem_bytes(gp.stage_bytes, warps);
+  const bool split = ks_up > 1;
+  const int occ_up = std::max(1, gemv_occupancy(act, nb, true, split, smem, warps));
+  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, split, smem, warps));
+  const int64_t tiles_up = (int64_t)max_items * rb_up * ks_up;
+  const int64_t tiles_dn = (int64_t)max_items * rb_dn * ks_dn;
+  const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + warps - 1) / warps));
+  const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + warps - 1) / warps));
+  if (split) CUDA_TRY(cudaMemsetAsync(gp.pre, 0, (size_t)n_pairs * 2 * gp.I * sizeof(float), s));
   CUDA_TRY(trace_mark(0, s));
-  CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, s));
+  CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, warps, s));
   CUDA_TRY(trace_mark(1, s));
-  CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, s));
+  CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, warps, s));
   CUDA_TRY(trace_mark(2, s));
   CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
   return MOEB200_OK;
@@ -431,6 +449,7 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<Item>(n);
   c.take<int32_t>(n);
   c.take<uint8_t>((size_t)n * layout->inter * 2);
+  c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * layout->inter);
   c.take<float>((size_t)layout->hidden);
   return c.off;
 }
@@ -454,6 +473,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   Item* items = c.take<Item>(n);
   int32_t* pos = c.take<int32_t>(n);
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
+  float* pre = c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * I);
   float* acc = c.take<float>((size_t)H);
   table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
   CUDA_TRY(cudaGetLastError());
@@ -468,11 +488,12 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.T = 1;
   gp.x = x;
   gp.h = hbuf;
+  gp.pre = pre;
   gp.acc = acc;
   gp.status = &hdr->status;
   gp.lay[0] = to_dev(*layout);
   gp.zero_acc = 1;
-  return run_expert_phases(gp, layout, 1, act_type, n, 8, s, out, /*add=*/1);
+  return run_expert_phases(gp, layout, 1, act_type, n, n, 8, s, out, /*add=*/1);
 }
 
 size_t moeb200_experts_workspace(const moeb200_expert_table* ex, int32_t T, int32_t k) {
@@ -553,13 +574,14 @@ int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32
   gp.T = T;
   gp.x = x;
   gp.h = fw.h;
+  gp.pre = fw.pre;
   gp.acc = fw.acc;
   gp.status = &fw.hdr->status;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
   // upper bound on items: every key splits into ceil(c / nt) items
   const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)E * P);
-  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, nt, s, out, /*add=*/0, gemm);
+  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, out, /*add=*/0, gemm);
 }
 
 int moeb200_check_workspace(void* ws, int32_t* status, void* stream) {

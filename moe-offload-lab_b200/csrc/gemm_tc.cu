@@ -178,6 +178,12 @@ __device__ __forceinline__ void dq_int8_chunk(uint32_t w0, uint32_t w1, uint16_t
 }
 
 // ---- kernel -------------------------------------------------------------------------------------------
+struct TcTile;
+template <typename AT, bool UP, int STAGES, int STAGE_BYTES>
+__device__ __forceinline__ bool dq_int4_tile(const TcTile& d, int nkb, int tile_i, int row, int c0, uint32_t& st,
+                                             uint32_t sbase, uint64_t* empty, uint64_t* full_a, int32_t* status,
+                                             int lane);
+
 struct TcTile {
   int item, r0, ntok, n, start, slot;
   const uint8_t* q[2];  // first weight row of each A tile
@@ -320,6 +326,65 @@ __device__ __forceinline__ void dq_store(const TcTile& d, int kb, int tile, int 
   }
 }
 
+// int4 records whose groups span whole 64-column k-blocks: the thread's raw bytes are loaded two to
+// three k-blocks ahead of their dequantisation, one scale per row per k-block.
+template <typename AT, bool UP, int STAGES, int STAGE_BYTES>
+__device__ __forceinline__ bool dq_int4_tile(const TcTile& d, int nkb, int tile_i, int row, int c0, uint32_t& st,
+                                             uint32_t sbase, uint64_t* empty, uint64_t* full_a, int32_t* status,
+                                             int lane) {
+  constexpr int NV = UP ? 2 : 1;   // 16-byte vectors per k-block (32 or 16 raw bytes)
+  constexpr int NCH = UP ? 8 : 4;  // 8-column chunks per k-block
+  const uint8_t* rowp = d.q[tile_i] + (int64_t)row * d.rstride + c0 * 4;
+  const uint16_t* srow = reinterpret_cast<const uint16_t*>(d.s[tile_i] + (int64_t)row * d.sstride);
+  const int kpg = d.gs / BK;  // k-blocks per scale group
+  constexpr int MB = 2;       // k-blocks per prefetch macro block
+  uint4 raw[MB][NV], nraw[MB][NV];
+  uint16_t sc[MB], nsc[MB];
+#pragma unroll
+  for (int u = 0; u < MB; ++u) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) raw[u][i] = ldg16(rowp + u * 32 + i * 16);
+    sc[u] = __ldg(srow + u / kpg);
+  }
+  for (int kb0 = 0; kb0 < nkb; kb0 += MB) {
+    const bool more = kb0 + MB < nkb;
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < MB; ++u) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) nraw[u][i] = ldg16(rowp + (kb0 + MB + u) * 32 + i * 16);
+        nsc[u] = __ldg(srow + (kb0 + MB + u) / kpg);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < MB; ++u, ++st) {
+      const int s = st % STAGES;
+      if (!mbar_wait(&empty[s], ((st / STAGES) & 1u) ^ 1u, status)) return false;
+      const uint32_t atile = sbase + s * STAGE_BYTES + tile_i * kTileBytes;
+      const uint32_t s2 = scale2<AT>(sc[u]);
+#pragma unroll
+      for (int ci = 0; ci < NCH; ++ci) {
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw[u][ci / 4]);
+        uint32_t o[4];
+        dq_int4_chunk<AT>(wv[ci % 4], s2, o);
+        sts16(swz(atile, row, c0 + ci), o[0], o[1], o[2], o[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[s]);
+    }
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < MB; ++u) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) raw[u][i] = nraw[u][i];
+        sc[u] = nsc[u];
+      }
+    }
+  }
+  return true;
+}
+
 template <typename AT, bool UP>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const GemvParams p) {
   using G = Geo<UP>;
@@ -380,6 +445,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const GemvParams p
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
       TcTile d;
       tc_describe<UP>(p, tile, rb_per_item, d);
+      if (d.wtype == MOEB200_I4 && d.gs % BK == 0 && nkb % 2 == 0) {
+        if (!dq_int4_tile<AT, UP, G::STAGES, G::STAGE_BYTES>(d, nkb, tile_i, row, c0, st, sbase, empty, full_a,
+                                                             p.status, lane)) {
+          ok = false;
+          break;
+        }
+        continue;
+      }
       Raw cur;
       dq_load<UP>(d, 0, tile_i, row, c0, cur);
       for (int kb = 0; kb < nkb; ++kb, ++st) {

@@ -1,12 +1,12 @@
-// Grouped expert GEMV ("decode path") shared declarations.
+// Grouped expert GEMV ("decode path") and shared work-item declarations.
 #pragma once
 
 #include "common.cuh"
 
 namespace moeb200 {
 
-// One unit of grouped work: up to 8*NB routed pairs that share one (expert, precision slot).
-// Field addresses are resolved by the producer of the list (dispatch or the pointer-table entry).
+// One unit of grouped work: up to 8*NB (GEMV) or 128 (GEMM) routed pairs that share one
+// (expert, precision slot). Field addresses are resolved by whoever builds the list.
 struct Item {
   int64_t p_guq;  // gate_up.q (float records: gate_up)
   int64_t p_gus;  // gate_up.s (float records: unused)
@@ -36,32 +36,40 @@ struct GemvParams {
   int32_t I;
   int32_t T;
   const void* x;   // [T, H] activations
-  void* h;         // [n_pairs, I] activations, row j = sorted pair j
+  void* h;         // [n_pairs, I] activations, row j = sorted pair j (unsplit up phase)
+  float* pre;      // [n_pairs, 2I] fp32 gate|up pre-activations (split-K up phase), else null
   float* acc;      // [T, H] fp32 combine buffer
   int32_t* status;
   LayoutDev lay[4];
-  int32_t scale_slot_bytes;  // bytes of one per-tile scale block slot
-  int32_t zero_acc;          // up phase: zero acc before use
+  int32_t ksplit_up;    // K splits of the up phase (1 = write h directly)
+  int32_t ksplit_dn;    // K splits of the down phase
+  int32_t stage_bytes;  // bytes of one warp stage (32 padded row segments)
+  int32_t zero_acc;     // up phase: zero acc before use
 };
 
-// Launch-time geometry shared by host and device.
+// Geometry shared by host and device.
 constexpr int kGemvStages = 2;
-constexpr int kGemvWarps = 6;
-constexpr int kStageRowBytes = 192;   // max padded row stride of one stage (int8 layout)
-constexpr int kStepBytes = 128;       // bytes of one weight row per pipeline step (<= kStageRowBytes - 64)
-constexpr int kStageBytes = 32 * kStageRowBytes;
+constexpr int kGemvMaxWarps = 12;
+constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline step
+constexpr int kSplitCols = 512;  // K splits are multiples of this many columns
 
-__host__ __device__ inline int gemv_warp_smem(int scale_slot_bytes) {
-  return kGemvStages * kStageBytes + kGemvStages * scale_slot_bytes;
+// Padded stride of one 256-byte row segment in a stage, per record element type: fragment reads of
+// the eight rows a warp touches at once then fall in different banks.
+__host__ __device__ inline int gemv_row_stride(int wtype) {
+  return wtype == MOEB200_I4 ? 288 : wtype == MOEB200_I8 ? 320 : 272;
+}
+
+__host__ __device__ inline int gemv_smem_bytes(int stage_bytes, int warps) {
+  return warps * (kGemvStages * stage_bytes + kGemvStages * 8);
 }
 
 // host launchers (gemv.cu)
-cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, cudaStream_t s);
-cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, cudaStream_t s);
+cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
+cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s);
+int gemv_occupancy(int act_type, int nb, bool up, bool split, int smem, int warps);
 // tcgen05 grouped GEMM (gemm_tc.cu): items of up to 128 pairs, I and H multiples of 128
 cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s);
 cudaError_t launch_gemm_down(const GemvParams& p, int act_type, int grid, cudaStream_t s);
-int gemv_smem_bytes(int scale_slot_bytes);
 
 }  // namespace moeb200
