@@ -153,7 +153,7 @@ class Clocks:
 class Stack:
     """The 16-layer MoE stack of config 1 with every record resident on the device."""
 
-    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0):
+    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0, ep: bool = False):
         import moeb200
         from moeb200 import format as F
         from moeb200 import ops
@@ -165,6 +165,17 @@ class Stack:
         self.lays = {p: F.record_layout(p, H, I) for p in cfg["precs"]}
         self.policy = ops.PolicySpec(**cfg["policy"])
         self.rt = moeb200.B200Runtime(cfg["precs"], self.lays, E, dev, self.policy, layers=range(L))
+        # expert parallelism when launched on several ranks: this rank holds only its expert block
+        self.ep = None
+        self.world = 1
+        if ep:
+            import torch.distributed as dist
+
+            from moeb200.ep import ExpertParallel
+
+            self.world = dist.get_world_size()
+            self.ep = ExpertParallel(self.rt)
+        self.e_lo, self.e_hi = (self.ep.e_lo, self.ep.e_hi) if self.ep else (0, E)
         g = torch.Generator(device=dev).manual_seed(seed)
         self.wr = []
         self.bias = (torch.randn(E, generator=g, device=dev) if cfg.get("bias") else None)
@@ -173,10 +184,17 @@ class Stack:
             for e in range(E):
                 gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
                 dn = torch.randn(H, I, generator=g, device=dev) * 0.02
+                if not self.e_lo <= e < self.e_hi:
+                    continue
                 for p in cfg["precs"]:
                     self.rt.add_record(li, e, p, F.encode_record(self.lays[p], gu, dn))
         self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"], self.bias) for w in self.wr]
-        self.experts = [moeb200.B200Experts(self.rt, li, torch.nn.SiLU(), E) for li in range(L)]
+        if self.ep:
+            from moeb200.ep import B200EPExperts
+
+            self.experts = [B200EPExperts(self.ep, li, torch.nn.SiLU(), E) for li in range(L)]
+        else:
+            self.experts = [moeb200.B200Experts(self.rt, li, torch.nn.SiLU(), E) for li in range(L)]
         self.record_bytes = {p: self.lays[p]["record_bytes"] for p in cfg["precs"]}
 
     # device-resident step: fused router (+ mask) -> experts, residual between layers
@@ -194,20 +212,40 @@ class Stack:
         tables = [self.rt._ctables[li] for li in range(L)]
         miss = self.rt.miss
 
+        ep = self.ep
+
         def step():
             for li in range(L):
                 b = self.bufs[li]
                 x = self.xs[li]
                 ops.router(x, self.wr[li], k, cfg["renorm"], self.bias, pols[li], want_probs=False, out=b)
-                ops.experts_forward(tables[li], x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li],
-                                    miss=miss)
+                if ep is not None:
+                    ep.run_layer(li, x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li])
+                else:
+                    ops.experts_forward(tables[li], x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li],
+                                        miss=miss)
                 torch.add(x, self.outs[li], out=self.xs[li + 1])
         return step
 
     def launches_per_step(self) -> int:
         # per layer: router logits, router top-k (+ levels), dispatch (count, scan, scatter),
-        # gate/up GEMV, down GEMV, finalize
-        return self.cfg["layers"] * 8
+        # gate/up GEMV, down GEMV, finalize; expert parallel: + pack, unpack, combine, no finalize
+        return self.cfg["layers"] * (10 if self.ep else 8)
+
+    def gathered_routing(self, li: int):
+        """idx, level, skip of every rank's tokens for layer li (numpy), outside any timed region."""
+        b = self.bufs[li]
+        if self.ep is None:
+            return b["idx"].cpu().numpy(), b["level"].cpu().numpy(), b["skip"].cpu().numpy().astype(bool)
+        import torch.distributed as dist
+
+        outs = []
+        for name in ("idx", "level", "skip"):
+            t = b[name]
+            full = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(full, t.contiguous())
+            outs.append(full.cpu().numpy())
+        return outs[0], outs[1], outs[2].astype(bool)
 
     def e2e_step(self, x_host: torch.Tensor, x_dev: torch.Tensor, y_host: torch.Tensor):
         x_dev.copy_(x_host, non_blocking=True)
@@ -240,16 +278,13 @@ class Stack:
             else:
                 gu_bytes[p] = nb("gate_up.q") + nb("gate_up.s")
                 dn_bytes[p] = nb("down.q") + nb("down.s")
-        T, H, I = self.xs[0].shape[0], cfg["H"], cfg["I"]
+        T, H, I = self.xs[0].shape[0] * self.world, cfg["H"], cfg["I"]
         for li in range(cfg["layers"]):
-            b = self.bufs[li]
-            idx = b["idx"].cpu().numpy()
-            lvl = b["level"].cpu().numpy()
-            skip = b["skip"].cpu().numpy().astype(bool)
+            idx, lvl, skip = self.gathered_routing(li)
             used = set()
             for t in range(idx.shape[0]):
                 for j in range(idx.shape[1]):
-                    if skip[t, j]:
+                    if skip[t, j] or not self.e_lo <= int(idx[t, j]) < self.e_hi:
                         continue
                     lv = int(lvl[t, j])
                     slot = min(lv, P - 1) if P >= 3 else (0 if lv == 0 else P - 1)
@@ -437,7 +472,7 @@ def main():
     from moeb200 import ops as _ops
 
     _ops.set_path(args.path)
-    stack = Stack(cfg, dev, seed=0)
+    stack = Stack(cfg, dev, seed=0, ep=world > 1)
     T = args.batch if not args.ncu or args.config == "c1" else cfg["T"]
     if args.ncu:
         step = stack.make_device_step(T)
@@ -510,7 +545,7 @@ def main():
     e2e = T * world / (e2e_ms / 1e3)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         stack.make_device_step(T)
         stack.xs[0].copy_(x0)
         st = stack.make_device_step(T)
@@ -522,7 +557,7 @@ def main():
                "sample": sample}
 
     extra = {}
-    for name in [c for c in args.extra.split(",") if c]:
+    for name in [c for c in args.extra.split(",") if c and world == 1]:
         cfgx = {"c0": CFG0, "c2": CFG2}[name]
         extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks)
 
@@ -535,7 +570,8 @@ def main():
             "config": {"workload": f"c1 OLMoE-1B-7B 16-layer MoE stack decode, T={T}/GPU, "
                                    "fp16/int4 by router prob >= 0.1, all experts resident",
                        "global_batch": T * world, "layers": L, "experts": CFG1["E"], "top_k": CFG1["k"],
-                       "hidden": H, "inter": CFG1["I"], "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+                       "hidden": H, "inter": CFG1["I"], "parallelism": f"ep{world} (experts in contiguous blocks, NCCL all_gather dispatch + "
+                                      "all_to_all combine)" if world > 1 else "1gpu",
                        "l2": "no flush: each step streams ~%.1f GB of records (> 126 MB L2)" % (
                            (rb["up"] + rb["down"]) / 1e9),
                        "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks"},

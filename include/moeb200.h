@@ -172,6 +172,28 @@ int moeb200_experts_forward(const moeb200_expert_table* experts, const void* x, 
                             const uint8_t* skip, void* out, int32_t* miss, void* ws, size_t ws_bytes,
                             void* stream);
 size_t moeb200_experts_workspace(const moeb200_expert_table* experts, int32_t T, int32_t k);
+/* ---- expert parallelism (no reference counterpart: moelab runs on one GPU) ---------------------
+ * moeb200_experts_forward restricted to the experts [e_lo, e_hi) that this GPU owns: pairs routed to
+ * other experts are dropped (not counted in miss), and the fp32 sums over the kept pairs are written
+ * to part [T,H] (overwritten, not cast), so partial results of several GPUs can be added exactly.
+ * Uses the workspace of moeb200_experts_workspace(experts, T, k). */
+int moeb200_experts_forward_part(const moeb200_expert_table* experts, int32_t e_lo, int32_t e_hi, const void* x,
+                                 int32_t act_type, int32_t T, const int64_t* idx, const float* w, int32_t k,
+                                 const uint8_t* level, const uint8_t* skip, float* part, int32_t* miss, void* ws,
+                                 size_t ws_bytes, void* stream);
+/* Combine of expert-parallel partial sums: out[i] = act_type(sum over s = 0..G-1, in that order, of
+ * parts[s*n + i]) (+ out[i] first when add != 0), i < n. act_type: F32, F16 or BF16. */
+int moeb200_combine_parts(const float* parts, int32_t G, int64_t n, int32_t act_type, void* out, int32_t add,
+                          void* stream);
+/* Exchange rows: one token as [x: H act_type values | idx: k int64 | w: k float32 | level: k uint8 |
+ * skip: k uint8 | zero padding to a multiple of 16 bytes] (moeb200_ep_row_bytes bytes), so one
+ * collective or peer copy moves a rank's tokens with their routing. level/skip NULL on pack write
+ * zeros; on unpack x, level and skip may be NULL (not written). x and rows 16-byte aligned. */
+size_t moeb200_ep_row_bytes(int32_t H, int32_t k, int32_t act_type);
+int moeb200_ep_pack(const void* x, const int64_t* idx, const float* w, const uint8_t* level, const uint8_t* skip,
+                    int32_t T, int32_t H, int32_t k, int32_t act_type, void* rows, void* stream);
+int moeb200_ep_unpack(const void* rows, int32_t n, int32_t H, int32_t k, int32_t act_type, void* x, int64_t* idx,
+                      float* w, uint8_t* level, uint8_t* skip, void* stream);
 
 /* Every workspace starts with a device status word that kernels set instead of hanging or
  * faulting (0 = OK, 1 = a bounded wait gave up, 2 = an expert index outside [0, E) reached

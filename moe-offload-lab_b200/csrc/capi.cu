@@ -221,7 +221,7 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
     CUDA_TRY(trace_mark(1, s));
     CUDA_TRY(launch_gemm_down(gp, act, grid_dn, s));
     CUDA_TRY(trace_mark(2, s));
-    CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
+    if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
     return MOEB200_OK;
   }
   const int sms = num_sms_cached();
@@ -255,7 +255,7 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
   CUDA_TRY(trace_mark(1, s));
   CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, warps, s));
   CUDA_TRY(trace_mark(2, s));
-  CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
+  if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
   return MOEB200_OK;
 }
 
@@ -418,6 +418,8 @@ int moeb200_dispatch(const int64_t* idx, const uint8_t* level, const uint8_t* sk
   DispatchParams dp{};
   Carve c(ws);
   WsHeader* hdr = c.take<WsHeader>(1);
+  dp.e_lo = 0;
+  dp.e_hi = E;
   dp.nblk = (n + kDispBlock - 1) / kDispBlock;
   dp.blk_k = c.take<int32_t>((size_t)dp.nblk * E * P);
   dp.blk_e = c.take<int32_t>((size_t)dp.nblk * E);
@@ -502,13 +504,20 @@ size_t moeb200_experts_workspace(const moeb200_expert_table* ex, int32_t T, int3
       .bytes;
 }
 
-int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32_t act_type, int32_t T,
-                            const int64_t* idx, const float* w, int32_t k, const uint8_t* level, const uint8_t* skip,
-                            void* out, int32_t* miss, void* ws, size_t ws_bytes, void* stream) {
-  if (!ex || !ex->table || !x || !idx || !w || !out || !ws) return fail(MOEB200_ERR_INVALID, "experts_forward: null pointer");
+namespace {
+// Shared body of moeb200_experts_forward (out in act_type) and moeb200_experts_forward_part
+// (part: fp32 partial sums over the experts [e_lo, e_hi), written straight by the down phase).
+int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e_hi, const void* x, int32_t act_type,
+                         int32_t T, const int64_t* idx, const float* w, int32_t k, const uint8_t* level,
+                         const uint8_t* skip, void* out, float* part, int32_t* miss, void* ws, size_t ws_bytes,
+                         void* stream) {
+  if (!ex || !ex->table || !x || !idx || !w || (!out && !part) || !ws)
+    return fail(MOEB200_ERR_INVALID, "experts_forward: null pointer");
   const int P = ex->n_prec, E = ex->num_experts;
   if (P <= 0 || P > 4 || E <= 0 || (int64_t)E * P > kMaxKeys)
     return fail(MOEB200_ERR_INVALID, "experts_forward: bad table (P=%d, E=%d, E*P <= %d)", P, E, kMaxKeys);
+  if (e_lo < 0 || e_hi > E || e_lo >= e_hi)
+    return fail(MOEB200_ERR_INVALID, "experts_forward: bad expert range [%d, %d) of %d", e_lo, e_hi, E);
   if (T <= 0 || k <= 0 || k > 32 || (int64_t)T * k >= (1ll << 30))
     return fail(MOEB200_ERR_INVALID, "experts_forward: bad sizes T=%d k=%d", T, k);
   if (act_type != MOEB200_F16 && act_type != MOEB200_BF16)
@@ -541,6 +550,8 @@ int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32
   dp.k = k;
   dp.E = E;
   dp.P = P;
+  dp.e_lo = e_lo;
+  dp.e_hi = e_hi;
   dp.nblk = (n + kDispBlock - 1) / kDispBlock;
   dp.nt = nt;
   dp.counts_e = fw.counts_e;
@@ -575,13 +586,42 @@ int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32
   gp.x = x;
   gp.h = fw.h;
   gp.pre = fw.pre;
-  gp.acc = fw.acc;
+  gp.acc = part ? part : fw.acc;
   gp.status = &fw.hdr->status;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
   // upper bound on items: every key splits into ceil(c / nt) items
-  const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)E * P);
-  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, out, /*add=*/0, gemm);
+  const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)(e_hi - e_lo) * P);
+  return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, part ? nullptr : out, /*add=*/0,
+                           gemm);
+}
+}  // namespace
+
+int moeb200_experts_forward(const moeb200_expert_table* ex, const void* x, int32_t act_type, int32_t T,
+                            const int64_t* idx, const float* w, int32_t k, const uint8_t* level, const uint8_t* skip,
+                            void* out, int32_t* miss, void* ws, size_t ws_bytes, void* stream) {
+  if (!out) return fail(MOEB200_ERR_INVALID, "experts_forward: null pointer");
+  return experts_forward_impl(ex, 0, ex ? ex->num_experts : 0, x, act_type, T, idx, w, k, level, skip, out, nullptr,
+                              miss, ws, ws_bytes, stream);
+}
+
+int moeb200_experts_forward_part(const moeb200_expert_table* ex, int32_t e_lo, int32_t e_hi, const void* x,
+                                 int32_t act_type, int32_t T, const int64_t* idx, const float* w, int32_t k,
+                                 const uint8_t* level, const uint8_t* skip, float* part, int32_t* miss, void* ws,
+                                 size_t ws_bytes, void* stream) {
+  if (!part) return fail(MOEB200_ERR_INVALID, "experts_forward_part: null pointer");
+  return experts_forward_impl(ex, e_lo, e_hi, x, act_type, T, idx, w, k, level, skip, nullptr, part, miss, ws,
+                              ws_bytes, stream);
+}
+
+int moeb200_combine_parts(const float* parts, int32_t G, int64_t n, int32_t act_type, void* out, int32_t add,
+                          void* stream) {
+  if (!parts || !out) return fail(MOEB200_ERR_INVALID, "combine_parts: null pointer");
+  if (G <= 0 || G > 64 || n <= 0) return fail(MOEB200_ERR_INVALID, "combine_parts: bad sizes G=%d n=%lld", G, (long long)n);
+  if (act_type != MOEB200_F16 && act_type != MOEB200_BF16 && act_type != MOEB200_F32)
+    return fail(MOEB200_ERR_UNSUPPORTED, "combine_parts: output must be F32, F16 or BF16");
+  CUDA_TRY(launch_combine_parts(parts, G, n, act_type, out, add, static_cast<cudaStream_t>(stream)));
+  return MOEB200_OK;
 }
 
 int moeb200_check_workspace(void* ws, int32_t* status, void* stream) {

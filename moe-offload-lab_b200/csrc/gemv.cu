@@ -563,6 +563,16 @@ __global__ void finalize_kernel(const float* __restrict__ acc, AT* __restrict__ 
   }
 }
 
+// out[i] = sum over s = 0..G-1, in that order, of parts[s*n + i] (+ out[i] when add), cast once.
+template <typename AT>
+__global__ void combine_parts_kernel(const float* __restrict__ parts, int G, int64_t n, AT* __restrict__ out, int add) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int g = 0; g < G; ++g) v += parts[(int64_t)g * n + i];
+    out[i] = from_f32<AT>(add ? to_f32<AT>(out[i]) + v : v);
+  }
+}
+
 template <typename AT, int NB, bool UP, bool SPLIT>
 cudaError_t launch_t(const GemvParams& p, int grid, int warps, cudaStream_t s) {
   const int smem = gemv_smem_bytes(p.stage_bytes, warps);
@@ -615,6 +625,20 @@ cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, 
 cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s) {
   return act_type == MOEB200_BF16 ? launch_phase<__nv_bfloat16, false>(p, nb, grid, warps, s)
                                   : launch_phase<__half, false>(p, nb, grid, warps, s);
+}
+
+cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_type, void* out, int add,
+                                 cudaStream_t s) {
+  const int threads = 256;
+  const int64_t nblk = (n + threads - 1) / threads;
+  const int grid = (int)(nblk < 148 * 8 ? nblk : 148 * 8);
+  if (act_type == MOEB200_BF16)
+    combine_parts_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(parts, G, n, static_cast<__nv_bfloat16*>(out), add);
+  else if (act_type == MOEB200_F16)
+    combine_parts_kernel<__half><<<grid, threads, 0, s>>>(parts, G, n, static_cast<__half*>(out), add);
+  else
+    combine_parts_kernel<float><<<grid, threads, 0, s>>>(parts, G, n, static_cast<float*>(out), add);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s) {

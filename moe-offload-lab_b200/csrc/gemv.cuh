@@ -67,6 +67,8 @@ __host__ __device__ inline int gemv_smem_bytes(int stage_bytes, int warps) {
 cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
 cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s);
+cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_type, void* out, int add,
+                                 cudaStream_t s);
 int gemv_occupancy(int act_type, int nb, bool up, bool split, int smem, int warps);
 // tcgen05 grouped GEMM (gemm_tc.cu): items of up to 128 pairs, I and H multiples of 128
 cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s);

@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(32) dispatch_count_kernel(DispatchParams p) {
       const int64_t ev = p.idx[i];
       if (ev < 0 || ev >= p.E) {
         if (p.status) atomicExch(p.status, kDevBadIndex);
-      } else if (!skipped) {
+      } else if (!skipped && ev >= p.e_lo && ev < p.e_hi) {
         e = (int)ev;
         const int lv = p.level ? p.level[i] : 0;
         key = e * p.P + slot_of(lv, p.P);

@@ -25,6 +25,7 @@ struct DispatchParams {
   const uint8_t* level;   // [T*k] or null
   const uint8_t* skip;    // [T*k] or null
   int32_t T, k, E, P;
+  int32_t e_lo, e_hi;     // experts kept by this dispatch (expert parallelism); others are dropped
   int32_t nblk;           // ceil(T*k / kDispBlock)
   int32_t nt;             // max pairs per work item
   // outputs

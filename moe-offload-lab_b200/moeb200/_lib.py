@@ -59,6 +59,12 @@ _SIGS = {
     "moeb200_experts_forward": (C.c_int, [C.POINTER(ExpertTable), _P, C.c_int32, C.c_int32, _P, _P, C.c_int32,
                                           _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "moeb200_experts_workspace": (C.c_size_t, [C.POINTER(ExpertTable), C.c_int32, C.c_int32]),
+    "moeb200_experts_forward_part": (C.c_int, [C.POINTER(ExpertTable), C.c_int32, C.c_int32, _P, C.c_int32,
+                                               C.c_int32, _P, _P, C.c_int32, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "moeb200_combine_parts": (C.c_int, [_P, C.c_int32, C.c_int64, C.c_int32, _P, C.c_int32, _P]),
+    "moeb200_ep_row_bytes": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32]),
+    "moeb200_ep_pack": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
+    "moeb200_ep_unpack": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, _P, _P]),
     "moeb200_check_workspace": (C.c_int, [_P, C.POINTER(C.c_int32), _P]),
 }
 

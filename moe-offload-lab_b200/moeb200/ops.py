@@ -182,6 +182,74 @@ def experts_forward(table: _lib.ExpertTable, x: torch.Tensor, idx: torch.Tensor,
     return out
 
 
+def experts_forward_part(table: _lib.ExpertTable, e_lo: int, e_hi: int, x: torch.Tensor, idx: torch.Tensor,
+                         w: torch.Tensor, level: torch.Tensor | None, skip: torch.Tensor | None,
+                         part: torch.Tensor | None = None, miss: torch.Tensor | None = None,
+                         ws: torch.Tensor | None = None) -> torch.Tensor:
+    """part[T,H] fp32 = sum over the kept pairs routed to experts [e_lo, e_hi) of w * expert(x)."""
+    _need_cuda(x, idx, w, level, skip)
+    T = x.shape[0]
+    k = idx.shape[1]
+    if part is None:
+        part = torch.empty(T, x.shape[1], dtype=torch.float32, device=x.device)
+    if part.dtype != torch.float32 or part.shape != (T, x.shape[1]) or not part.is_contiguous():
+        raise ValueError("part must be a contiguous float32 [T, H] tensor")
+    L = _lib.lib()
+    nbytes = L.moeb200_experts_workspace(C.byref(table), T, k)
+    if ws is None:
+        ws = workspace(nbytes, x.device, slot=0)
+    elif ws.numel() < nbytes:
+        raise ValueError("workspace too small")
+    _lib.check(L.moeb200_experts_forward_part(C.byref(table), e_lo, e_hi, _ptr(x), _act(x.dtype), T, _ptr(idx),
+                                              _ptr(w), k, _ptr(level), _ptr(skip), _ptr(part), _ptr(miss), _ptr(ws),
+                                              ws.numel(), _stream(x.device)))
+    return part
+
+
+def combine_parts(parts: torch.Tensor, out: torch.Tensor, add: bool = False) -> torch.Tensor:
+    """out = cast(sum over parts[0..G-1]) in that order (+ out when add); parts fp32 [G, *out.shape]."""
+    _need_cuda(parts, out)
+    if parts.dtype != torch.float32 or not parts.is_contiguous() or parts.shape[1:] != out.shape:
+        raise ValueError("parts must be contiguous float32 [G, *out.shape]")
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    _lib.check(_lib.lib().moeb200_combine_parts(_ptr(parts), parts.shape[0], out.numel(), _act(out.dtype), _ptr(out),
+                                                int(add), _stream(out.device)))
+    return out
+
+
+def ep_row_bytes(H: int, k: int, dtype: torch.dtype) -> int:
+    """Bytes of one exchange row (token hidden row + its routing) for expert parallelism."""
+    return int(_lib.lib().moeb200_ep_row_bytes(H, k, _act(dtype)))
+
+
+def ep_pack(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, level: torch.Tensor | None,
+            skip: torch.Tensor | None, rows: torch.Tensor | None = None) -> torch.Tensor:
+    """rows [T, ep_row_bytes] uint8 = each token's hidden row followed by its routing."""
+    _need_cuda(x, idx, w, level, skip)
+    T, H = x.shape
+    k = idx.shape[1]
+    rb = ep_row_bytes(H, k, x.dtype)
+    if rows is None:
+        rows = torch.empty(T, rb, dtype=torch.uint8, device=x.device)
+    if rows.shape != (T, rb) or rows.dtype != torch.uint8 or not rows.is_contiguous():
+        raise ValueError(f"rows must be contiguous uint8 [{T}, {rb}]")
+    _lib.check(_lib.lib().moeb200_ep_pack(_ptr(x), _ptr(idx), _ptr(w), _ptr(level), _ptr(skip), T, H, k,
+                                          _act(x.dtype), _ptr(rows), _stream(x.device)))
+    return rows
+
+
+def ep_unpack(rows: torch.Tensor, H: int, k: int, dtype: torch.dtype, x: torch.Tensor, idx: torch.Tensor,
+              w: torch.Tensor, level: torch.Tensor | None, skip: torch.Tensor | None) -> None:
+    """Split exchange rows [n, ep_row_bytes] back into x [n,H], idx/w/level/skip [n,k]."""
+    _need_cuda(rows, x, idx, w, level, skip)
+    n = rows.shape[0]
+    if rows.shape[1] != ep_row_bytes(H, k, dtype) or not rows.is_contiguous():
+        raise ValueError("rows do not match (H, k, dtype)")
+    _lib.check(_lib.lib().moeb200_ep_unpack(_ptr(rows), n, H, k, _act(dtype), _ptr(x), _ptr(idx), _ptr(w),
+                                            _ptr(level), _ptr(skip), _stream(rows.device)))
+
+
 def set_path(path: str) -> None:
     """Expert-product path for this thread's next experts_forward calls: "auto", "gemv" or "gemm"."""
     _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2}[path]))
