@@ -90,6 +90,10 @@ int moeb200_num_sms(void);
  * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 16*E, grouped GEMV
  * otherwise), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128). */
 int moeb200_set_path(int32_t path);
+/* Pairs per grouped-GEMV work item for the following moeb200_experts_forward calls on the calling
+ * thread (no reference counterpart): 0 = automatic (16 when T >= 64, else 8), 8 or 16. A larger
+ * item streams an expert's record once for more tokens at the cost of more multiplies per byte. */
+int moeb200_set_item_tokens(int32_t nt);
 
 /* Measurement hooks (no reference counterpart). Between trace_begin and trace_end, every
  * grouped-expert call of the calling thread records CUDA events (owned by the library) on its
@@ -195,6 +199,18 @@ int moeb200_ep_pack(const void* x, const int64_t* idx, const float* w, const uin
 int moeb200_ep_unpack(const void* rows, int32_t n, int32_t H, int32_t k, int32_t act_type, void* x, int64_t* idx,
                       float* w, uint8_t* level, uint8_t* skip, void* stream);
 
+/* ---- shared expert ---------------------------------------------------------------------------
+ * Replaces the shared-expert branch of Qwen3NextSparseMoeBlock.forward
+ * (qwen3_next/modeling_qwen3_next.py:789-801), which runs beside the experts module:
+ *   out[t] (+)= sigmoid(x[t] . wg) * down(silu(gate x[t]) * up x[t])   for t < T.
+ * The shared MLP is one record of any store precision (gate_up = [gate_proj; up_proj], down =
+ * down_proj; 256-byte aligned). wg [H] (act_type) is the shared_expert_gate weight: the logit is
+ * accumulated in fp32 and rounded to act_type as F.linear returns it, the sigmoid is fp32.
+ * add != 0 adds into out (after the routed experts), 0 overwrites it. */
+int moeb200_shared_expert(const moeb200_layout* layout, const void* record, const void* wg, const void* x,
+                          int32_t act_type, int32_t T, void* out, int32_t add, void* ws, size_t ws_bytes,
+                          void* stream);
+size_t moeb200_shared_expert_workspace(const moeb200_layout* layout, int32_t T);
 /* Every workspace starts with a device status word that kernels set instead of hanging or
  * faulting (0 = OK, 1 = a bounded wait gave up, 2 = an expert index outside [0, E) reached
  * dispatch). This call copies it to *status and clears it; it is the one entry point that

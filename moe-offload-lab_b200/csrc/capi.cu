@@ -45,6 +45,7 @@ cudaError_t trace_mark(int which, cudaStream_t s) {
 }
 // Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM.
 thread_local int g_path = 0;
+thread_local int g_item_tokens = 0;  // GEMV work-item size: 0 = automatic, else 8 or 16
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -167,10 +168,11 @@ bool split_ok(const moeb200_layout* L, int nlay, bool up, int ks) {
 
 struct ForwardWs {
   WsHeader* hdr;
-  int32_t *pos_e, *pos_k, *counts_e, *counts_k, *offs_k, *blk_k, *blk_e, *rank_k, *rank_e;
+  int32_t *pos_e, *pos_k, *counts_e, *counts_k, *offs_k, *offs_e, *blk_k, *blk_e, *rank_k, *rank_e;
   Item* items;
   uint8_t* h;
   float* pre;
+  int32_t* cnt;
   float* acc;
   float* logits;
   size_t bytes;
@@ -188,6 +190,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.counts_e = c.take<int32_t>(E);
   w.counts_k = c.take<int32_t>(keys);
   w.offs_k = c.take<int32_t>(keys);
+  w.offs_e = c.take<int32_t>(E);
   w.blk_k = c.take<int32_t>((size_t)nblk * keys);
   w.blk_e = c.take<int32_t>((size_t)nblk * E);
   w.rank_k = c.take<int32_t>(n);
@@ -195,6 +198,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.items = c.take<Item>(n);
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
   w.pre = c.take<float>((size_t)std::min(n, kMaxSplitPairs) * 2 * I);
+  w.cnt = c.take<int32_t>((size_t)std::min(n, kMaxSplitPairs) * (I / 16));
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
   return w;
@@ -244,12 +248,15 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
   const int smem = gemv_smem_bytes(gp.stage_bytes, warps);
   const bool split = ks_up > 1;
   const int occ_up = std::max(1, gemv_occupancy(act, nb, true, split, smem, warps));
-  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, split, smem, warps));
+  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, false, smem, warps));
   const int64_t tiles_up = (int64_t)max_items * rb_up * ks_up;
   const int64_t tiles_dn = (int64_t)max_items * rb_dn * ks_dn;
   const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + warps - 1) / warps));
   const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + warps - 1) / warps));
-  if (split) CUDA_TRY(cudaMemsetAsync(gp.pre, 0, (size_t)n_pairs * 2 * gp.I * sizeof(float), s));
+  if (split) {
+    CUDA_TRY(cudaMemsetAsync(gp.pre, 0, (size_t)n_pairs * 2 * gp.I * sizeof(float), s));
+    CUDA_TRY(cudaMemsetAsync(gp.tile_cnt, 0, (size_t)max_items * (gp.I / 16) * sizeof(int32_t), s));
+  }
   CUDA_TRY(trace_mark(0, s));
   CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, warps, s));
   CUDA_TRY(trace_mark(1, s));
@@ -292,6 +299,52 @@ __global__ void table_items_kernel(const int64_t* __restrict__ tab, const float*
   if (threadIdx.x == 0) *n_items = base;
 }
 
+// Shared expert (Qwen3-Next): one warp per token computes the gate logit x[t] . wg (fp32 FMA chain
+// over the columns lane*8 + 256*i + j, xor butterfly, rounded to the activation type as F.linear
+// returns it) and the combine weight sigmoid(logit) in fp32; the first threads write the work items
+// (consecutive tokens, nt per item) of the single shared record.
+template <typename AT>
+__global__ void __launch_bounds__(256) shared_gate_kernel(const AT* __restrict__ x, const AT* __restrict__ wg, int T,
+                                                          int H, int nt, int64_t rec, LayoutOffs lo,
+                                                          float* __restrict__ w, int32_t* __restrict__ pos,
+                                                          Item* __restrict__ items, int32_t* __restrict__ n_items) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int ni = (T + nt - 1) / nt;
+  if (gtid < ni) {
+    Item it;
+    it.p_guq = rec + lo.gu_q;
+    it.p_gus = rec + lo.gu_s;
+    it.p_dnq = rec + lo.dn_q;
+    it.p_dns = rec + lo.dn_s;
+    it.slot = 0;
+    it.start = gtid * nt;
+    it.ntok = min(nt, T - gtid * nt);
+    it._pad = 0;
+    items[gtid] = it;
+  }
+  if (gtid == 0) *n_items = ni;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const AT* xr = x + (int64_t)t * H;
+  float acc = 0.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wg + c));
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + c));
+    const AT* wa = reinterpret_cast<const AT*>(&wv);
+    const AT* xa = reinterpret_cast<const AT*>(&xv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<AT>(xa[i]), to_f32<AT>(wa[i]), acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    const float g = to_f32<AT>(from_f32<AT>(acc));
+    w[t] = 1.f / (1.f + expf(-g));
+    pos[t] = t;
+  }
+}
+
 }  // namespace
 
 namespace moeb200 {
@@ -325,6 +378,12 @@ int moeb200_num_sms(void) { return num_sms_cached(); }
 int moeb200_set_path(int32_t path) {
   if (path < 0 || path > 2) return fail(MOEB200_ERR_INVALID, "set_path: path must be 0 (auto), 1 (GEMV) or 2 (GEMM)");
   g_path = path;
+  return MOEB200_OK;
+}
+
+int moeb200_set_item_tokens(int32_t nt) {
+  if (nt != 0 && nt != 8 && nt != 16) return fail(MOEB200_ERR_INVALID, "set_item_tokens: 0 (automatic), 8 or 16");
+  g_item_tokens = nt;
   return MOEB200_OK;
 }
 
@@ -404,6 +463,7 @@ size_t moeb200_dispatch_workspace(int32_t T, int32_t k, int32_t E, int32_t P) {
   c.take<int32_t>(n);
   c.take<int32_t>(n);
   c.take<int32_t>((size_t)E * P);
+  c.take<int32_t>(E);
   return c.off;
 }
 
@@ -426,6 +486,7 @@ int moeb200_dispatch(const int64_t* idx, const uint8_t* level, const uint8_t* sk
   dp.rank_k = c.take<int32_t>(n);
   dp.rank_e = c.take<int32_t>(n);
   dp.offs_k = c.take<int32_t>((size_t)E * P);
+  dp.offs_e = c.take<int32_t>(E);
   dp.idx = idx;
   dp.level = level;
   dp.skip = skip;
@@ -452,6 +513,7 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<int32_t>(n);
   c.take<uint8_t>((size_t)n * layout->inter * 2);
   c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * layout->inter);
+  c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (layout->inter / 16));
   c.take<float>((size_t)layout->hidden);
   return c.off;
 }
@@ -476,6 +538,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   int32_t* pos = c.take<int32_t>(n);
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
   float* pre = c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * I);
+  int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (I / 16));
   float* acc = c.take<float>((size_t)H);
   table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
   CUDA_TRY(cudaGetLastError());
@@ -491,6 +554,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.x = x;
   gp.h = hbuf;
   gp.pre = pre;
+  gp.tile_cnt = cnt;
   gp.acc = acc;
   gp.status = &hdr->status;
   gp.lay[0] = to_dev(*layout);
@@ -541,7 +605,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
     if (g_path == 2) return fail(MOEB200_ERR_UNSUPPORTED, "GEMM path needs H and I multiples of 128 (H=%d, I=%d)", H, I);
     gemm = false;
   }
-  const int nt = gemm ? 128 : (T >= 128 ? 16 : 8);
+  const int nt = gemm ? 128 : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
   DispatchParams dp{};
   dp.idx = idx;
   dp.level = level;
@@ -558,6 +622,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   dp.pos_e = fw.pos_e;
   dp.counts_k = fw.counts_k;
   dp.offs_k = fw.offs_k;
+  dp.offs_e = fw.offs_e;
   dp.pos_k = fw.pos_k;
   dp.n_kept = &fw.hdr->n_kept;
   dp.blk_k = fw.blk_k;
@@ -586,6 +651,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.x = x;
   gp.h = fw.h;
   gp.pre = fw.pre;
+  gp.tile_cnt = fw.cnt;
   gp.acc = part ? part : fw.acc;
   gp.status = &fw.hdr->status;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
@@ -622,6 +688,84 @@ int moeb200_combine_parts(const float* parts, int32_t G, int64_t n, int32_t act_
     return fail(MOEB200_ERR_UNSUPPORTED, "combine_parts: output must be F32, F16 or BF16");
   CUDA_TRY(launch_combine_parts(parts, G, n, act_type, out, add, static_cast<cudaStream_t>(stream)));
   return MOEB200_OK;
+}
+
+size_t moeb200_shared_expert_workspace(const moeb200_layout* layout, int32_t T) {
+  if (!layout || T <= 0) return 0;
+  Carve c(nullptr);
+  c.take<WsHeader>(1);
+  c.take<Item>(T);
+  c.take<int32_t>(T);
+  c.take<float>(T);
+  c.take<uint8_t>((size_t)T * layout->inter * 2);
+  c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * layout->inter);
+  c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (layout->inter / 16));
+  c.take<float>((size_t)T * layout->hidden);
+  return c.off;
+}
+
+int moeb200_shared_expert(const moeb200_layout* layout, const void* record, const void* wg, const void* x,
+                          int32_t act_type, int32_t T, void* out, int32_t add, void* ws, size_t ws_bytes,
+                          void* stream) {
+  if (!layout || !record || !wg || !x || !out || !ws) return fail(MOEB200_ERR_INVALID, "shared_expert: null pointer");
+  if (T <= 0 || T >= (1 << 24)) return fail(MOEB200_ERR_INVALID, "shared_expert: bad T=%d", T);
+  if (act_type != MOEB200_F16 && act_type != MOEB200_BF16)
+    return fail(MOEB200_ERR_UNSUPPORTED, "shared_expert: activations must be F16 or BF16");
+  const int H = layout->hidden, I = layout->inter;
+  int rc = check_shapes(H, I);
+  if (rc) return rc;
+  rc = check_layout(*layout, H, I);
+  if (rc) return rc;
+  if (reinterpret_cast<uintptr_t>(record) % 256) return fail(MOEB200_ERR_INVALID, "shared_expert: record must be 256-byte aligned");
+  if (ws_bytes < moeb200_shared_expert_workspace(layout, T))
+    return fail(MOEB200_ERR_WORKSPACE, "shared_expert: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool gemm_ok = (H % 128 == 0) && (I % 128 == 0);
+  bool gemm = g_path == 2 || (g_path == 0 && T >= 64);
+  if (gemm && !gemm_ok) {
+    if (g_path == 2) return fail(MOEB200_ERR_UNSUPPORTED, "GEMM path needs H and I multiples of 128 (H=%d, I=%d)", H, I);
+    gemm = false;
+  }
+  const int nt = gemm ? 128 : g_item_tokens ? g_item_tokens : (T >= 128 ? 16 : 8);
+  Carve c(ws);
+  WsHeader* hdr = c.take<WsHeader>(1);
+  Item* items = c.take<Item>(T);
+  int32_t* pos = c.take<int32_t>(T);
+  float* wt = c.take<float>(T);
+  uint8_t* hbuf = c.take<uint8_t>((size_t)T * I * 2);
+  float* pre = c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * I);
+  int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (I / 16));
+  float* acc = c.take<float>((size_t)T * H);
+  const LayoutOffs lo{layout->off_gu_q, is_int(layout->wtype) ? layout->off_gu_s : 0, layout->off_dn_q,
+                      is_int(layout->wtype) ? layout->off_dn_s : 0};
+  const int64_t rec = (int64_t)reinterpret_cast<uintptr_t>(record);
+  const int grid = (T + 7) / 8;
+  if (act_type == MOEB200_BF16)
+    shared_gate_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                           static_cast<const __nv_bfloat16*>(wg), T, H, nt, rec, lo, wt,
+                                                           pos, items, &hdr->n_items);
+  else
+    shared_gate_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(wg), T, H,
+                                                    nt, rec, lo, wt, pos, items, &hdr->n_items);
+  CUDA_TRY(cudaGetLastError());
+  GemvParams gp{};
+  gp.items = items;
+  gp.n_items = &hdr->n_items;
+  gp.pos = pos;
+  gp.wflat = wt;
+  gp.k = 1;
+  gp.H = H;
+  gp.I = I;
+  gp.T = T;
+  gp.x = x;
+  gp.h = hbuf;
+  gp.pre = pre;
+  gp.tile_cnt = cnt;
+  gp.acc = acc;
+  gp.status = &hdr->status;
+  gp.lay[0] = to_dev(*layout);
+  gp.zero_acc = 1;
+  return run_expert_phases(gp, layout, 1, act_type, (T + nt - 1) / nt, T, nt, s, out, add ? 1 : 0, gemm);
 }
 
 int moeb200_check_workspace(void* ws, int32_t* status, void* stream) {

@@ -19,7 +19,8 @@
 // loaded while the current one is multiplied.
 //
 // Small batches split K across warps: the up phase then adds fp32 partial pre-activations into
-// pre[j, 0:2I] (gate | up) and the down phase forms h = silu(gate) * up while loading its operand.
+// pre[j, 0:2I] (gate | up); the warp whose split of a tile arrives last (a per-tile counter) forms
+// h = silu(gate) * up for the tile's 16 rows, so the down phase always reads h.
 #include <type_traits>
 
 #include "gemv.cuh"
@@ -91,12 +92,9 @@ __device__ __forceinline__ void ldg(const void* p, uint32_t (&w)[NW]) {
 }
 
 // ---- B operand (activations of the lane's token(s)): NW words = 2*NW values, natural order ---------
-// Source rows are activation rows (AT) or, in the split-K down phase, fp32 gate|up pre-activation
-// rows from which h = silu(gate) * up is formed on the fly.
-template <typename AT, int NB, bool PRE>
+template <typename AT, int NB>
 struct BSrc {
-  const void* row[NB];  // null = token slot unused (zeros)
-  int I;                // pre-activation row: gate at [0, I), up at [I, 2I)
+  const AT* row[NB];  // null = token slot unused (zeros)
 
   template <int NW>
   __device__ __forceinline__ void load(int col, uint32_t (&xb)[NB][NW]) const {
@@ -105,24 +103,8 @@ struct BSrc {
       if (row[nb] == nullptr) {
 #pragma unroll
         for (int i = 0; i < NW; ++i) xb[nb][i] = 0u;
-      } else if constexpr (!PRE) {
-        ldg<NW>(static_cast<const AT*>(row[nb]) + col, xb[nb]);
       } else {
-        const float* gp = static_cast<const float*>(row[nb]) + col;
-        const float* up = gp + I;
-        if constexpr (NW == 1) {
-          const float2 gv = *reinterpret_cast<const float2*>(gp);
-          const float2 uv = *reinterpret_cast<const float2*>(up);
-          xb[nb][0] = Dq<AT>::pack_f32(silu_mul(gv.x, uv.x), silu_mul(gv.y, uv.y));
-        } else {
-#pragma unroll
-          for (int i = 0; i < NW; i += 2) {  // 4 values per iteration
-            const float4 gv = *reinterpret_cast<const float4*>(gp + 2 * i);
-            const float4 uv = *reinterpret_cast<const float4*>(up + 2 * i);
-            xb[nb][i] = Dq<AT>::pack_f32(silu_mul(gv.x, uv.x), silu_mul(gv.y, uv.y));
-            xb[nb][i + 1] = Dq<AT>::pack_f32(silu_mul(gv.z, uv.z), silu_mul(gv.w, uv.w));
-          }
-        }
+        ldg<NW>(row[nb] + col, xb[nb]);
       }
     }
   }
@@ -279,8 +261,8 @@ __device__ __forceinline__ void chunk_float(const uint8_t* st, int rs, int c, co
 // ---- one pipeline step: the chunks of a stage, activations and scales loaded one chunk ahead ---------
 // KIND selects the chunk routine; chunks alternate between two register sets so the next chunk's
 // loads are in flight while the current chunk is multiplied.
-template <typename AT, int NB, bool PRE, int KIND>
-__device__ __forceinline__ void run_step(const uint8_t* st, int col0, int ncols, const BSrc<AT, NB, PRE>& B,
+template <typename AT, int NB, int KIND>
+__device__ __forceinline__ void run_step(const uint8_t* st, int col0, int ncols, const BSrc<AT, NB>& B,
                                          const Scales& S, int gs, float (&tot)[2][NB][4], int g, int t) {
   constexpr bool I4 = KIND == kI4w2 || KIND == kI4w1;
   constexpr bool I8 = KIND == kI8w4 || KIND == kI8w2 || KIND == kI8w1;
@@ -339,6 +321,11 @@ struct TileDesc {
   int32_t item, r0;
 };
 
+// Input columns of one K split (a multiple of kSplitCols); splits past K are empty.
+__device__ __forceinline__ int split_cols(int K, int ks_n) {
+  return ks_n > 1 ? ((K / ks_n + kSplitCols - 1) / kSplitCols) * kSplitCols : K;
+}
+
 template <bool UP>
 __device__ __forceinline__ void describe_tile(const GemvParams& p, int tile, int rb_per_item, int ks_n,
                                               TileDesc& d) {
@@ -359,7 +346,7 @@ __device__ __forceinline__ void describe_tile(const GemvParams& p, int tile, int
   d.rstride = K * d.wbits / 8;
   d.sstride = isint ? (K / d.gs) * 2 : 0;
   d.step_cols = kStepBytes * 8 / d.wbits;
-  const int kc = ks_n > 1 ? ((K / ks_n + kSplitCols - 1) / kSplitCols) * kSplitCols : K;
+  const int kc = split_cols(K, ks_n);
   d.k_lo = min(K, ks * kc);
   d.k_hi = min(K, d.k_lo + kc);
   d.nsteps = d.k_hi > d.k_lo ? (d.k_hi - d.k_lo + d.step_cols - 1) / d.step_cols : 0;
@@ -398,7 +385,6 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
   const int nwarps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  constexpr bool PRE = !UP && SPLIT;  // down phase reading split-K pre-activations
 
   if (UP && p.zero_acc) {  // the down phase reduces into acc; clear it first (grid-stride)
     const int64_t n = (int64_t)p.T * p.H;
@@ -452,8 +438,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
 
   int ctile = first, cstep = 0;
   float tot[2][NB][4];
-  BSrc<AT, NB, PRE> B;
-  B.I = p.I;
+  BSrc<AT, NB> B;
   Scales S;
   Item cit;
   auto begin_tile = [&]() {
@@ -471,8 +456,6 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
         if (UP) {
           const int tok = p.pos[j] / p.k;
           B.row[nb] = static_cast<const AT*>(p.x) + (int64_t)tok * p.H;
-        } else if (PRE) {
-          B.row[nb] = p.pre + (int64_t)j * 2 * p.I;
         } else {
           B.row[nb] = static_cast<const AT*>(p.h) + (int64_t)j * p.I;
         }
@@ -494,19 +477,19 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
     const int col0 = cd.k_lo + cstep * cd.step_cols;
     const int ncols = min(cd.step_cols, cd.k_hi - col0);
     switch (cd.kind) {
-      case kI4w2: run_step<AT, NB, PRE, kI4w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI4w1: run_step<AT, NB, PRE, kI4w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w4: run_step<AT, NB, PRE, kI8w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w2: run_step<AT, NB, PRE, kI8w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w1: run_step<AT, NB, PRE, kI8w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w4: run_step<AT, NB, PRE, kF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w2: run_step<AT, NB, PRE, kF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w1: run_step<AT, NB, PRE, kF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w4: run_step<AT, NB, PRE, kBF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w2: run_step<AT, NB, PRE, kBF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w1: run_step<AT, NB, PRE, kBF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF32w2: run_step<AT, NB, PRE, kF32w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF32w1: run_step<AT, NB, PRE, kF32w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kI4w2: run_step<AT, NB, kI4w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kI4w1: run_step<AT, NB, kI4w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kI8w4: run_step<AT, NB, kI8w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kI8w2: run_step<AT, NB, kI8w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kI8w1: run_step<AT, NB, kI8w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kF16w4: run_step<AT, NB, kF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kF16w2: run_step<AT, NB, kF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kF16w1: run_step<AT, NB, kF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kBF16w4: run_step<AT, NB, kBF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kBF16w2: run_step<AT, NB, kBF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kBF16w1: run_step<AT, NB, kBF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kF32w2: run_step<AT, NB, kF32w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
+      case kF32w1: run_step<AT, NB, kF32w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
       default: break;
     }
     const bool last = (cstep + 1 == cd.nsteps);
@@ -521,7 +504,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
           const int rrow = g + 8 * (i >> 1);
           const int j = cit.start + tk;
           if (UP) {
-            if (SPLIT) {
+            if constexpr (SPLIT) {
               float* prow = p.pre + (int64_t)j * 2 * p.I + cd.r0 + rrow;
               red_add_f32(prow, tot[0][nb][i]);
               red_add_f32(prow + p.I, tot[1][nb][i]);
@@ -538,6 +521,28 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
             red_add_f32(arow + 16 + rrow, wv * tot[1][nb][i]);
           }
         }
+      if constexpr (UP && SPLIT) {
+        // the last K split to arrive at this tile turns its 16 gate|up pre-activation rows into h
+        __threadfence();
+        __syncwarp();
+        const int kc = split_cols(p.H, ks_n);
+        const int ksplits = (p.H + kc - 1) / kc;  // non-empty splits
+        int fin = 0;
+        if (lane == 0) {
+          int32_t* cnt = p.tile_cnt + (int64_t)cd.item * rb_per_item + cd.r0 / 16;
+          fin = atomicAdd(cnt, 1) == ksplits - 1;
+        }
+        fin = __shfl_sync(0xffffffffu, fin, 0);
+        if (fin) {
+          __threadfence();
+          for (int q = lane; q < 16 * cit.ntok; q += 32) {
+            const int j = cit.start + q / 16, r = cd.r0 + (q & 15);
+            const float* prow = p.pre + (int64_t)j * 2 * p.I;
+            const float hv = silu_mul(__ldcg(prow + r), __ldcg(prow + p.I + r));
+            static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
+          }
+        }
+      }
     }
     __syncwarp();
     produce(sidx);  // refill the stage just consumed with the step kGemvStages ahead
@@ -592,10 +597,10 @@ int occupancy_t(int smem, int warps) {
   return nb;
 }
 
-// The down phase reads split-K pre-activations exactly when the up phase was split.
+// SPLIT: the up phase adds split-K partials into pre (the down phase always reads h).
 template <typename AT, bool UP>
 cudaError_t launch_phase(const GemvParams& p, int nb, int grid, int warps, cudaStream_t s) {
-  if (p.ksplit_up > 1)
+  if (UP && p.ksplit_up > 1)
     return nb == 2 ? launch_t<AT, 2, UP, true>(p, grid, warps, s) : launch_t<AT, 1, UP, true>(p, grid, warps, s);
   return nb == 2 ? launch_t<AT, 2, UP, false>(p, grid, warps, s) : launch_t<AT, 1, UP, false>(p, grid, warps, s);
 }

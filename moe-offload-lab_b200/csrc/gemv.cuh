@@ -38,6 +38,7 @@ struct GemvParams {
   const void* x;   // [T, H] activations
   void* h;         // [n_pairs, I] activations, row j = sorted pair j (unsplit up phase)
   float* pre;      // [n_pairs, 2I] fp32 gate|up pre-activations (split-K up phase), else null
+  int32_t* tile_cnt;  // [items, I/16] arrivals of the K splits of each up tile (split-K), zeroed per call
   float* acc;      // [T, H] fp32 combine buffer
   int32_t* status;
   LayoutDev lay[4];

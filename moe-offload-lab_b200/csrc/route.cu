@@ -22,31 +22,58 @@ __device__ __forceinline__ float round_act(float v) {
 }
 
 // ---- router logits --------------------------------------------------------------------------------
-template <typename AT>
+// One warp per tile of RE experts x RT tokens (a block of 8 warps = EG expert tiles x 8/EG token
+// tiles, so its warps share the router rows and token rows in L1). For every (token, expert) lane l
+// accumulates the columns l*8 + 256*i + j in that order in its own fp32 FMA chain; an xor butterfly
+// over offsets 16..1 adds the 32 lane sums. The arithmetic of each logit is therefore the same for
+// every tile shape (bit-exact with the single-token form).
+template <typename AT, int RE, int RT, int EG>
 __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict__ h, const AT* __restrict__ wr,
-                                                            int T, int H, int E, int tok_per_block,
-                                                            float* __restrict__ logits) {
+                                                            int T, int H, int E, float* __restrict__ logits) {
+  constexpr int TG = 8 / EG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
-  if (e >= E) return;
-  const int t0 = blockIdx.y * tok_per_block;
-  const int t1 = min(T, t0 + tok_per_block);
-  const AT* wrow = wr + (int64_t)e * H;
-  for (int t = t0; t < t1; ++t) {
-    const AT* xrow = h + (int64_t)t * H;
-    float acc = 0.f;
-    for (int c = lane * 8; c < H; c += 256) {
-      uint4 wv = *reinterpret_cast<const uint4*>(wrow + c);
-      uint4 xv = *reinterpret_cast<const uint4*>(xrow + c);
-      const AT* wa = reinterpret_cast<const AT*>(&wv);
-      const AT* xa = reinterpret_cast<const AT*>(&xv);
+  const int e0 = (blockIdx.x * EG + warp % EG) * RE;
+  const int t0 = (blockIdx.y * TG + warp / EG) * RT;
+  if (e0 >= E || t0 >= T) return;
+  const int ne = min(RE, E - e0), nt = min(RT, T - t0);
+  float acc[RE][RT];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<AT>(xa[i]), to_f32<AT>(wa[i]), acc);
+  for (int r = 0; r < RE; ++r)
+#pragma unroll
+    for (int q = 0; q < RT; ++q) acc[r][q] = 0.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    float wf[RE][8];
+#pragma unroll
+    for (int r = 0; r < RE; ++r) {
+      uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+      if (r < ne) wv = __ldg(reinterpret_cast<const uint4*>(wr + (int64_t)(e0 + r) * H + c));
+      const AT* wa = reinterpret_cast<const AT*>(&wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wf[r][i] = to_f32<AT>(wa[i]);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) logits[(int64_t)t * E + e] = round_act<AT>(acc);
+    for (int q = 0; q < RT; ++q) {
+      if (q < nt) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(h + (int64_t)(t0 + q) * H + c));
+        const AT* xa = reinterpret_cast<const AT*>(&xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xf = to_f32<AT>(xa[i]);
+#pragma unroll
+          for (int r = 0; r < RE; ++r) acc[r][q] = fmaf(xf, wf[r][i], acc[r][q]);
+        }
+      }
+    }
   }
+#pragma unroll
+  for (int r = 0; r < RE; ++r)
+#pragma unroll
+    for (int q = 0; q < RT; ++q) {
+      float a = acc[r][q];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0 && r < ne && q < nt) logits[(int64_t)(t0 + q) * E + e0 + r] = round_act<AT>(a);
+    }
 }
 
 // fp32 activations: 4 values per 16-byte load
@@ -255,19 +282,30 @@ __global__ void __launch_bounds__(32) dispatch_count_kernel(DispatchParams p) {
   const int b = blockIdx.x;
   const int base = b * kDispBlock;
   const int end = min(n, base + kDispBlock);
+  // keys of the whole block first (independent loads, all in flight), ranked in order below
+  int32_t* key_s = sh + keys + p.E;   // [kDispBlock]
+  int32_t* e_s = key_s + kDispBlock;  // [kDispBlock]
+  for (int i = base + lane; i < end; i += 32) {
+    int key = -1, e = -1;
+    const bool skipped = p.skip && p.skip[i];
+    const int64_t ev = p.idx[i];
+    if (ev < 0 || ev >= p.E) {
+      if (p.status) atomicExch(p.status, kDevBadIndex);
+    } else if (!skipped && ev >= p.e_lo && ev < p.e_hi) {
+      e = (int)ev;
+      const int lv = p.level ? p.level[i] : 0;
+      key = e * p.P + slot_of(lv, p.P);
+    }
+    key_s[i - base] = key;
+    e_s[i - base] = e;
+  }
+  __syncwarp();
   for (int c = base; c < end; c += 32) {
     const int i = c + lane;
     int key = -1, e = -1;
     if (i < end) {
-      const bool skipped = p.skip && p.skip[i];
-      const int64_t ev = p.idx[i];
-      if (ev < 0 || ev >= p.E) {
-        if (p.status) atomicExch(p.status, kDevBadIndex);
-      } else if (!skipped && ev >= p.e_lo && ev < p.e_hi) {
-        e = (int)ev;
-        const int lv = p.level ? p.level[i] : 0;
-        key = e * p.P + slot_of(lv, p.P);
-      }
+      key = key_s[i - base];
+      e = e_s[i - base];
     }
     const uint32_t lt = (1u << lane) - 1u;
     const uint32_t mk = __match_any_sync(0xffffffffu, key);
@@ -329,8 +367,8 @@ __device__ int32_t block_exclusive_scan(int32_t (&v)[PER], int32_t* sh_warp) {
   return total;
 }
 
-// D2: one block of 1024 threads. Turns per-block counts into per-(block, key) bases, writes the
-// per-key counts, and builds the work items.
+// D2: one block of 1024 threads. Turns per-block counts into per-(block, key) prefixes, writes the
+// per-key counts and first positions, and builds the work items.
 __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
   __shared__ int32_t sh_warp[32];
   const int keys = p.E * p.P;
@@ -338,26 +376,38 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
   if (tid == 0 && p.miss) *p.miss = 0;
   __syncthreads();
   constexpr int PER = kMaxKeys / 1024;
-  // per key: running prefix over blocks; totals
+  // per key: exclusive prefix over the dispatch blocks (8 independent loads in flight), totals
   int32_t tot_k[PER], tot_e[PER], nit[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int key = tid * PER + i;
     int32_t run = 0;
     if (key < keys)
-      for (int b = 0; b < p.nblk; ++b) {
-        const int32_t c = p.blk_k[(int64_t)b * keys + key];
-        p.blk_k[(int64_t)b * keys + key] = run;
-        run += c;
+      for (int b0 = 0; b0 < p.nblk; b0 += 8) {
+        int32_t cv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_k[(int64_t)(b0 + u) * keys + key] : 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (b0 + u < p.nblk) {
+            p.blk_k[(int64_t)(b0 + u) * keys + key] = run;
+            run += cv[u];
+          }
       }
     tot_k[i] = key < keys ? run : 0;
     int32_t rune = 0;
     const int e = tid * PER + i;
     if (e < p.E)
-      for (int b = 0; b < p.nblk; ++b) {
-        const int32_t c = p.blk_e[(int64_t)b * p.E + e];
-        p.blk_e[(int64_t)b * p.E + e] = rune;
-        rune += c;
+      for (int b0 = 0; b0 < p.nblk; b0 += 8) {
+        int32_t cv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_e[(int64_t)(b0 + u) * p.E + e] : 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (b0 + u < p.nblk) {
+            p.blk_e[(int64_t)(b0 + u) * p.E + e] = rune;
+            rune += cv[u];
+          }
       }
     tot_e[i] = e < p.E ? rune : 0;
     // work items: only for keys whose expert record is resident
@@ -386,7 +436,6 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
     if (key < keys) {
       p.counts_k[key] = tot_k[i];
       p.offs_k[key] = off_k[i];
-      for (int b = 0; b < p.nblk; ++b) p.blk_k[(int64_t)b * keys + key] += off_k[i];
       if (nit[i] > 0) {
         const int ex = key / p.P, sl = key % p.P;
         const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
@@ -408,7 +457,7 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
     const int e = tid * PER + i;
     if (e < p.E) {
       p.counts_e[e] = tot_e[i];
-      for (int b = 0; b < p.nblk; ++b) p.blk_e[(int64_t)b * p.E + e] += off_e[i];
+      p.offs_e[e] = off_e[i];
     }
   }
   if (tid == 0) {
@@ -428,8 +477,8 @@ __global__ void dispatch_scatter_kernel(DispatchParams p) {
   const int e = (int)p.idx[i];
   const int lv = p.level ? p.level[i] : 0;
   const int key = e * p.P + slot_of(lv, p.P);
-  p.pos_k[p.blk_k[(int64_t)b * p.E * p.P + key] + rk] = i;
-  p.pos_e[p.blk_e[(int64_t)b * p.E + e] + p.rank_e[i]] = i;
+  p.pos_k[p.offs_k[key] + p.blk_k[(int64_t)b * p.E * p.P + key] + rk] = i;
+  p.pos_e[p.offs_e[e] + p.blk_e[(int64_t)b * p.E + e] + p.rank_e[i]] = i;
 }
 
 }  // namespace
@@ -439,14 +488,25 @@ cudaError_t launch_router(const void* h, const void* wr, const float* bias, int 
                           uint8_t* level, uint8_t* skip, cudaStream_t s) {
   const int tpb = T <= 8 ? T : 8;
   dim3 grid((E + 7) / 8, (T + tpb - 1) / tpb);
-  if (act_type == MOEB200_F16)
-    router_logits_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(h), static_cast<const __half*>(wr),
-                                                      T, H, E, tpb, logits);
-  else if (act_type == MOEB200_BF16)
-    router_logits_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h),
-                                                             static_cast<const __nv_bfloat16*>(wr), T, H, E, tpb,
-                                                             logits);
-  else
+  // few (token, expert) logits: one expert x 8 tokens per warp (8 experts per block) keeps every SM
+  // busy; many: 4 x 8 per warp (8 x 32 per block) cuts the L2 re-reads of token and router rows
+  const bool big = (int64_t)T * E >= 65536;
+  const dim3 g16 = big ? dim3((E + 7) / 8, (T + 31) / 32) : dim3((E + 7) / 8, (T + 7) / 8);
+  if (act_type == MOEB200_F16) {
+    if (big)
+      router_logits_kernel<__half, 4, 8, 2><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
+                                                                static_cast<const __half*>(wr), T, H, E, logits);
+    else
+      router_logits_kernel<__half, 1, 8, 8><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
+                                                                static_cast<const __half*>(wr), T, H, E, logits);
+  } else if (act_type == MOEB200_BF16) {
+    if (big)
+      router_logits_kernel<__nv_bfloat16, 4, 8, 2><<<g16, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
+    else
+      router_logits_kernel<__nv_bfloat16, 1, 8, 8><<<g16, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
+  } else
     router_logits_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(h), static_cast<const float*>(wr), T, H,
                                                   E, tpb, logits);
   cudaError_t e = cudaGetLastError();
@@ -466,7 +526,7 @@ cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, ui
 
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
   const int keys = p.E * p.P;
-  const size_t sh = (size_t)(keys + p.E) * sizeof(int32_t);
+  const size_t sh = (size_t)(keys + p.E + 2 * kDispBlock) * sizeof(int32_t);
   dispatch_count_kernel<<<p.nblk, 32, sh, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

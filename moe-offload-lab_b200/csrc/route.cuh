@@ -32,7 +32,8 @@ struct DispatchParams {
   int32_t* counts_e;      // [E]
   int32_t* pos_e;         // [T*k]
   int32_t* counts_k;      // [E*P]
-  int32_t* offs_k;        // [E*P]
+  int32_t* offs_k;        // [E*P] first sorted position of each key
+  int32_t* offs_e;        // [E]   first sorted position of each expert (scratch)
   int32_t* pos_k;         // [T*k]
   int32_t* n_kept;        // [1] or null
   // scratch

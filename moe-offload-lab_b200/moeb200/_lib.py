@@ -47,6 +47,7 @@ _SIGS = {
     "moeb200_router": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                  _P, _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
     "moeb200_set_path": (C.c_int, [C.c_int32]),
+    "moeb200_set_item_tokens": (C.c_int, [C.c_int32]),
     "moeb200_router_workspace": (C.c_size_t, [C.c_int32, C.c_int32]),
     "moeb200_levels": (C.c_int, [_P, C.c_int32, C.c_int32, C.POINTER(Policy), _P, _P, _P]),
     "moeb200_dispatch": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, _P,
@@ -65,6 +66,9 @@ _SIGS = {
     "moeb200_ep_row_bytes": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32]),
     "moeb200_ep_pack": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
     "moeb200_ep_unpack": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, _P, _P]),
+    "moeb200_shared_expert": (C.c_int, [C.POINTER(Layout), _P, _P, _P, C.c_int32, C.c_int32, _P, C.c_int32, _P,
+                                        C.c_size_t, _P]),
+    "moeb200_shared_expert_workspace": (C.c_size_t, [C.POINTER(Layout), C.c_int32]),
     "moeb200_check_workspace": (C.c_int, [_P, C.POINTER(C.c_int32), _P]),
 }
 

@@ -250,9 +250,33 @@ def ep_unpack(rows: torch.Tensor, H: int, k: int, dtype: torch.dtype, x: torch.T
                                             _ptr(level), _ptr(skip), _stream(rows.device)))
 
 
+def shared_expert(layout_c: _lib.Layout, record: torch.Tensor, wg: torch.Tensor, x: torch.Tensor,
+                  out: torch.Tensor | None = None, add: bool = False, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """out (+)= sigmoid(x . wg) * SwiGLU_shared(x) (Qwen3-Next shared expert; one record)."""
+    _need_cuda(record, wg, x, out)
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty_like(x)
+        add = False
+    L = _lib.lib()
+    nbytes = L.moeb200_shared_expert_workspace(C.byref(layout_c), T)
+    if ws is None:
+        ws = workspace(nbytes, x.device, slot=4)
+    elif ws.numel() < nbytes:
+        raise ValueError("workspace too small")
+    _lib.check(L.moeb200_shared_expert(C.byref(layout_c), _ptr(record), _ptr(wg), _ptr(x), _act(x.dtype), T, _ptr(out),
+                                       int(add), _ptr(ws), ws.numel(), _stream(x.device)))
+    return out
+
+
 def set_path(path: str) -> None:
     """Expert-product path for this thread's next experts_forward calls: "auto", "gemv" or "gemm"."""
     _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2}[path]))
+
+
+def set_item_tokens(nt: int) -> None:
+    """Pairs per grouped-GEMV work item for this thread's next experts_forward calls (0 = auto, 8, 16)."""
+    _lib.check(_lib.lib().moeb200_set_item_tokens(nt))
 
 
 def check_workspace(ws: torch.Tensor) -> int:

@@ -427,6 +427,17 @@ def expert_ffn_f32(x: np.ndarray, gate_up: np.ndarray, down: np.ndarray) -> np.n
     return (silu(g_u[:, :I]) * g_u[:, I:]) @ down.T.astype(np.float32)
 
 
+def shared_expert(x: np.ndarray, wg: np.ndarray, record: np.ndarray, layout: dict, dtype: str) -> np.ndarray:
+    """Qwen3-Next shared-expert branch in float32: sigmoid(x . wg) * down(silu(gate x) * up x)
+    (transformers qwen3_next/modeling_qwen3_next.py:789-801). The gate logit is rounded to the
+    model dtype as F.linear returns it; the shared MLP is one record (gate_up = [gate_proj; up_proj])."""
+    xf = np.asarray(x, np.float32)
+    g = _round_f64_to(xf.astype(np.float64) @ np.asarray(wg, np.float64), dtype)
+    s = (np.float32(1) / (np.float32(1) + np.exp(-g.astype(np.float32)))).astype(np.float32)
+    gu, dn = materialize_f32(layout, record)
+    return s[:, None] * expert_ffn_f32(xf, gu, dn)
+
+
 def grouped_ffn(x_row: np.ndarray, records: list, layout: dict, weights: list) -> np.ndarray:
     """sum_e w_e * expert_e(x) for one token, fp32 (the reference kernels' contract,
     moelab/kernels.py:834-872; reference test helper tests/test_kernels.py:23-29)."""
