@@ -45,6 +45,18 @@ CFG0 = dict(name="c0", layers=1, H=2048, I=1024, E=64, k=8, renorm=False, precs=
             policy=dict(mode="lo"), act="fp16", bias=False, T=1)
 CFG2 = dict(name="c2", layers=1, H=2048, I=768, E=128, k=8, renorm=True, precs=["int4"],
             policy=dict(mode="lo"), act="bf16", bias=True, T=2048)
+# config 3: Qwen3-Next-shaped layers, one protected (int8) and one int4, each with the sigmoid-gated
+# shared expert (same precision as its layer); decode T=1 and prefill T=4096
+CFG3 = dict(name="c3", layers=2, H=2048, I=512, E=512, k=10, renorm=True, precs=["int8", "int4"],
+            layer_precs=[["int8"], ["int4"]], policy=dict(mode="lo", protect_layers=frozenset({0})), act="bf16",
+            bias=False, shared=True, T=1)
+CFG3P = dict(CFG3, name="c3p", T=4096)
+# config 4: batched decode on the Qwen3-Next layer shape, Zipf(1.1) expert popularity as a router
+# bias, fp16/int4 by router prob >= 0.05, 40 % of the experts (seeded choice) held in pinned host
+# memory and uploaded every step on a copy stream (no record stays cached across steps)
+CFG4 = dict(name="c4", layers=1, H=2048, I=512, E=512, k=10, renorm=True, precs=["fp16", "int4"],
+            policy=dict(mode="threshold", thr=0.05), act="bf16", bias="zipf", T=256, cold_frac=0.4)
+CONFIGS = {"c0": CFG0, "c1": CFG1, "c2": CFG2, "c3": CFG3, "c3p": CFG3P, "c4": CFG4}
 
 
 def parse():
@@ -57,11 +69,12 @@ def parse():
     ap.add_argument("--sweep", default="1,8,32", help="extra batch sizes reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
-    ap.add_argument("--config", default="c1", choices=["c0", "c1", "c2"], help="workload of --ncu mode")
+    ap.add_argument("--config", default="c1", choices=["c0", "c1", "c2", "c3", "c3p", "c4"],
+                    help="workload of --ncu mode")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
-    ap.add_argument("--extra", default="c0,c2", help="single-layer configs measured beside the headline")
+    ap.add_argument("--extra", default="c0,c2,c3,c3p,c4", help="single-layer configs measured beside the headline")
     return ap.parse_args()
 
 
@@ -178,16 +191,29 @@ class Stack:
         self.e_lo, self.e_hi = (self.ep.e_lo, self.ep.e_hi) if self.ep else (0, E)
         g = torch.Generator(device=dev).manual_seed(seed)
         self.wr = []
-        self.bias = (torch.randn(E, generator=g, device=dev) if cfg.get("bias") else None)
+        if cfg.get("bias") == "zipf":  # log(rank^-1.1) over a seeded permutation of the experts
+            perm = torch.randperm(E, generator=g, device=dev)
+            self.bias = torch.empty(E, device=dev)
+            self.bias[perm] = -1.1 * torch.log(torch.arange(1, E + 1, device=dev, dtype=torch.float32))
+        else:
+            self.bias = (torch.randn(E, generator=g, device=dev) if cfg.get("bias") else None)
+        self.shared = []  # per layer (record, layout, wg) of the shared expert, if the config has one
         for li in range(L):
             self.wr.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(self.act))
+            lprecs = cfg["layer_precs"][li] if cfg.get("layer_precs") else cfg["precs"]
             for e in range(E):
                 gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
                 dn = torch.randn(H, I, generator=g, device=dev) * 0.02
                 if not self.e_lo <= e < self.e_hi:
                     continue
-                for p in cfg["precs"]:
+                for p in lprecs:
                     self.rt.add_record(li, e, p, F.encode_record(self.lays[p], gu, dn))
+            if cfg.get("shared"):
+                gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
+                dn = torch.randn(H, I, generator=g, device=dev) * 0.02
+                wg = (torch.randn(H, generator=g, device=dev) * 0.02).to(self.act)
+                lay = self.lays[lprecs[0]]
+                self.shared.append((F.encode_record(lay, gu, dn), lay, F.to_c(lay), wg))
         self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"], self.bias) for w in self.wr]
         if self.ep:
             from moeb200.ep import B200EPExperts
@@ -213,6 +239,7 @@ class Stack:
         miss = self.rt.miss
 
         ep = self.ep
+        shared = self.shared
 
         def step():
             for li in range(L):
@@ -224,13 +251,17 @@ class Stack:
                 else:
                     ops.experts_forward(tables[li], x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li],
                                         miss=miss)
+                if shared:
+                    rec, _, lay_c, wg = shared[li]
+                    ops.shared_expert(lay_c, rec, wg, x, out=self.outs[li], add=True)
                 torch.add(x, self.outs[li], out=self.xs[li + 1])
         return step
 
     def launches_per_step(self) -> int:
         # per layer: router logits, router top-k (+ levels), dispatch (count, scan, scatter),
         # gate/up GEMV, down GEMV, finalize; expert parallel: + pack, unpack, combine, no finalize
-        return self.cfg["layers"] * (10 if self.ep else 8)
+        # shared expert: gate kernel, gate/up, down, finalize
+        return self.cfg["layers"] * ((10 if self.ep else 8) + (4 if self.shared else 0))
 
     def gathered_routing(self, li: int):
         """idx, level, skip of every rank's tokens for layer li (numpy), outside any timed region."""
@@ -295,7 +326,13 @@ class Stack:
                 out["up"] += gu_bytes[p]
                 out["down"] += dn_bytes[p]
             out["records"] += len(used)
-        n_pairs = out["pairs"]
+        for rec, lay, _, _ in self.shared:
+            p = lay["precision"]
+            out["up"] += gu_bytes[p]
+            out["down"] += dn_bytes[p]
+            out["records"] += 1
+            out["shared_pairs"] = out.get("shared_pairs", 0) + T
+        n_pairs = out["pairs"] + out.get("shared_pairs", 0)
         out["up_total"] = out["up"] + cfg["layers"] * T * H * 2 + n_pairs * I * 2
         out["down_total"] = out["down"] + n_pairs * I * 2 + cfg["layers"] * T * H * 4
         return out
@@ -331,7 +368,7 @@ def time_graph(step, K: int, W: int, world: int):
 
 
 def phase_times(step, reps: int = 5):
-    """Average duration (ms) of the gate/up and down expert kernels over the step, from CUDA events
+    """Summed duration (ms) per step of the gate/up and of the down expert kernels, from CUDA events
     that libmoeb200 records on the launching stream around its phases (eager replay of the step)."""
     import ctypes as C
 
@@ -345,7 +382,7 @@ def phase_times(step, reps: int = 5):
         step()
     up, dn, n = C.c_float(), C.c_float(), C.c_int32()
     _lib.check(lib.moeb200_trace_end(C.byref(up), C.byref(dn), C.byref(n)))
-    return up.value / max(n.value, 1), dn.value / max(n.value, 1)
+    return up.value / reps, dn.value / reps
 
 
 def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: dict) -> dict:
@@ -353,6 +390,7 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
     its expert kernels: HBM bytes for decode, tensor flops for prefill (tcgen05 path)."""
     stack = Stack(cfg, dev, seed=1)
     T = cfg["T"]
+    L = cfg["layers"]
     step = stack.make_device_step(T)
     stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
     g, ms = time_graph(step, steps, warmup, world)
@@ -360,27 +398,97 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
     ms = max_over_ranks(ms, world)
     rb = stack.routing_bytes()
     up_ms, dn_ms = phase_times(step)
-    pairs = rb["pairs"]
-    out = {"workload": cfg["name"], "T": T, "tokens_per_s": T * world / (ms / 1e3), "ms_per_layer": ms,
-           "experts_ms": up_ms + dn_ms, "records": rb["records"], "pairs": pairs}
+    pairs = rb["pairs"] + rb.get("shared_pairs", 0)
+    out = {"workload": cfg["name"], "T": T, "layers": L, "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": ms,
+           "ms_per_layer": ms / L, "experts_ms": up_ms + dn_ms, "records": rb["records"], "pairs": pairs,
+           "layer_precisions": [lp[0] for lp in cfg["layer_precs"]] if cfg.get("layer_precs") else cfg["precs"],
+           "shared_expert": bool(cfg.get("shared"))}
     prefill = T * cfg["k"] >= 16 * cfg["E"]
     if prefill:
         flops = 6.0 * cfg["H"] * cfg["I"] * pairs
         tf = flops / ((up_ms + dn_ms) / 1e3) / 1e12
         peak = peaks.get("bf16_tflops", 1590.0)
         out["roofline"] = {"bound": "tensor", "kernel": "tcgen05 grouped GEMM (up + down)", "achieved": tf,
-                           "peak": peak, "unit": "TFLOP/s", "frac": tf / peak, "flops_per_layer": flops,
+                           "peak": peak, "unit": "TFLOP/s", "frac": tf / peak, "flops_per_step": flops,
                            "up_ms": up_ms, "down_ms": dn_ms}
     else:
         byts = rb["up_total"] + rb["down_total"]
         gbs = byts / ((up_ms + dn_ms) / 1e3) / 1e9
         peak = peaks.get("hbm_gbs", 6650.0)
         out["roofline"] = {"bound": "hbm", "kernel": "grouped GEMV (up + down)", "achieved": gbs, "peak": peak,
-                           "unit": "GB/s", "frac": gbs / peak, "bytes_per_layer": byts, "up_ms": up_ms,
+                           "unit": "GB/s", "frac": gbs / peak, "bytes_per_step": byts, "up_ms": up_ms,
                            "down_ms": dn_ms}
     del stack
     torch.cuda.empty_cache()
     return out
+
+
+def h2d_peak_gbs(dev, nbytes: int = 256 << 20) -> float:
+    """Pinned host -> device copy bandwidth of this box (one large cudaMemcpyAsync, best of 3)."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, nbytes / (a.elapsed_time(b) / 1e3) / 1e9)
+    return best
+
+
+def measure_cold(cfg: dict, dev, steps: int, warmup: int) -> dict:
+    """Config 4: every step routes T tokens, uploads the routed cold records from pinned host memory
+    on a copy stream while the resident pairs run, then runs the uploaded pairs. Eager steps (one
+    routing read-back per layer, as the reference), CUDA events around the steps."""
+    from moeb200 import ops
+    from moeb200.cold import ColdExperts
+
+    stack = Stack(cfg, dev, seed=2)
+    E, T, k = cfg["E"], cfg["T"], cfg["k"]
+    g = torch.Generator().manual_seed(4)
+    cold_set = sorted(torch.randperm(E, generator=g)[: int(round(cfg["cold_frac"] * E))].tolist())
+    cold = ColdExperts(stack.rt, {p: len(cold_set) for p in cfg["precs"]})
+    for e in cold_set:
+        for p in cfg["precs"]:
+            cold.add_cold(0, e, p, stack.rt._records[(0, e, p)].cpu())
+    torch.cuda.empty_cache()
+    b = dict(w=torch.empty(T, k, device=dev), idx=torch.empty(T, k, dtype=torch.int64, device=dev),
+             level=torch.empty(T, k, dtype=torch.uint8, device=dev), skip=torch.empty(T, k, dtype=torch.uint8, device=dev))
+    x = torch.randn(T, cfg["H"], device=dev).to(stack.act)
+    out = torch.empty_like(x)
+    pol = stack.policy.to_c(0)
+
+    def step():
+        cold.reset()  # nothing stays cached: the cold records are uploaded again every step
+        ops.router(x, stack.wr[0], k, cfg["renorm"], stack.bias, pol, want_probs=False, out=b)
+        cold.run_layer(0, x, b["idx"], b["w"], b["level"], b["skip"], out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    up0, by0 = cold.uploads, cold.uploaded_bytes
+    a, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    e_.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(e_) / steps
+    ups = (cold.uploads - up0) / steps
+    byts = (cold.uploaded_bytes - by0) / steps
+    peak = h2d_peak_gbs(dev)
+    gbs = byts / (ms / 1e3) / 1e9
+    res = {"workload": "c4", "T": T, "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "cold_experts": len(cold_set),
+           "uploads_per_step": ups, "upload_bytes_per_step": byts, "miss": int(stack.rt.miss.item()),
+           "roofline": {"bound": "h2d", "kernel": "cold-record uploads (cudaMemcpyAsync on a copy stream)",
+                        "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                        "peak_kind": "measured pinned H2D copy, 256 MiB"},
+           "timing": "eager steps (routing read back per layer), CUDA events"}
+    del stack, cold
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---- CPU baseline (oracle restatement of the reference's CPU expert path) ---------------------------------------
@@ -466,7 +574,7 @@ def main():
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
     dev = torch.device("cuda", local)
-    cfg = dict({"c0": CFG0, "c1": CFG1, "c2": CFG2}[args.config] if args.ncu else CFG1)
+    cfg = dict(CONFIGS[args.config] if args.ncu else CFG1)
     if args.layers:
         cfg["layers"] = args.layers
     from moeb200 import ops as _ops
@@ -505,6 +613,7 @@ def main():
     # roofline of the dominant kernel (gate/up GEMV) from CUDA events on its stream
     try:
         up_ms, dn_ms = phase_times(step)
+        up_ms, dn_ms = up_ms / cfg["layers"], dn_ms / cfg["layers"]  # one call per layer
     except Exception as exc:  # the measurement hook failed: report no roofline rather than guess
         print(f"phase timing unavailable: {exc}", file=sys.stderr)
         up_ms = dn_ms = float("nan")
@@ -558,8 +667,11 @@ def main():
 
     extra = {}
     for name in [c for c in args.extra.split(",") if c and world == 1]:
-        cfgx = {"c0": CFG0, "c2": CFG2}[name]
-        extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks)
+        cfgx = CONFIGS[name]
+        if cfgx.get("cold_frac"):
+            extra[name] = measure_cold(cfgx, dev, max(5, args.steps // 2), 3)
+        else:
+            extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks)
 
     if rank == 0:
         line = {

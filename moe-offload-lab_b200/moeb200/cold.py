@@ -1,0 +1,173 @@
+"""Cold experts: records held in pinned host memory and uploaded to device slots when routed.
+
+Mirrors moelab's VRAM-miss path for resident-or-host experts: `_to_fast` copies a pinned record
+to the device on a dedicated copy stream and records an event, `_ready` makes the compute stream
+wait on it before use (moelab/runtime.py:310-333), and the host pool lends pinned slots and only
+reuses a slot after the event of its last use (moelab/hostpool.py:52-196).
+
+Per layer, `ColdExperts.run_layer`:
+  1. reads the routing back once (the reference reads it back too, moelab/runtime.py:505) and
+     lists the (expert, precision) records that are routed but only held on the host;
+  2. assigns each one a device slot (least recently used first, never a slot that this layer needs)
+     and issues one cudaMemcpyAsync per record on the copy stream; a reused slot's copy first waits
+     on the event that ended its previous use; one event marks the end of the uploads;
+  3. runs the resident (hot) pairs on the compute stream while the copies are in flight, then waits
+     on the upload event and runs the uploaded (cold) pairs; both passes write fp32 partial sums
+     that are added in a fixed order and cast once (moeb200_combine_parts).
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import torch
+
+from . import ops
+
+
+class SlotPlan:
+    """Slot bookkeeping of one precision (host logic only, no CUDA): a key is
+    (layer, expert, precision); slots are reused least recently used first."""
+
+    def __init__(self, n_slots: int):
+        if n_slots <= 0:
+            raise ValueError("at least one slot")
+        self.n_slots = n_slots
+        self.key_of: list[tuple | None] = [None] * n_slots
+        self.slot_of: dict[tuple, int] = {}
+        self.lru: OrderedDict[int, None] = OrderedDict((i, None) for i in range(n_slots))  # oldest first
+
+    def assign(self, needed: list[tuple]) -> tuple[dict, list]:
+        """Slots for every key of `needed` (distinct keys). Returns (slot of each key, uploads) where
+        uploads lists (key, slot, evicted key or None) for keys that were not in a slot yet."""
+        need = list(dict.fromkeys(needed))
+        if len(need) > self.n_slots:
+            raise RuntimeError(f"{len(need)} cold records routed at once but only {self.n_slots} device slots")
+        res, uploads = {}, []
+        for key in need:
+            s = self.slot_of.get(key)
+            if s is not None:
+                res[key] = s
+                self.lru.move_to_end(s)
+        busy = set(res.values())
+        for key in need:
+            if key in res:
+                continue
+            s = next(i for i in self.lru if i not in busy)
+            old = self.key_of[s]
+            if old is not None:
+                del self.slot_of[old]
+            self.key_of[s] = key
+            self.slot_of[key] = s
+            self.lru.move_to_end(s)
+            busy.add(s)
+            res[key] = s
+            uploads.append((key, s, old))
+        return res, uploads
+
+    def clear(self) -> list[tuple]:
+        """Forget every slot's content; returns the keys that were held."""
+        held = [k for k in self.key_of if k is not None]
+        self.key_of = [None] * self.n_slots
+        self.slot_of.clear()
+        return held
+
+
+class ColdExperts:
+    """Host-held records of a B200Runtime, uploaded into `slots[prec]` device slots on demand."""
+
+    def __init__(self, runtime, slots: dict[str, int]):
+        self.rt = runtime
+        self.dev = runtime.device
+        self.copy_stream = torch.cuda.Stream(self.dev)
+        self.host: dict[tuple, torch.Tensor] = {}
+        self.plans = {p: SlotPlan(n) for p, n in slots.items()}
+        self.buf = {}
+        for p, n in slots.items():
+            rb = runtime.layouts[p]["record_bytes"]  # a multiple of 4096: every slot stays aligned
+            self.buf[p] = torch.empty(n, rb, dtype=torch.uint8, device=self.dev)
+        self.last_use: dict[tuple[str, int], torch.cuda.Event] = {}
+        self.uploaded_bytes = 0
+        self.uploads = 0
+
+    def add_cold(self, layer: int, expert: int, prec: str, blob: torch.Tensor) -> None:
+        """Register a record held on the host (pinned uint8 tensor; pinned here if it is not)."""
+        if blob.is_cuda or blob.dtype != torch.uint8:
+            raise ValueError("cold records are uint8 host tensors")
+        if blob.numel() != self.rt.layouts[prec]["record_bytes"]:
+            raise ValueError("record size does not match the precision's layout")
+        if prec not in self.plans:
+            raise ValueError(f"no device slots for precision {prec}")
+        self.host[(layer, expert, prec)] = blob if blob.is_pinned() else blob.pin_memory()
+        self.rt.remove_record(layer, expert, prec)
+
+    def reset(self) -> None:
+        """Drop every uploaded record (their table entries go back to not resident)."""
+        for p, plan in self.plans.items():
+            for (layer, e, prec) in plan.clear():
+                self.rt._table(layer)[self.rt.precisions.index(prec), e] = 0
+
+    @torch.no_grad()
+    def run_layer(self, layer: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, level: torch.Tensor | None,
+                  skip: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+        rt = self.rt
+        T, k = idx.shape
+        P = rt.n_prec
+        idx_h = idx.cpu()
+        lv_h = level.cpu() if level is not None else torch.zeros(T, k, dtype=torch.uint8)
+        sk_h = skip.cpu().bool() if skip is not None else torch.zeros(T, k, dtype=torch.bool)
+        from .runtime import level_to_slot
+
+        cold_pair = torch.zeros(T, k, dtype=torch.bool)
+        needed: dict[str, list] = {p: [] for p in self.plans}
+        for t in range(T):
+            for j in range(k):
+                if sk_h[t, j]:
+                    continue
+                prec = rt.precisions[level_to_slot(int(lv_h[t, j]), P)]
+                key = (layer, int(idx_h[t, j]), prec)
+                if key in self.host:
+                    cold_pair[t, j] = True
+                    needed[prec].append(key)
+        if not cold_pair.any():
+            return rt.run_layer(layer, x, idx, w, level=level, skip=skip, out=out)
+        table = rt._table(layer)
+        cur = torch.cuda.current_stream(self.dev)
+        self.copy_stream.wait_stream(cur)  # the routing and any earlier table writes come first
+        used = []
+        with torch.cuda.stream(self.copy_stream):
+            for prec, keys in needed.items():
+                if not keys:
+                    continue
+                slot_of, uploads = self.plans[prec].assign(keys)
+                used += [(prec, s) for s in slot_of.values()]
+                for key, s, old in uploads:
+                    ev = self.last_use.get((prec, s))
+                    if ev is not None:
+                        self.copy_stream.wait_event(ev)  # quarantine: the slot's last reader is done
+                    self.buf[prec][s].copy_(self.host[key], non_blocking=True)
+                    self.uploaded_bytes += self.host[key].numel()
+                    self.uploads += 1
+                    if old is not None:
+                        ol, oe, op = old
+                        rt._table(ol)[rt.precisions.index(op), oe] = 0
+                for (l_, e, p_), s in slot_of.items():
+                    table[rt.precisions.index(p_), e] = self.buf[p_][s].data_ptr()
+            done = torch.cuda.Event()
+            done.record(self.copy_stream)
+        mask = cold_pair.to(self.dev, non_blocking=True).to(torch.uint8)
+        base = skip if skip is not None else torch.zeros(T, k, dtype=torch.uint8, device=self.dev)
+        parts = torch.empty(2, T, x.shape[-1], dtype=torch.float32, device=self.dev)
+        ct = rt._ctables[layer]
+        # hot pairs run while the uploads are in flight (the cold pairs' table entries are written on
+        # the copy stream and only read after the compute stream has waited on `done`)
+        ops.experts_forward_part(ct, 0, rt.num_experts, x, idx, w, level, base | mask, part=parts[0], miss=rt.miss)
+        cur.wait_event(done)
+        ops.experts_forward_part(ct, 0, rt.num_experts, x, idx, w, level, base | (1 - mask), part=parts[1],
+                                 miss=rt.miss)
+        for prec, s in used:
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self.last_use[(prec, s)] = ev
+        ops.combine_parts(parts, out)
+        return out
