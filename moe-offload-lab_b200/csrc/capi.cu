@@ -28,21 +28,6 @@ thread_local bool g_tracing = false;
 thread_local std::vector<TraceRec> g_trace_pool;
 thread_local size_t g_trace_used = 0;
 
-cudaError_t trace_mark(int which, cudaStream_t s) {
-  if (!g_tracing) return cudaSuccess;
-  if (which == 0) {
-    if (g_trace_used == g_trace_pool.size()) {
-      TraceRec r{};
-      for (auto& e : r.ev) {
-        cudaError_t err = cudaEventCreate(&e);
-        if (err != cudaSuccess) return err;
-      }
-      g_trace_pool.push_back(r);
-    }
-    ++g_trace_used;
-  }
-  return cudaEventRecord(g_trace_pool[g_trace_used - 1].ev[which], s);
-}
 // Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM.
 thread_local int g_path = 0;
 thread_local int g_item_tokens = 0;  // GEMV work-item size: 0 = automatic, else 8 or 16
@@ -90,19 +75,6 @@ struct WsHeader {
 
 int act_bytes(int act) { return act == MOEB200_F32 ? 4 : 2; }
 
-int num_sms_cached() {
-  static std::mutex mu;
-  static int cache[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  std::lock_guard<std::mutex> lk(mu);
-  if (cache[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
-  }
-  return cache[dev];
-}
 
 bool is_int(int wt) { return wt == MOEB200_I4 || wt == MOEB200_I8; }
 
@@ -156,15 +128,6 @@ int check_shapes(int H, int I) {
 // pre-activation buffer is sized for kMaxSplitPairs pairs).
 constexpr int kMaxSplitPairs = 256;
 
-bool split_ok(const moeb200_layout* L, int nlay, bool up, int ks) {
-  if (ks == 1) return true;
-  for (int i = 0; i < nlay; ++i) {
-    const int K = up ? L[i].hidden : L[i].inter;
-    if (K < ks * kSplitCols / 2) return false;
-    if (is_int(L[i].wtype) && kSplitCols % (up ? L[i].gs_up : L[i].gs_dn)) return false;
-  }
-  return true;
-}
 
 struct ForwardWs {
   WsHeader* hdr;
@@ -173,6 +136,7 @@ struct ForwardWs {
   uint8_t* h;
   float* pre;
   int32_t* cnt;
+  uint8_t* tmaps;
   float* acc;
   float* logits;
   size_t bytes;
@@ -199,6 +163,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
   w.pre = c.take<float>((size_t)std::min(n, kMaxSplitPairs) * 2 * I);
   w.cnt = c.take<int32_t>((size_t)std::min(n, kMaxSplitPairs) * (I / 16));
+  w.tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
   return w;
@@ -228,40 +193,11 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
     if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
     return MOEB200_OK;
   }
-  const int sms = num_sms_cached();
   const int nb = nt > 8 ? 2 : 1;
-  // split K while the tiles would not give every resident warp two of them
-  const int64_t rb_up = gp.I / 16, rb_dn = gp.H / 32;
-  int ks_up = 1, ks_dn = 1;
-  const int64_t want = 2ll * sms * kGemvMaxWarps;
-  const bool can_split = max_items <= kMaxSplitPairs && n_pairs <= kMaxSplitPairs && gp.pre != nullptr;
-  while (can_split && ks_up < 4 && (int64_t)max_items * rb_up * ks_up < want && split_ok(lays, nlay, true, ks_up * 2))
-    ks_up *= 2;
-  while (ks_dn < 4 && (int64_t)max_items * rb_dn * ks_dn < want && split_ok(lays, nlay, false, ks_dn * 2)) ks_dn *= 2;
-  gp.ksplit_up = ks_up;
-  gp.ksplit_dn = ks_dn;
-  int rstride = 0;
-  for (int i = 0; i < nlay; ++i) rstride = std::max(rstride, gemv_row_stride(lays[i].wtype));
-  gp.stage_bytes = 32 * rstride;
-  int warps = kGemvMaxWarps;
-  while (warps > 1 && gemv_smem_bytes(gp.stage_bytes, warps) > 227 * 1024) --warps;
-  const int smem = gemv_smem_bytes(gp.stage_bytes, warps);
-  const bool split = ks_up > 1;
-  const int occ_up = std::max(1, gemv_occupancy(act, nb, true, split, smem, warps));
-  const int occ_dn = std::max(1, gemv_occupancy(act, nb, false, false, smem, warps));
-  const int64_t tiles_up = (int64_t)max_items * rb_up * ks_up;
-  const int64_t tiles_dn = (int64_t)max_items * rb_dn * ks_dn;
-  const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_up * sms, (tiles_up + warps - 1) / warps));
-  const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)occ_dn * sms, (tiles_dn + warps - 1) / warps));
-  if (split) {
-    CUDA_TRY(cudaMemsetAsync(gp.pre, 0, (size_t)n_pairs * 2 * gp.I * sizeof(float), s));
-    CUDA_TRY(cudaMemsetAsync(gp.tile_cnt, 0, (size_t)max_items * (gp.I / 16) * sizeof(int32_t), s));
-  }
-  CUDA_TRY(trace_mark(0, s));
-  CUDA_TRY(launch_gemv_up(gp, act, nb, grid_up, warps, s));
-  CUDA_TRY(trace_mark(1, s));
-  CUDA_TRY(launch_gemv_down(gp, act, nb, grid_dn, warps, s));
-  CUDA_TRY(trace_mark(2, s));
+  const cudaError_t e = launch_gemv_phases(gp, lays, nlay, act, nb, max_items, n_pairs, kMaxSplitPairs, s);
+  if (e == cudaErrorInvalidConfiguration)
+    return fail(MOEB200_ERR_UNSUPPORTED, "GEMV: the record layouts need more shared memory than a CTA has");
+  CUDA_TRY(e);
   if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
   return MOEB200_OK;
 }
@@ -348,6 +284,38 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const AT* __restrict__
 }  // namespace
 
 namespace moeb200 {
+// Phase mark of the measurement hooks (moeb200_trace_begin/end) on the stream, when tracing.
+cudaError_t trace_mark(int which, cudaStream_t s) {
+  if (!g_tracing) return cudaSuccess;
+  if (which == 0) {
+    if (g_trace_used == g_trace_pool.size()) {
+      TraceRec r{};
+      for (auto& e : r.ev) {
+        cudaError_t err = cudaEventCreate(&e);
+        if (err != cudaSuccess) return err;
+      }
+      g_trace_pool.push_back(r);
+    }
+    ++g_trace_used;
+  }
+  return cudaEventRecord(g_trace_pool[g_trace_used - 1].ev[which], s);
+}
+
+// SM count of the current device (cached per device).
+int num_sms_cached() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 // Records an error message for moeb200_last_error from other translation units of the library.
 int set_error(int code, const char* fmt, ...) {
   char buf[512];
@@ -514,6 +482,7 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<uint8_t>((size_t)n * layout->inter * 2);
   c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * layout->inter);
   c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (layout->inter / 16));
+  c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
   c.take<float>((size_t)layout->hidden);
   return c.off;
 }
@@ -539,6 +508,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
   float* pre = c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * I);
   int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (I / 16));
+  uint8_t* tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)H);
   table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
   CUDA_TRY(cudaGetLastError());
@@ -555,6 +525,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.h = hbuf;
   gp.pre = pre;
   gp.tile_cnt = cnt;
+  gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;
   gp.lay[0] = to_dev(*layout);
@@ -652,6 +623,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.h = fw.h;
   gp.pre = fw.pre;
   gp.tile_cnt = fw.cnt;
+  gp.tmap_ws = fw.tmaps;
   gp.acc = part ? part : fw.acc;
   gp.status = &fw.hdr->status;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
@@ -700,6 +672,7 @@ size_t moeb200_shared_expert_workspace(const moeb200_layout* layout, int32_t T) 
   c.take<uint8_t>((size_t)T * layout->inter * 2);
   c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * layout->inter);
   c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (layout->inter / 16));
+  c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
   c.take<float>((size_t)T * layout->hidden);
   return c.off;
 }
@@ -735,6 +708,7 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   uint8_t* hbuf = c.take<uint8_t>((size_t)T * I * 2);
   float* pre = c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * I);
   int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (I / 16));
+  uint8_t* tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)T * H);
   const LayoutOffs lo{layout->off_gu_q, is_int(layout->wtype) ? layout->off_gu_s : 0, layout->off_dn_q,
                       is_int(layout->wtype) ? layout->off_dn_s : 0};
@@ -761,6 +735,7 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   gp.h = hbuf;
   gp.pre = pre;
   gp.tile_cnt = cnt;
+  gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;
   gp.lay[0] = to_dev(*layout);

@@ -1,26 +1,34 @@
 // Grouped expert GEMV -- the decode path of the MoE layer on B200.
 //
 // Replaces the Triton grouped kernels of moelab (kernels.py `_grp4_up` 312-361, `_grp4_down`
-// 363-396, `_grp8_up/_grp8_down` 667-740, `_grpf_up/_grpf_down` 398-451) with one warp-level
-// pipeline per phase:
+// 363-396, `_grp8_up/_grp8_down` 667-740, `_grpf_up/_grpf_down` 398-451):
 //
 //   up   : h[j, r]  = silu(gate_r . x_tok(j)) * (up_r . x_tok(j))      for each pair j of an item
 //   down : acc[t, r] += w_j * (down_r . h[j])                           (fp32 reduction = combine)
 //
-// Work is split into warp tiles (item, 32 weight rows, K split): the up phase pairs 16 gate rows
-// with the 16 matching up rows so SwiGLU happens in registers; the down phase takes 32 consecutive
-// rows. Each warp streams its rows through its own ring of shared-memory stages filled by 1-D bulk
-// TMA copies (one 256-byte row segment per lane per stage; padded row strides keep the fragment
-// reads bank-conflict free), dequantises int4/int8 in registers straight into tensor-core A
-// fragments and multiplies them with the activations of up to 8*NB tokens on mma.sync m16n8k16
-// (fp32 accumulators, two independent accumulator sets per chunk so consecutive MMAs do not wait on
-// each other). The fp16 group scale multiplies the fp32 partial of each chunk (a chunk never
-// straddles a group), so weights are never rounded. The activation operand of the next chunk is
-// loaded while the current one is multiplied.
-//
-// Small batches split K across warps: the up phase then adds fp32 partial pre-activations into
-// pre[j, 0:2I] (gate | up); the warp whose split of a tile arrives last (a per-tile counter) forms
-// h = silu(gate) * up for the tile's 16 rows, so the down phase always reads h.
+// One persistent CTA per SM works through jobs = (work item, 256 weight rows, K split). Eight
+// consumer warps own 32 rows each (up: 16 gate rows and the matching 16 up rows, so SwiGLU happens
+// in registers); a producer warp streams the job's K range through a ring of shared-memory stages
+// with 1-D bulk TMA copies: a stage holds one 256-byte segment of each of the 256 rows (padded row
+// stride, conflict-free fragment reads) and the same columns of the item's token rows, and the
+// job's group scales go to a double-buffered scale area with cp.async. Consumers dequantise in
+// registers straight into mma.sync m16n8k16 A fragments and multiply them with up to 8*NB tokens:
+//   fp16 activations, int4/int8 records: the weight is dequantised together with its scale in
+//     fp16, w = fp16((q - 8) * s) (the exact (q - 8) times s, rounded once: the value moelab's
+//     materialize gives), and accumulated in fp32 across all groups;
+//   bf16 activations: (q - 8) is exact in bf16; the fp16 scale multiplies the fp32 partial of each
+//     group (bf16 cannot hold the scale exactly);
+//   float records: converted to the activation type when the types differ.
+// Small batches split K over jobs: the up phase then adds fp32 partial pre-activations into
+// pre[j, 0:2I] (gate | up) and the job whose split of a row block arrives last (a per-(item, row
+// block) counter) forms h = silu(gate) * up for its rows, so the down phase always reads h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include "gemv.cuh"
@@ -29,14 +37,17 @@ namespace moeb200 {
 
 namespace {
 
+// Tensor-map templates of a launch: for each precision slot, the weight field of the phase
+// (gate_up.q or down.q) as a 2-D uint8 tensor [rows][row bytes] read in 128-byte x R-row boxes with
+// 128-byte swizzle; the kernel swaps in each record's address (tensormap.replace) per job.
+struct alignas(64) TmaTemplates {
+  CUtensorMap m[4];
+};
+
 enum Kind : int32_t {
   kI4w2 = 0, kI4w1, kI8w4, kI8w2, kI8w1, kF16w4, kF16w2, kF16w1, kBF16w4, kBF16w2, kBF16w1, kF32w2, kF32w1,
   kBadKind
 };
-
-__device__ __forceinline__ int wbits_of(int wtype) {
-  return wtype == MOEB200_I4 ? 4 : wtype == MOEB200_I8 ? 8 : wtype == MOEB200_F32 ? 32 : 16;
-}
 
 __device__ __forceinline__ int kind_of(int wtype, int K, int gs) {
   switch (wtype) {
@@ -59,10 +70,9 @@ __device__ __forceinline__ int kind_of(int wtype, int K, int gs) {
   return kBadKind;
 }
 
-// ---- shared / global vector loads ----------------------------------------------------------------
+// ---- shared-memory helpers ---------------------------------------------------------------------------
 template <int NW>
-__device__ __forceinline__ void lds(const uint8_t* p, uint32_t (&w)[NW]) {
-  const uint32_t a = smem_u32(p);
+__device__ __forceinline__ void lds(uint32_t a, uint32_t (&w)[NW]) {
   if constexpr (NW == 1) {
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[0]) : "r"(a));
   } else if constexpr (NW == 2) {
@@ -76,49 +86,81 @@ __device__ __forceinline__ void lds(const uint8_t* p, uint32_t (&w)[NW]) {
   }
 }
 
+// Weight words of one row from the swizzled weight tile: bytes [o, o + 4*NW) of the row's 256-byte
+// step, given the swizzled offsets of the 16-byte pieces that hold them (so0: first piece, so1:
+// second piece when the access spans 32 bytes).
 template <int NW>
-__device__ __forceinline__ void ldg(const void* p, uint32_t (&w)[NW]) {
-  if constexpr (NW == 1) {
-    asm("ld.global.nc.u32 %0, [%1];" : "=r"(w[0]) : "l"(p));
-  } else if constexpr (NW == 2) {
-    asm("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+__device__ __forceinline__ void ldw(uint32_t row, uint32_t so0, uint32_t so1, uint32_t (&w)[NW]) {
+  if constexpr (NW <= 4) {
+    lds<NW>(row + so0, w);
   } else {
+    static_assert(NW == 8, "weight accesses span one or two 16-byte pieces");
+    uint32_t a[4], b[4];
+    lds<4>(row + so0, a);
+    lds<4>(row + so1, b);
 #pragma unroll
-    for (int i = 0; i < NW; i += 4)
-      asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(w[i]), "=r"(w[i + 1]), "=r"(w[i + 2]), "=r"(w[i + 3])
-                   : "l"(static_cast<const uint8_t*>(p) + 16 * (i / 4)));
+    for (int i = 0; i < 4; ++i) {
+      w[i] = a[i];
+      w[4 + i] = b[i];
+    }
   }
 }
 
-// ---- B operand (activations of the lane's token(s)): NW words = 2*NW values, natural order ---------
-template <typename AT, int NB>
-struct BSrc {
-  const AT* row[NB];  // null = token slot unused (zeros)
+// Offset of byte o (o < 256) of a row's step inside the weight tile: the two 128-byte halves are
+// separate TMA boxes 32 KB apart; inside a half, 16-byte piece c of row R sits at piece c ^ (R % 8)
+// (128-byte swizzle). Every row a lane touches has R % 8 == g.
+__device__ __forceinline__ uint32_t swz(uint32_t o, uint32_t g) {
+  return ((o >> 7) << 15) | ((((o >> 4) & 7u) ^ g) << 4) | (o & 15u);
+}
 
-  template <int NW>
-  __device__ __forceinline__ void load(int col, uint32_t (&xb)[NB][NW]) const {
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      if (row[nb] == nullptr) {
-#pragma unroll
-        for (int i = 0; i < NW; ++i) xb[nb][i] = 0u;
-      } else {
-        ldg<NW>(row[nb] + col, xb[nb]);
-      }
-    }
-  }
-};
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
 
-// Scales of the lane's four rows (row tile rt, row g / g+8), read straight from the record (the 2-byte
-// values of one row are contiguous, so consecutive chunks hit the same L1 sector).
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// The mbarrier receives one arrival once every cp.async issued so far by this thread has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Named barrier of the consumer warps only (the producer warp never takes part).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kGemvCons * 32) : "memory");
+}
+
+// ---- scales of the lane's four rows (row tile rt, row g / g+8) for one group -------------------------
 struct Scales {
-  const __half* p[2][2];
-  __device__ __forceinline__ void load(int gi, float (&s)[2][2]) const {
+  uint32_t row[2][2];  // shared address of each row's first scale in the job's scale area
+  __device__ __forceinline__ void f32(int gi, float (&s)[2][2]) const {
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) s[rt][hh] = __half2float(__ldg(p[rt][hh] + gi));
+      for (int hh = 0; hh < 2; ++hh)
+        s[rt][hh] = __half2float(__ushort_as_half((unsigned short)lds_u16(row[rt][hh] + 2 * gi)));
+  }
+  __device__ __forceinline__ void h2(int gi, uint32_t (&s)[2][2]) const {
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t v = lds_u16(row[rt][hh] + 2 * gi);
+        s[rt][hh] = v | (v << 16);
+      }
   }
 };
 
@@ -136,98 +178,165 @@ __device__ __forceinline__ void fold_scaled(float (&tot)[2][NB][4], const float 
     }
 }
 
-// ---- one 8*WPL-column (int4) / 4*WPL-column (int8, float) chunk per lane ----------------------------------
-// st: stage (32 rows, stride rs; rows 0..15 = row tile 0, 16..31 = row tile 1); c: column of the chunk
-// inside the stage; xb: the lane's activation words for the chunk; s: the rows' scales.
+// ---- one chunk per lane --------------------------------------------------------------------------------
+// wr[rt][hh]: shared address of the start of the lane's weight row g + 8*hh of row tile rt in the
+// weight tile; so0/so1: swizzled offsets of the lane's bytes of the chunk in those rows (ldw);
+// xb[nb]: the lane's activation words of the chunk (token g + 8*nb).
 
-template <typename AT, int NB, int WPL>
-__device__ __forceinline__ void chunk_int4(const uint8_t* st, int rs, int c, const uint32_t (&xb)[NB][4 * WPL],
-                                           const float (&s)[2][2], float (&tot)[2][NB][4], int g, int t) {
+// int4: chunk = 32*WPL columns, lane t holds columns [c + 8*WPL*t, +8*WPL) as WPL words per row.
+// SCALED (fp16 activations): weights dequantised with their scale, MMAs straight into tot.
+template <typename AT, int NB, int WPL, bool SCALED>
+__device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
+                                           const uint32_t (&xb)[NB][4 * WPL], const Scales& S, int gi,
+                                           float (&tot)[2][NB][4]) {
   uint32_t wa[2][2][WPL];
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) lds<WPL>(st + (rt * 16 + g + 8 * hh) * rs + c / 2 + 4 * WPL * t, wa[rt][hh]);
-  float d[2][NB][2][4];
+    for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
+  if constexpr (SCALED) {
+    uint32_t s2[2][2];
+    S.h2(gi, s2);
 #pragma unroll
-  for (int j = 0; j < WPL; ++j) {
-    uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
+    for (int j = 0; j < WPL; ++j) {
+      uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+      for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) Dq<AT>::int4x8(wa[rt][hh][j], p04[rt][hh], p15[rt][hh], p26[rt][hh], p37[rt][hh]);
+        for (int hh = 0; hh < 2; ++hh) {
+          Dq<__half>::int4x8(wa[rt][hh][j], p04[rt][hh], p15[rt][hh], p26[rt][hh], p37[rt][hh]);
+          p04[rt][hh] = hmul2(p04[rt][hh], s2[rt][hh]);
+          p15[rt][hh] = hmul2(p15[rt][hh], s2[rt][hh]);
+          p26[rt][hh] = hmul2(p26[rt][hh], s2[rt][hh]);
+          p37[rt][hh] = hmul2(p37[rt][hh], s2[rt][hh]);
+        }
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const uint32_t x0 = xb[nb][4 * j], x1 = xb[nb][4 * j + 1], x2 = xb[nb][4 * j + 2], x3 = xb[nb][4 * j + 3];
-      const uint32_t b00 = prmt(x0, x2, 0x5410), b01 = prmt(x0, x2, 0x7632);  // (c, c+4), (c+1, c+5)
-      const uint32_t b10 = prmt(x1, x3, 0x5410), b11 = prmt(x1, x3, 0x7632);  // (c+2, c+6), (c+3, c+7)
+      for (int nb = 0; nb < NB; ++nb) {
+        const uint32_t x0 = xb[nb][4 * j], x1 = xb[nb][4 * j + 1], x2 = xb[nb][4 * j + 2], x3 = xb[nb][4 * j + 3];
+        const uint32_t b00 = prmt(x0, x2, 0x5410), b01 = prmt(x0, x2, 0x7632);  // (c, c+4), (c+1, c+5)
+        const uint32_t b10 = prmt(x1, x3, 0x5410), b11 = prmt(x1, x3, 0x7632);  // (c+2, c+6), (c+3, c+7)
 #pragma unroll
-      for (int rt = 0; rt < 2; ++rt) {
-        const uint32_t a0[4] = {p04[rt][0], p04[rt][1], p15[rt][0], p15[rt][1]};
-        const uint32_t a1[4] = {p26[rt][0], p26[rt][1], p37[rt][0], p37[rt][1]};
-        if (j == 0) {
-          MmaOp<AT>::first(d[rt][nb][0], a0, b00, b01);
-          MmaOp<AT>::first(d[rt][nb][1], a1, b10, b11);
-        } else {
-          MmaOp<AT>::run(d[rt][nb][0], a0, b00, b01);
-          MmaOp<AT>::run(d[rt][nb][1], a1, b10, b11);
+        for (int rt = 0; rt < 2; ++rt) {
+          const uint32_t a0[4] = {p04[rt][0], p04[rt][1], p15[rt][0], p15[rt][1]};
+          const uint32_t a1[4] = {p26[rt][0], p26[rt][1], p37[rt][0], p37[rt][1]};
+          MmaOp<__half>::run(tot[rt][nb], a0, b00, b01);
+          MmaOp<__half>::run(tot[rt][nb], a1, b10, b11);
         }
       }
     }
+  } else {
+    float d[2][NB][2][4];
+#pragma unroll
+    for (int j = 0; j < WPL; ++j) {
+      uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
+#pragma unroll
+      for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          Dq<AT>::int4x8(wa[rt][hh][j], p04[rt][hh], p15[rt][hh], p26[rt][hh], p37[rt][hh]);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const uint32_t x0 = xb[nb][4 * j], x1 = xb[nb][4 * j + 1], x2 = xb[nb][4 * j + 2], x3 = xb[nb][4 * j + 3];
+        const uint32_t b00 = prmt(x0, x2, 0x5410), b01 = prmt(x0, x2, 0x7632);
+        const uint32_t b10 = prmt(x1, x3, 0x5410), b11 = prmt(x1, x3, 0x7632);
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt) {
+          const uint32_t a0[4] = {p04[rt][0], p04[rt][1], p15[rt][0], p15[rt][1]};
+          const uint32_t a1[4] = {p26[rt][0], p26[rt][1], p37[rt][0], p37[rt][1]};
+          if (j == 0) {
+            MmaOp<AT>::first(d[rt][nb][0], a0, b00, b01);
+            MmaOp<AT>::first(d[rt][nb][1], a1, b10, b11);
+          } else {
+            MmaOp<AT>::run(d[rt][nb][0], a0, b00, b01);
+            MmaOp<AT>::run(d[rt][nb][1], a1, b10, b11);
+          }
+        }
+      }
+    }
+    float s[2][2];
+    S.f32(gi, s);
+    fold_scaled<NB>(tot, d, s);
   }
-  fold_scaled<NB>(tot, d, s);
 }
 
-template <typename AT, int NB, int WPL>
-__device__ __forceinline__ void chunk_int8(const uint8_t* st, int rs, int c, const uint32_t (&xb)[NB][2 * WPL],
-                                           const float (&s)[2][2], float (&tot)[2][NB][4], int g, int t) {
+// int8: chunk = 16*WPL columns, lane t holds columns [c + 4*WPL*t, +4*WPL) as WPL words per row.
+template <typename AT, int NB, int WPL, bool SCALED>
+__device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
+                                           const uint32_t (&xb)[NB][2 * WPL], const Scales& S, int gi,
+                                           float (&tot)[2][NB][4]) {
   uint32_t wa[2][2][WPL];
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) lds<WPL>(st + (rt * 16 + g + 8 * hh) * rs + c + 4 * WPL * t, wa[rt][hh]);
-  float d[2][NB][2][4];
+    for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
+  if constexpr (SCALED) {
+    uint32_t s2[2][2];
+    S.h2(gi, s2);
 #pragma unroll
-  for (int m = 0; m < WPL; ++m) {
-    uint32_t p01[2][2], p23[2][2];
+    for (int m = 0; m < WPL; ++m) {
+      uint32_t p01[2][2], p23[2][2];
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+      for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) Dq<AT>::int8x4(wa[rt][hh][m], p01[rt][hh], p23[rt][hh]);
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int rt = 0; rt < 2; ++rt) {
-        const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
-        if (m < 2)
-          MmaOp<AT>::first(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
-        else
-          MmaOp<AT>::run(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
-      }
-  }
-  if (WPL == 1) {  // only the first accumulator set was written
-#pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+        for (int hh = 0; hh < 2; ++hh) {
+          Dq<__half>::int8x4(wa[rt][hh][m], p01[rt][hh], p23[rt][hh]);
+          p01[rt][hh] = hmul2(p01[rt][hh], s2[rt][hh]);
+          p23[rt][hh] = hmul2(p23[rt][hh], s2[rt][hh]);
+        }
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) d[rt][nb][1][i] = 0.f;
+        for (int rt = 0; rt < 2; ++rt) {
+          const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
+          MmaOp<__half>::run(tot[rt][nb], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
+        }
+    }
+  } else {
+    float d[2][NB][2][4];
+#pragma unroll
+    for (int m = 0; m < WPL; ++m) {
+      uint32_t p01[2][2], p23[2][2];
+#pragma unroll
+      for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) Dq<AT>::int8x4(wa[rt][hh][m], p01[rt][hh], p23[rt][hh]);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt) {
+          const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
+          if (m < 2)
+            MmaOp<AT>::first(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
+          else
+            MmaOp<AT>::run(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
+        }
+    }
+    if (WPL == 1) {  // only the first accumulator set was written
+#pragma unroll
+      for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d[rt][nb][1][i] = 0.f;
+    }
+    float s[2][2];
+    S.f32(gi, s);
+    fold_scaled<NB>(tot, d, s);
   }
-  fold_scaled<NB>(tot, d, s);
 }
 
 // Float records: WT is the stored element type; it is converted to the activation type when it
-// differs (the reference materialises records in the activation dtype).
+// differs (the reference materialises records in the activation dtype). Chunk = 16*WPL columns,
+// lane t holds columns [c + 4*WPL*t, +4*WPL).
 template <typename AT, typename WT, int NB, int WPL>
-__device__ __forceinline__ void chunk_float(const uint8_t* st, int rs, int c, const uint32_t (&xb)[NB][2 * WPL],
-                                            float (&tot)[2][NB][4], int g, int t) {
+__device__ __forceinline__ void chunk_float(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
+                                            const uint32_t (&xb)[NB][2 * WPL], float (&tot)[2][NB][4]) {
   constexpr int NWR = WPL * 4 * (int)sizeof(WT) / 4;  // weight words per row per lane per chunk
-  uint32_t wr[2][2][NWR];
+  uint32_t wv[2][2][NWR];
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
-      lds<NWR>(st + (rt * 16 + g + 8 * hh) * rs + (c + 4 * WPL * t) * (int)sizeof(WT), wr[rt][hh]);
+    for (int hh = 0; hh < 2; ++hh) ldw<NWR>(wr[rt][hh], so0, so1, wv[rt][hh]);
 #pragma unroll
   for (int m = 0; m < WPL; ++m) {
     uint32_t ap[2][2][2];  // [rt][hh][pair]
@@ -236,14 +345,14 @@ __device__ __forceinline__ void chunk_float(const uint8_t* st, int rs, int c, co
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         if constexpr (sizeof(WT) == 4) {
-          const float* f = reinterpret_cast<const float*>(wr[rt][hh]) + 4 * m;
+          const float* f = reinterpret_cast<const float*>(wv[rt][hh]) + 4 * m;
           ap[rt][hh][0] = Dq<AT>::pack_f32(f[0], f[1]);
           ap[rt][hh][1] = Dq<AT>::pack_f32(f[2], f[3]);
         } else if constexpr (std::is_same<WT, AT>::value) {
-          ap[rt][hh][0] = wr[rt][hh][2 * m];
-          ap[rt][hh][1] = wr[rt][hh][2 * m + 1];
+          ap[rt][hh][0] = wv[rt][hh][2 * m];
+          ap[rt][hh][1] = wv[rt][hh][2 * m + 1];
         } else {
-          const WT* v = reinterpret_cast<const WT*>(&wr[rt][hh][2 * m]);
+          const WT* v = reinterpret_cast<const WT*>(&wv[rt][hh][2 * m]);
           ap[rt][hh][0] = Dq<AT>::pack_f32(to_f32<WT>(v[0]), to_f32<WT>(v[1]));
           ap[rt][hh][1] = Dq<AT>::pack_f32(to_f32<WT>(v[2]), to_f32<WT>(v[3]));
         }
@@ -258,80 +367,88 @@ __device__ __forceinline__ void chunk_float(const uint8_t* st, int rs, int c, co
   }
 }
 
-// ---- one pipeline step: the chunks of a stage, activations and scales loaded one chunk ahead ---------
-// KIND selects the chunk routine; chunks alternate between two register sets so the next chunk's
-// loads are in flight while the current chunk is multiplied.
+// ---- one stage: its chunks, the lane's activation words read from the stage's token rows ----------
+// rowoff[rt][hh]: offset of the lane's row in the weight tile (row index * 128).
 template <typename AT, int NB, int KIND>
-__device__ __forceinline__ void run_step(const uint8_t* st, int col0, int ncols, const BSrc<AT, NB>& B,
-                                         const Scales& S, int gs, float (&tot)[2][NB][4], int g, int t) {
+__device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowoff)[2][2], uint32_t bbase,
+                                          int bstride, int ntok, int ncols, int col0, int gs, int g0,
+                                          const Scales& S, float (&tot)[2][NB][4], int g, int t) {
   constexpr bool I4 = KIND == kI4w2 || KIND == kI4w1;
   constexpr bool I8 = KIND == kI8w4 || KIND == kI8w2 || KIND == kI8w1;
   constexpr int WPL = (KIND == kI4w2 || KIND == kI8w2 || KIND == kF16w2 || KIND == kBF16w2 || KIND == kF32w2) ? 2
                       : (KIND == kI8w4 || KIND == kF16w4 || KIND == kBF16w4)                                   ? 4
                                                                                                                   : 1;
-  constexpr int CH = I4 ? 32 * WPL : 16 * WPL;     // columns per chunk
-  constexpr int NW = I4 ? 4 * WPL : 2 * WPL;       // activation words per lane per chunk
-  constexpr int LOFF = I4 ? 8 * WPL : 4 * WPL;     // lane column offset inside a chunk
+  constexpr int CH = I4 ? 32 * WPL : 16 * WPL;  // columns per chunk
+  constexpr int NW = I4 ? 4 * WPL : 2 * WPL;    // activation words per lane per chunk
+  constexpr int LOFF = I4 ? 8 * WPL : 4 * WPL;  // lane column offset inside a chunk
   constexpr int WT = KIND == kF32w2 || KIND == kF32w1 ? 2 : (KIND == kBF16w4 || KIND == kBF16w2 || KIND == kBF16w1) ? 1 : 0;
-  constexpr int WTYPE = I4 ? MOEB200_I4 : I8 ? MOEB200_I8 : WT == 2 ? MOEB200_F32 : WT == 1 ? MOEB200_BF16 : MOEB200_F16;
-  const int rs = gemv_row_stride(WTYPE);
+  constexpr int W2 = I4 ? 1 : I8 ? 2 : WT == 2 ? 8 : 4;  // weight bytes per column, times 2
+  constexpr bool SCALED = std::is_same<AT, __half>::value;
   const int nch = ncols / CH;
-  const int cpg = (I4 || I8) ? gs / CH : 1;
-  const int g0 = (I4 || I8) ? col0 / gs : 0;
-  auto chunk = [&](int ci, const uint32_t (&xv)[NB][NW], const float (&sv)[2][2]) {
-    const int c = ci * CH;
-    if constexpr (I4) {
-      chunk_int4<AT, NB, WPL>(st, rs, c, xv, sv, tot, g, t);
-    } else if constexpr (I8) {
-      chunk_int8<AT, NB, WPL>(st, rs, c, xv, sv, tot, g, t);
-    } else if constexpr (WT == 2) {
-      chunk_float<AT, float, NB, WPL>(st, rs, c, xv, tot, g, t);
-    } else if constexpr (WT == 1) {
-      chunk_float<AT, __nv_bfloat16, NB, WPL>(st, rs, c, xv, tot, g, t);
-    } else {
-      chunk_float<AT, __half, NB, WPL>(st, rs, c, xv, tot, g, t);
-    }
-  };
-  auto fetch = [&](int ci, uint32_t (&xv)[NB][NW], float (&sv)[2][2]) {
-    B.template load<NW>(col0 + ci * CH + LOFF * t, xv);
-    if constexpr (I4 || I8) S.load(g0 + (cpg == 1 ? ci : ci / cpg), sv);
-  };
-  uint32_t xa[NB][NW], xc[NB][NW];
-  float sa[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, sc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  fetch(0, xa, sa);
-  int ci = 0;
-  for (; ci + 1 < nch; ci += 2) {
-    fetch(ci + 1, xc, sc);
-    chunk(ci, xa, sa);
-    if (ci + 2 < nch) fetch(ci + 2, xa, sa);
-    chunk(ci + 1, xc, sc);
+  uint32_t wr[2][2];
+#pragma unroll
+  for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) wr[rt][hh] = wtile + rowoff[rt][hh];
+  uint32_t brow[NB];
+  bool bon[NB];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    bon[nb] = g + 8 * nb < ntok;
+    brow[nb] = bbase + (g + 8 * nb) * bstride + LOFF * t * 2;
   }
-  if (ci < nch) chunk(ci, xa, sa);
+  const uint32_t lo = LOFF * t * W2 / 2;  // the lane's first byte inside a chunk
+#pragma unroll 2
+  for (int ci = 0; ci < nch; ++ci) {
+    uint32_t xb[NB][NW];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      if (bon[nb]) {
+        lds<NW>(brow[nb] + ci * CH * 2, xb[nb]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < NW; ++i) xb[nb][i] = 0u;
+      }
+    }
+    const uint32_t o = ci * (CH * W2 / 2) + lo;
+    const uint32_t so0 = swz(o, g), so1 = swz(o + 16, g);
+    if constexpr (I4) {
+      chunk_int4<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, (col0 + ci * CH) / gs - g0, tot);
+    } else if constexpr (I8) {
+      chunk_int8<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, (col0 + ci * CH) / gs - g0, tot);
+    } else if constexpr (WT == 2) {
+      chunk_float<AT, float, NB, WPL>(wr, so0, so1, xb, tot);
+    } else if constexpr (WT == 1) {
+      chunk_float<AT, __nv_bfloat16, NB, WPL>(wr, so0, so1, xb, tot);
+    } else {
+      chunk_float<AT, __half, NB, WPL>(wr, so0, so1, xb, tot);
+    }
+  }
 }
 
-// ---- tile description ---------------------------------------------------------------------------------
-struct TileDesc {
-  const uint8_t* rowbase[2];  // first row of each 16-row tile
-  const uint8_t* sbase[2];    // first scale row of each 16-row tile (integer records)
-  int32_t rstride;            // bytes per weight row
-  int32_t sstride;            // bytes per scale row
-  int32_t wtype, kind, gs, wbits;
-  int32_t k_lo, k_hi;         // input columns of this K split
-  int32_t step_cols, nsteps;
-  int32_t item, r0;
-};
-
+// ---- jobs ----------------------------------------------------------------------------------------------
 // Input columns of one K split (a multiple of kSplitCols); splits past K are empty.
-__device__ __forceinline__ int split_cols(int K, int ks_n) {
+__host__ __device__ __forceinline__ int split_cols(int K, int ks_n) {
   return ks_n > 1 ? ((K / ks_n + kSplitCols - 1) / kSplitCols) * kSplitCols : K;
 }
 
+struct Job {
+  const uint8_t* q;  // weight field of the record (gate_up or down)
+  const uint8_t* s;  // scale field (integer records)
+  int32_t item, rb, start, ntok, slot;
+  int32_t kind, gs, wbits;
+  int32_t r0, nrow;          // up: first gate row and gate rows (up rows mirror them); down: rows
+  int32_t k_lo, k_hi;        // input columns of this K split
+  int32_t step_cols, nsteps;
+  int32_t rstride, sstride;  // bytes per weight row / scale row in the record
+  int32_t g0, ngr, sst;      // first group, groups of the split, scale-area row stride
+};
+
 template <bool UP>
-__device__ __forceinline__ void describe_tile(const GemvParams& p, int tile, int rb_per_item, int ks_n,
-                                              TileDesc& d) {
+__device__ __forceinline__ void describe_job(const GemvParams& p, int job, int rb_per_item, int ks_n, Job& d) {
   const int per_item = rb_per_item * ks_n;
-  const int item = tile / per_item;
-  const int rem = tile - item * per_item;
+  const int item = job / per_item;
+  const int rem = job - item * per_item;
   const int ks = rem / rb_per_item;
   const int rb = rem - ks * rb_per_item;
   const Item it = p.items[item];
@@ -339,8 +456,11 @@ __device__ __forceinline__ void describe_tile(const GemvParams& p, int tile, int
   const int K = UP ? p.H : p.I;
   const bool isint = L.wtype == MOEB200_I4 || L.wtype == MOEB200_I8;
   d.item = item;
-  d.wtype = L.wtype;
-  d.wbits = wbits_of(L.wtype);
+  d.rb = rb;
+  d.slot = it.slot;
+  d.start = it.start;
+  d.ntok = it.ntok;
+  d.wbits = gemv_wbits(L.wtype);
   d.gs = isint ? (UP ? L.gs_up : L.gs_dn) : 64;
   d.kind = kind_of(L.wtype, K, d.gs);
   d.rstride = K * d.wbits / 8;
@@ -350,39 +470,77 @@ __device__ __forceinline__ void describe_tile(const GemvParams& p, int tile, int
   d.k_lo = min(K, ks * kc);
   d.k_hi = min(K, d.k_lo + kc);
   d.nsteps = d.k_hi > d.k_lo ? (d.k_hi - d.k_lo + d.step_cols - 1) / d.step_cols : 0;
-  const uint8_t* q = reinterpret_cast<const uint8_t*>(UP ? it.p_guq : it.p_dnq);
-  const uint8_t* s = reinterpret_cast<const uint8_t*>(UP ? it.p_gus : it.p_dns);
-  int rA, rB;
+  d.q = reinterpret_cast<const uint8_t*>(UP ? it.p_guq : it.p_dnq);
+  d.s = reinterpret_cast<const uint8_t*>(UP ? it.p_gus : it.p_dns);
   if (UP) {
-    d.r0 = rb * 16;
-    rA = d.r0;
-    rB = p.I + d.r0;
+    d.r0 = rb * (kGemvJobRows / 2);
+    d.nrow = min(kGemvJobRows / 2, p.I - d.r0);
   } else {
-    d.r0 = rb * 32;
-    rA = d.r0;
-    rB = d.r0 + 16;
+    d.r0 = rb * kGemvJobRows;
+    d.nrow = min(kGemvJobRows, p.H - d.r0);
   }
-  d.rowbase[0] = q + (int64_t)rA * d.rstride;
-  d.rowbase[1] = q + (int64_t)rB * d.rstride;
-  d.sbase[0] = s + (int64_t)rA * d.sstride;
-  d.sbase[1] = s + (int64_t)rB * d.sstride;
+  d.g0 = isint ? d.k_lo / d.gs : 0;
+  d.ngr = isint ? (d.k_hi - d.k_lo + d.gs - 1) / d.gs : 0;
+  d.sst = isint ? gemv_s_stride(d.ngr) : 0;
 }
 
-// Issue the bulk copies of one step (all 32 lanes take part; lane 0 arms the barrier first).
-__device__ __forceinline__ void issue_step(const TileDesc& d, int step, uint8_t* stage, uint64_t* bar, int lane) {
-  const int col0 = d.k_lo + step * d.step_cols;
-  const int ncols = min(d.step_cols, d.k_hi - col0);
-  const uint32_t seg = (uint32_t)(ncols * d.wbits / 8);
-  if (lane == 0) mbar_arrive_expect_tx(bar, 32u * seg);
+// Record row of stage slot m (m < 256) of a job, or -1 if the slot is unused. Slots 32w..32w+31
+// belong to consumer warp w: up = 16 gate rows then the 16 matching up rows; down = 32 rows.
+template <bool UP>
+__device__ __forceinline__ int slot_row(const Job& d, int I, int m) {
+  const int w = m >> 5, i = m & 31;
+  if (UP) {
+    const int gr = 16 * w + (i & 15);
+    if (gr >= d.nrow) return -1;
+    return (i < 16 ? 0 : I) + d.r0 + gr;
+  }
+  const int r = 32 * w + i;
+  return r < d.nrow ? d.r0 + r : -1;
+}
+
+// Row of the job's scale area that holds record row `row` (up: gate rows first, up rows at 128).
+template <bool UP>
+__device__ __forceinline__ int scale_slot(const Job& d, int I, int row) {
+  if (UP) return row >= I ? kGemvJobRows / 2 + (row - I - d.r0) : row - d.r0;
+  return row - d.r0;
+}
+
+// ---- TMA with tensor maps ------------------------------------------------------------------------------
+__device__ __forceinline__ void tma2d(uint32_t dst, uint64_t tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// The producer warp points one of its CTA's four global tensor-map slots at a record: the template
+// is staged in shared memory, its global address replaced, and the result copied out with a
+// release fence for the tensor-map proxy; the issuing lane then acquires it before using it.
+__device__ __forceinline__ void retarget_tmap(const CUtensorMap& tmpl, uint32_t sdesc, uint64_t gdesc,
+                                              const void* base, int lane) {
+  const uint32_t v = reinterpret_cast<const uint32_t*>(&tmpl)[lane];
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(sdesc + 4 * lane), "r"(v) : "memory");
   __syncwarp();
-  const int rt = lane >> 4, row = lane & 15;
-  bulk_g2s(stage + lane * gemv_row_stride(d.wtype), d.rowbase[rt] + row * d.rstride + col0 * d.wbits / 8, seg, bar);
+  if (lane == 0)
+    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(sdesc),
+                 "l"(reinterpret_cast<uint64_t>(base))
+                 : "memory");
+  __syncwarp();
+  asm volatile("tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::
+                   "l"(gdesc),
+               "r"(sdesc)
+               : "memory");
+  if (lane == 0) asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(gdesc) : "memory");
+  __syncwarp();
 }
 
+// ---- the kernel -----------------------------------------------------------------------------------------
 template <typename AT, int NB, bool UP, bool SPLIT>
-__global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int nwarps = blockDim.x >> 5;
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p, const __grid_constant__ TmaTemplates tm) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned base: the 128-byte swizzle of the weight tiles repeats every 1024 bytes
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
@@ -392,170 +550,250 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
       p.acc[i] = 0.f;
   }
 
-  const int sb = p.stage_bytes;
-  uint8_t* stages = smem + warp * kGemvStages * sb;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * kGemvStages * sb) + warp * kGemvStages;
+  uint8_t* stages = smem;
+  uint8_t* sarea = smem + kGemvStages * p.stage_bytes;
+  uint8_t* sdesc = sarea + 2 * p.s_bytes;  // 128-byte tensor-map staging of the producer
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdesc + 128);
+  uint64_t* full = bars;        // [2] stage landed
+  uint64_t* empty = bars + 2;   // [2] stage consumed by every consumer warp
+  uint64_t* sfull = bars + 4;   // [2] scale area landed
+  uint64_t* sempty = bars + 6;  // [2] scale area released
+  int32_t* bcast = reinterpret_cast<int32_t*>(bars + 8);
 
-  const int n_items = *p.n_items;
-  const int rb_per_item = UP ? p.I / 16 : p.H / 32;
-  const int ks_n = UP ? p.ksplit_up : p.ksplit_dn;
-  const int n_tiles = n_items * rb_per_item * ks_n;
-  const int gw = blockIdx.x * nwarps + warp;
-  const int nw = gridDim.x * nwarps;
-  if (gw >= n_tiles) return;
-
-  // first tile of this warp with a non-empty K split (the producer and consumer walk the same list)
-  int first = gw;
-  TileDesc pd;
-  describe_tile<UP>(p, first, rb_per_item, ks_n, pd);
-  while (pd.nsteps == 0) {
-    first += nw;
-    if (first >= n_tiles) return;
-    describe_tile<UP>(p, first, rb_per_item, ks_n, pd);
-  }
-
-  if (lane == 0) {
-    for (int s = 0; s < kGemvStages; ++s) mbar_init(&bars[s], 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemvStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvCons);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sfull[s], 32);
+      mbar_init(&sempty[s], kGemvCons);
+    }
     fence_mbar_init();
   }
-  __syncwarp();
+  __syncthreads();
 
-  int ptile = first, pstep = 0;
-  auto produce = [&](int sidx) {
-    if (ptile >= n_tiles) return;
-    issue_step(pd, pstep, stages + sidx * sb, &bars[sidx], lane);
-    if (++pstep == pd.nsteps) {
-      pstep = 0;
-      do {
-        ptile += nw;
-        if (ptile < n_tiles) describe_tile<UP>(p, ptile, rb_per_item, ks_n, pd);
-      } while (ptile < n_tiles && pd.nsteps == 0);
-    }
-  };
-  TileDesc cd = pd;  // the consumer starts on the same first tile
-#pragma unroll
-  for (int s = 0; s < kGemvStages; ++s) produce(s);
+  const int n_items = *p.n_items;
+  const int rb_per_item = UP ? (p.I + kGemvJobRows / 2 - 1) / (kGemvJobRows / 2)
+                             : (p.H + kGemvJobRows - 1) / kGemvJobRows;
+  const int ks_n = UP ? p.ksplit_up : p.ksplit_dn;
+  const int n_jobs = n_items * rb_per_item * ks_n;
 
-  int ctile = first, cstep = 0;
-  float tot[2][NB][4];
-  BSrc<AT, NB> B;
-  Scales S;
-  Item cit;
-  auto begin_tile = [&]() {
-    cit = p.items[cd.item];
-#pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        S.p[rt][hh] = reinterpret_cast<const __half*>(cd.sbase[rt] + (int64_t)(g + 8 * hh) * cd.sstride);
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const int tk = g + 8 * nb;
-      if (tk < cit.ntok) {
-        const int j = cit.start + tk;
-        if (UP) {
-          const int tok = p.pos[j] / p.k;
-          B.row[nb] = static_cast<const AT*>(p.x) + (int64_t)tok * p.H;
-        } else {
-          B.row[nb] = static_cast<const AT*>(p.h) + (int64_t)j * p.I;
+  if (warp == kGemvCons) {
+    // ---------------- producer warp ----------------
+    uint32_t it = 0, sj = 0, jn = 0;
+    bool ok = true;
+    for (int job = blockIdx.x; job < n_jobs && ok; job += gridDim.x) {
+      Job d;
+      describe_job<UP>(p, job, rb_per_item, ks_n, d);
+      if (d.nsteps == 0) continue;
+      // tensor map of the job's weight field (a ring of four per CTA: the copies that used a slot
+      // four jobs ago have landed, the stage ring being two deep)
+      const uint64_t gdesc = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * 4 + (jn & 3)) * 128;
+      retarget_tmap(tm.m[d.slot], smem_u32(sdesc), gdesc, d.q, lane);
+      ++jn;
+      if (d.ngr > 0) {
+        // the job's scale area: every used row's groups [g0, g0 + ngr)
+        const int par = sj & 1;
+        if (sj >= 2) ok = mbar_wait(&sempty[par], ((sj >> 1) - 1) & 1, p.status);
+        if (!ok) break;
+        const uint32_t sa = smem_u32(sarea + par * p.s_bytes);
+        const int nb2 = d.ngr * 2;
+        for (int m = lane; m < kGemvJobRows; m += 32) {
+          const int row = slot_row<UP>(d, p.I, m);
+          if (row < 0) continue;
+          const uint8_t* src = d.s + (int64_t)row * d.sstride + 2 * d.g0;
+          const uint32_t dst = sa + scale_slot<UP>(d, p.I, row) * d.sst;
+          const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+          if ((a % 16) == 0 && nb2 % 16 == 0) {
+            for (int b = 0; b < nb2; b += 16) cp_async16(dst + b, src + b);
+          } else if ((a % 4) == 0 && nb2 % 4 == 0) {
+            for (int b = 0; b < nb2; b += 4) cp_async4(dst + b, src + b);
+          } else {  // odd group counts (small shapes): plain copies
+            for (int b = 0; b < nb2; b += 2) {
+              const uint16_t v = *reinterpret_cast<const uint16_t*>(src + b);
+              asm volatile("st.shared.u16 [%0], %1;" ::"r"(dst + b), "h"(v) : "memory");
+            }
+          }
         }
-      } else {
-        B.row[nb] = nullptr;
+        __threadfence_block();  // plain stores of this lane before its arrival
+        cp_async_arrive(&sfull[par]);
+        ++sj;
       }
+      for (int step = 0; step < d.nsteps; ++step, ++it) {
+        const int sidx = it % kGemvStages;
+        if (it >= kGemvStages) ok = mbar_wait(&empty[sidx], ((it / kGemvStages) - 1) & 1, p.status);
+        if (!ok) break;
+        const int col0 = d.k_lo + step * d.step_cols;
+        const int ncols = min(d.step_cols, d.k_hi - col0);
+        const uint32_t bseg = (uint32_t)(ncols * (int)sizeof(AT));
+        const uint32_t wst = smem_u32(stages + sidx * p.stage_bytes);
+        if (lane == 0) {
+          // the weight tile: whole boxes land (rows or bytes past the tensor read as zeros)
+          mbar_arrive_expect_tx(&full[sidx], kGemvWBytes + d.ntok * bseg);
+          const int xb = col0 * d.wbits / 8;  // first byte of the step in each row
+          if (UP) {
+            tma2d(wst, gdesc, xb, d.r0, &full[sidx]);                                   // gate rows -> R 0..127
+            tma2d(wst + kGemvWBytes / 2, gdesc, xb + 128, d.r0, &full[sidx]);
+            tma2d(wst + 128 * 128, gdesc, xb, p.I + d.r0, &full[sidx]);                 // up rows -> R 128..255
+            tma2d(wst + kGemvWBytes / 2 + 128 * 128, gdesc, xb + 128, p.I + d.r0, &full[sidx]);
+          } else {
+            tma2d(wst, gdesc, xb, d.r0, &full[sidx]);                                   // rows -> R 0..255
+            tma2d(wst + kGemvWBytes / 2, gdesc, xb + 128, d.r0, &full[sidx]);
+          }
+        }
+        __syncwarp();
+        if (lane < d.ntok) {
+          const int j = d.start + lane;
+          const AT* src = UP ? static_cast<const AT*>(p.x) + (int64_t)(p.pos[j] / p.k) * p.H
+                             : static_cast<const AT*>(p.h) + (int64_t)j * p.I;
+          bulk_g2s(stages + sidx * p.stage_bytes + kGemvWBytes + lane * p.b_stride, src + col0, bseg, &full[sidx]);
+        }
+      }
+    }
+    // the CTA must not exit with copies in flight: wait for the last stages issued (consumed
+    // already in the normal flow; after a failed wait they may still be landing)
+    for (uint32_t q = it > kGemvStages ? it - kGemvStages : 0; q < it; ++q)
+      mbar_wait(&full[q % kGemvStages], (q / kGemvStages) & 1, nullptr);
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  uint32_t it = 0, sj = 0;
+  bool failed = false;  // a bounded wait gave up (status word set): stop after the current job
+  const uint32_t st0 = smem_u32(stages);
+  const uint32_t sa0 = smem_u32(sarea);
+  // rows of this lane in the weight tile (R * 128): up = gate rows 16w.. and up rows 128 + 16w..;
+  // down = rows 32w..32w+31
+  uint32_t rowoff[2][2];
+#pragma unroll
+  for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int R = UP ? rt * 128 + 16 * warp + g + 8 * hh : 32 * warp + 16 * rt + g + 8 * hh;
+      rowoff[rt][hh] = R * 128;
+    }
+  for (int job = blockIdx.x; job < n_jobs && !failed; job += gridDim.x) {
+    Job d;
+    describe_job<UP>(p, job, rb_per_item, ks_n, d);
+    if (d.nsteps == 0) continue;
+    const bool mine = UP ? 16 * warp < d.nrow : 32 * warp < d.nrow;  // this warp has rows in the job
+    Scales S{};
+    int par = 0;
+    if (d.ngr > 0) {
+      par = sj & 1;
+      if (!mbar_wait(&sfull[par], (sj >> 1) & 1, p.status)) failed = true;
+      const uint32_t sa = sa0 + par * p.s_bytes;
 #pragma unroll
       for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int row = slot_row<UP>(d, p.I, 32 * warp + 16 * rt + g + 8 * hh);
+          S.row[rt][hh] = sa + (row < 0 ? 0 : scale_slot<UP>(d, p.I, row) * d.sst);
+        }
+    }
+    float tot[2][NB][4];
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
         for (int i = 0; i < 4; ++i) tot[rt][nb][i] = 0.f;
+    for (int step = 0; step < d.nsteps && !failed; ++step, ++it) {
+      const int sidx = it % kGemvStages;
+      if (!mbar_wait(&full[sidx], (it / kGemvStages) & 1, p.status)) {
+        failed = true;  // finish this job's barriers with the other consumer warps, then stop
+        break;
+      }
+      const int col0 = d.k_lo + step * d.step_cols;
+      const int ncols = min(d.step_cols, d.k_hi - col0);
+      const uint32_t wtile = st0 + sidx * p.stage_bytes;
+      const uint32_t bbase = wtile + kGemvWBytes;
+      if (mine) {
+        switch (d.kind) {
+#define MOEB200_STAGE(K)                                                                                      \
+  case K:                                                                                                     \
+    run_stage<AT, NB, K>(wtile, rowoff, bbase, p.b_stride, d.ntok, ncols, col0, d.gs, d.g0, S, tot, g, t); \
+    break;
+          MOEB200_STAGE(kI4w2)
+          MOEB200_STAGE(kI4w1)
+          MOEB200_STAGE(kI8w4)
+          MOEB200_STAGE(kI8w2)
+          MOEB200_STAGE(kI8w1)
+          MOEB200_STAGE(kF16w4)
+          MOEB200_STAGE(kF16w2)
+          MOEB200_STAGE(kF16w1)
+          MOEB200_STAGE(kBF16w4)
+          MOEB200_STAGE(kBF16w2)
+          MOEB200_STAGE(kBF16w1)
+          MOEB200_STAGE(kF32w2)
+          MOEB200_STAGE(kF32w1)
+#undef MOEB200_STAGE
+          default:
+            break;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[sidx]);
     }
-  };
-  begin_tile();
-
-  for (uint32_t it = 0;; ++it) {
-    const int sidx = it % kGemvStages;
-    if (!mbar_wait(&bars[sidx], (it / kGemvStages) & 1u, p.status)) return;
-    const uint8_t* st = stages + sidx * sb;
-    const int col0 = cd.k_lo + cstep * cd.step_cols;
-    const int ncols = min(cd.step_cols, cd.k_hi - col0);
-    switch (cd.kind) {
-      case kI4w2: run_step<AT, NB, kI4w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI4w1: run_step<AT, NB, kI4w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w4: run_step<AT, NB, kI8w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w2: run_step<AT, NB, kI8w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kI8w1: run_step<AT, NB, kI8w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w4: run_step<AT, NB, kF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w2: run_step<AT, NB, kF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF16w1: run_step<AT, NB, kF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w4: run_step<AT, NB, kBF16w4>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w2: run_step<AT, NB, kBF16w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kBF16w1: run_step<AT, NB, kBF16w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF32w2: run_step<AT, NB, kF32w2>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      case kF32w1: run_step<AT, NB, kF32w1>(st, col0, ncols, B, S, cd.gs, tot, g, t); break;
-      default: break;
+    if (d.ngr > 0) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[par]);
+      ++sj;
     }
-    const bool last = (cstep + 1 == cd.nsteps);
-    if (last) {
-      // epilogue: c-fragment (row g | g+8, token 2t | 2t+1) per row tile and token block
+    // epilogue: c-fragment (row g | g+8, token 2t | 2t+1) per row tile and token block
+    if (mine) {
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int tk = 8 * nb + 2 * t + (i & 1);
-          if (tk >= cit.ntok) continue;
+          if (tk >= d.ntok) continue;
           const int rrow = g + 8 * (i >> 1);
-          const int j = cit.start + tk;
+          const int j = d.start + tk;
           if (UP) {
+            if (16 * warp + rrow >= d.nrow) continue;
+            const int r = d.r0 + 16 * warp + rrow;  // gate row; its up row is I + r
             if constexpr (SPLIT) {
-              float* prow = p.pre + (int64_t)j * 2 * p.I + cd.r0 + rrow;
+              float* prow = p.pre + (int64_t)j * 2 * p.I + r;
               red_add_f32(prow, tot[0][nb][i]);
               red_add_f32(prow + p.I, tot[1][nb][i]);
             } else {
               const float hv = silu_mul(tot[0][nb][i], tot[1][nb][i]);
-              static_cast<AT*>(p.h)[(int64_t)j * p.I + cd.r0 + rrow] = from_f32<AT>(hv);
+              static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
             }
           } else {
             const int pos = p.pos[j];
             const int tok = pos / p.k;
             const float wv = p.wflat[pos];
-            float* arow = p.acc + (int64_t)tok * p.H + cd.r0;
+            float* arow = p.acc + (int64_t)tok * p.H + d.r0 + 32 * warp;
             red_add_f32(arow + rrow, wv * tot[0][nb][i]);
             red_add_f32(arow + 16 + rrow, wv * tot[1][nb][i]);
           }
         }
-      if constexpr (UP && SPLIT) {
-        // the last K split to arrive at this tile turns its 16 gate|up pre-activation rows into h
-        __threadfence();
-        __syncwarp();
+    }
+    if constexpr (UP && SPLIT) {
+      // the last K split of this row block to arrive turns the block's pre-activations into h
+      __threadfence();
+      consumers_sync();
+      if (threadIdx.x == 0) {
         const int kc = split_cols(p.H, ks_n);
         const int ksplits = (p.H + kc - 1) / kc;  // non-empty splits
-        int fin = 0;
-        if (lane == 0) {
-          int32_t* cnt = p.tile_cnt + (int64_t)cd.item * rb_per_item + cd.r0 / 16;
-          fin = atomicAdd(cnt, 1) == ksplits - 1;
-        }
-        fin = __shfl_sync(0xffffffffu, fin, 0);
-        if (fin) {
-          __threadfence();
-          for (int q = lane; q < 16 * cit.ntok; q += 32) {
-            const int j = cit.start + q / 16, r = cd.r0 + (q & 15);
-            const float* prow = p.pre + (int64_t)j * 2 * p.I;
-            const float hv = silu_mul(__ldcg(prow + r), __ldcg(prow + p.I + r));
-            static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
-          }
+        int32_t* cnt = p.tile_cnt + (int64_t)d.item * rb_per_item + d.rb;
+        *bcast = atomicAdd(cnt, 1) == ksplits - 1;
+      }
+      consumers_sync();
+      const int fin = *bcast;
+      consumers_sync();  // bcast is reused by the next job
+      if (fin) {
+        __threadfence();
+        for (int q = threadIdx.x; q < d.nrow * d.ntok; q += kGemvCons * 32) {
+          const int j = d.start + q / d.nrow, r = d.r0 + q % d.nrow;
+          const float* prow = p.pre + (int64_t)j * 2 * p.I;
+          const float hv = silu_mul(__ldcg(prow + r), __ldcg(prow + p.I + r));
+          static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
         }
       }
-    }
-    __syncwarp();
-    produce(sidx);  // refill the stage just consumed with the step kGemvStages ahead
-    if (last) {
-      cstep = 0;
-      do {
-        ctile += nw;
-        if (ctile < n_tiles) describe_tile<UP>(p, ctile, rb_per_item, ks_n, cd);
-      } while (ctile < n_tiles && cd.nsteps == 0);
-      if (ctile >= n_tiles) break;
-      begin_tile();
-    } else {
-      ++cstep;
     }
   }
 }
@@ -579,57 +817,136 @@ __global__ void combine_parts_kernel(const float* __restrict__ parts, int G, int
 }
 
 template <typename AT, int NB, bool UP, bool SPLIT>
-cudaError_t launch_t(const GemvParams& p, int grid, int warps, cudaStream_t s) {
-  const int smem = gemv_smem_bytes(p.stage_bytes, warps);
+cudaError_t launch_t(const GemvParams& p, const TmaTemplates& tm, int grid, int smem, cudaStream_t s) {
   auto kern = gemv_kernel<AT, NB, UP, SPLIT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, warps * 32, smem, s>>>(p);
+  kern<<<grid, kGemvThreads, smem, s>>>(p, tm);
   return cudaGetLastError();
 }
 
-template <typename AT, int NB, bool UP, bool SPLIT>
-int occupancy_t(int smem, int warps) {
-  auto kern = gemv_kernel<AT, NB, UP, SPLIT>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 1;
-  int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, warps * 32, smem) != cudaSuccess) return 1;
-  return nb;
-}
-
-// SPLIT: the up phase adds split-K partials into pre (the down phase always reads h).
 template <typename AT, bool UP>
-cudaError_t launch_phase(const GemvParams& p, int nb, int grid, int warps, cudaStream_t s) {
+cudaError_t launch_phase(const GemvParams& p, const TmaTemplates& tm, int nb, int grid, int smem, cudaStream_t s) {
   if (UP && p.ksplit_up > 1)
-    return nb == 2 ? launch_t<AT, 2, UP, true>(p, grid, warps, s) : launch_t<AT, 1, UP, true>(p, grid, warps, s);
-  return nb == 2 ? launch_t<AT, 2, UP, false>(p, grid, warps, s) : launch_t<AT, 1, UP, false>(p, grid, warps, s);
+    return nb == 2 ? launch_t<AT, 2, UP, true>(p, tm, grid, smem, s) : launch_t<AT, 1, UP, true>(p, tm, grid, smem, s);
+  return nb == 2 ? launch_t<AT, 2, UP, false>(p, tm, grid, smem, s) : launch_t<AT, 1, UP, false>(p, tm, grid, smem, s);
 }
 
-template <typename AT>
-int occupancy_at(int nb, bool up, bool split, int smem, int warps) {
-  if (up) {
-    if (split) return nb == 2 ? occupancy_t<AT, 2, true, true>(smem, warps) : occupancy_t<AT, 1, true, true>(smem, warps);
-    return nb == 2 ? occupancy_t<AT, 2, true, false>(smem, warps) : occupancy_t<AT, 1, true, false>(smem, warps);
+// Tensor-map template of a weight field: uint8 [rows][row_bytes], boxes of 128 bytes x box_rows,
+// 128-byte swizzle. The address is a placeholder (16-byte aligned device memory): every job swaps
+// in its record's address. Templates are cached per shape.
+cudaError_t weight_template(CUtensorMap* out, int row_bytes, int rows, int box_rows, void* placeholder) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, CUtensorMap> cache;
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(row_bytes, rows, box_rows);
+  auto f = cache.find(key);
+  if (f != cache.end()) {
+    *out = f->second;
+    return cudaSuccess;
   }
-  if (split) return nb == 2 ? occupancy_t<AT, 2, false, true>(smem, warps) : occupancy_t<AT, 1, false, true>(smem, warps);
-  return nb == 2 ? occupancy_t<AT, 2, false, false>(smem, warps) : occupancy_t<AT, 1, false, false>(smem, warps);
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q{};
+    void* fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, placeholder, dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  cache[key] = m;
+  *out = m;
+  return cudaSuccess;
+}
+
+bool is_int_type(int wt) { return wt == MOEB200_I4 || wt == MOEB200_I8; }
+
+// A K split must cover whole groups and whole chunks: kSplitCols is a multiple of every group size.
+bool split_ok(const moeb200_layout* L, int nlay, int K, bool up, int ks) {
+  if (K < ks * kSplitCols / 2) return false;
+  for (int i = 0; i < nlay; ++i)
+    if (is_int_type(L[i].wtype) && kSplitCols % (up ? L[i].gs_up : L[i].gs_dn)) return false;
+  return true;
+}
+
+// Shared-memory geometry of a phase (2 stages, 2 scale areas, tensor-map staging, barriers, 1024
+// bytes of alignment slack); returns its bytes.
+int phase_smem(GemvParams& p, const moeb200_layout* lays, int nlay, int nb, int K, bool up, int ks) {
+  int bst = 0, sst = 0;
+  const int kc = std::min(K, split_cols(K, ks));
+  for (int i = 0; i < nlay; ++i) {
+    bst = std::max(bst, gemv_b_stride(lays[i].wtype));
+    if (is_int_type(lays[i].wtype)) {
+      const int gs = up ? lays[i].gs_up : lays[i].gs_dn;
+      sst = std::max(sst, gemv_s_stride((kc + gs - 1) / gs));
+    }
+  }
+  p.b_stride = bst;
+  p.b_rows = 8 * nb;
+  p.stage_bytes = (kGemvWBytes + p.b_rows * bst + 1023) / 1024 * 1024;
+  p.s_bytes = (kGemvJobRows * sst + 127) / 128 * 128;
+  return kGemvStages * p.stage_bytes + 2 * p.s_bytes + 128 + 10 * 8 + 1024;
+}
+
+cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay, int act, int nb, int max_items,
+                            int n_pairs, int max_split_pairs, bool up, cudaStream_t s) {
+  const int sms = num_sms_cached();
+  const int K = up ? p.H : p.I;
+  const int rows = up ? p.I : p.H;
+  const int rpj = up ? kGemvJobRows / 2 : kGemvJobRows;
+  const int64_t jobs1 = (int64_t)max_items * ((rows + rpj - 1) / rpj);
+  // split K while the jobs would not give every SM two of them (up: only with room for pre)
+  int ks = 1;
+  const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
+  while (can_split && ks < 8 && jobs1 * ks < 2ll * sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
+  if (up)
+    p.ksplit_up = ks;
+  else
+    p.ksplit_dn = ks;
+  const int smem = phase_smem(p, lays, nlay, nb, K, up, ks);
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  TmaTemplates tm{};
+  for (int i = 0; i < nlay; ++i) {
+    const int row_bytes = K * gemv_wbits(lays[i].wtype) / 8;
+    cudaError_t e = weight_template(&tm.m[i], row_bytes, up ? 2 * p.I : p.H, up ? kGemvJobRows / 2 : kGemvJobRows,
+                                    p.tmap_ws);
+    if (e != cudaSuccess) return e;
+  }
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(sms, kGemvMaxGrid), jobs1 * ks));
+  if (up && ks > 1) {
+    cudaError_t e = cudaMemsetAsync(p.pre, 0, (size_t)n_pairs * 2 * p.I * sizeof(float), s);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p.tile_cnt, 0, (size_t)max_items * ((p.I + rpj - 1) / rpj) * sizeof(int32_t), s);
+    if (e != cudaSuccess) return e;
+  }
+  if (act == MOEB200_BF16)
+    return up ? launch_phase<__nv_bfloat16, true>(p, tm, nb, grid, smem, s)
+              : launch_phase<__nv_bfloat16, false>(p, tm, nb, grid, smem, s);
+  return up ? launch_phase<__half, true>(p, tm, nb, grid, smem, s) : launch_phase<__half, false>(p, tm, nb, grid, smem, s);
 }
 
 }  // namespace
 
-int gemv_occupancy(int act_type, int nb, bool up, bool split, int smem, int warps) {
-  return act_type == MOEB200_BF16 ? occupancy_at<__nv_bfloat16>(nb, up, split, smem, warps)
-                                  : occupancy_at<__half>(nb, up, split, smem, warps);
-}
-
-cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s) {
-  return act_type == MOEB200_BF16 ? launch_phase<__nv_bfloat16, true>(p, nb, grid, warps, s)
-                                  : launch_phase<__half, true>(p, nb, grid, warps, s);
-}
-
-cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s) {
-  return act_type == MOEB200_BF16 ? launch_phase<__nv_bfloat16, false>(p, nb, grid, warps, s)
-                                  : launch_phase<__half, false>(p, nb, grid, warps, s);
+cudaError_t launch_gemv_phases(GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int nb,
+                               int max_items, int n_pairs, int max_split_pairs, cudaStream_t s) {
+  p.ksplit_up = p.ksplit_dn = 1;
+  cudaError_t e = trace_mark(0, s);
+  if (e != cudaSuccess) return e;
+  e = plan_and_launch(p, lays, nlay, act_type, nb, max_items, n_pairs, max_split_pairs, true, s);
+  if (e != cudaSuccess) return e;
+  e = trace_mark(1, s);
+  if (e != cudaSuccess) return e;
+  e = plan_and_launch(p, lays, nlay, act_type, nb, max_items, n_pairs, max_split_pairs, false, s);
+  if (e != cudaSuccess) return e;
+  return trace_mark(2, s);
 }
 
 cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_type, void* out, int add,

@@ -36,41 +36,62 @@ struct GemvParams {
   int32_t I;
   int32_t T;
   const void* x;   // [T, H] activations
-  void* h;         // [n_pairs, I] activations, row j = sorted pair j (unsplit up phase)
+  void* h;         // [n_pairs, I] activations, row j = sorted pair j
   float* pre;      // [n_pairs, 2I] fp32 gate|up pre-activations (split-K up phase), else null
-  int32_t* tile_cnt;  // [items, I/16] arrivals of the K splits of each up tile (split-K), zeroed per call
+  int32_t* tile_cnt;  // [items, I/16] arrivals of the K splits of each up job (split-K), zeroed per call
   float* acc;      // [T, H] fp32 combine buffer
   int32_t* status;
   LayoutDev lay[4];
   int32_t ksplit_up;    // K splits of the up phase (1 = write h directly)
   int32_t ksplit_dn;    // K splits of the down phase
-  int32_t stage_bytes;  // bytes of one warp stage (32 padded row segments)
+  void* tmap_ws;        // [4 * grid] 128-byte tensor-map slots of the GEMV CTAs (device memory)
+  // shared-memory geometry of a GEMV launch (set by launch_gemv_phases)
+  int32_t b_stride;     // bytes between two token rows of a stage
+  int32_t b_rows;       // token rows of a stage (8 * NB)
+  int32_t stage_bytes;  // one stage: the weight tile (kGemvJobRows x 256 bytes), then b_rows token rows
+  int32_t s_bytes;      // one job's scale area
   int32_t zero_acc;     // up phase: zero acc before use
 };
 
 // Geometry shared by host and device.
+constexpr int kGemvCons = 8;                  // consumer warps of a GEMV CTA
+constexpr int kGemvJobRows = 32 * kGemvCons;  // weight rows of one job (up: 128 gate + 128 up)
+constexpr int kGemvThreads = 32 * (kGemvCons + 1);
 constexpr int kGemvStages = 2;
-constexpr int kGemvMaxWarps = 12;
-constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline step
+constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline stage
 constexpr int kSplitCols = 512;  // K splits are multiples of this many columns
 
-// Padded stride of one 256-byte row segment in a stage, per record element type: fragment reads of
-// the eight rows a warp touches at once then fall in different banks.
-__host__ __device__ inline int gemv_row_stride(int wtype) {
-  return wtype == MOEB200_I4 ? 288 : wtype == MOEB200_I8 ? 320 : 272;
+constexpr int kGemvWBytes = kGemvJobRows * kStepBytes;  // weight tile of a stage (two 128-byte halves)
+constexpr int kGemvMaxGrid = 160;                        // tensor-map slots are carved for this many CTAs
+
+__host__ __device__ inline int gemv_wbits(int wtype) {
+  return wtype == MOEB200_I4 ? 4 : wtype == MOEB200_I8 ? 8 : wtype == MOEB200_F32 ? 32 : 16;
 }
 
-__host__ __device__ inline int gemv_smem_bytes(int stage_bytes, int warps) {
-  return warps * (kGemvStages * stage_bytes + kGemvStages * 8);
+// Bytes of one token row in a stage (the stage's columns in a 16-bit activation type, padded to an
+// odd multiple of 16 bytes so the token rows a warp reads at once fall in different banks).
+__host__ __device__ inline int gemv_b_stride(int wtype) {
+  return kStepBytes * 8 / gemv_wbits(wtype) * 2 + 16;
+}
+
+// Bytes of one row of a job's scale area: ngroups fp16 scales padded to an odd multiple of 16.
+__host__ __device__ inline int gemv_s_stride(int ngroups) {
+  int s = (ngroups * 2 + 15) / 16 * 16;
+  if ((s / 16) % 2 == 0) s += 16;
+  return s;
 }
 
 // host launchers (gemv.cu)
-cudaError_t launch_gemv_up(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
-cudaError_t launch_gemv_down(const GemvParams& p, int act_type, int nb, int grid, int warps, cudaStream_t s);
+// Plans split-K and the shared-memory geometry of the two GEMV phases, then launches gate/up and
+// down (with trace marks around them). nb: token blocks of 8 per item (1 or 2).
+cudaError_t launch_gemv_phases(GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int nb,
+                               int max_items, int n_pairs, int max_split_pairs, cudaStream_t s);
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s);
 cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_type, void* out, int add,
                                  cudaStream_t s);
-int gemv_occupancy(int act_type, int nb, bool up, bool split, int smem, int warps);
+// trace hook of capi.cu: records a phase mark on the stream when tracing is on
+cudaError_t trace_mark(int which, cudaStream_t s);
+int num_sms_cached();
 // tcgen05 grouped GEMM (gemm_tc.cu): items of up to 128 pairs, I and H multiples of 128
 cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s);
 cudaError_t launch_gemm_down(const GemvParams& p, int act_type, int grid, cudaStream_t s);

@@ -270,22 +270,21 @@ __device__ __forceinline__ int slot_of(int level, int P) {
 
 // D1: one warp per block of kDispBlock pairs, processed in order 32 at a time. Each pair gets its
 // rank among the earlier pairs of the block with the same key (expert, and expert*P + slot).
-__global__ void __launch_bounds__(32) dispatch_count_kernel(DispatchParams p) {
+__global__ void __launch_bounds__(kDispLoadThreads) dispatch_count_kernel(DispatchParams p) {
   extern __shared__ int32_t sh[];
   int32_t* cnt_k = sh;               // [E*P]
   int32_t* cnt_e = sh + p.E * p.P;   // [E]
-  const int lane = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int keys = p.E * p.P;
-  for (int i = lane; i < keys + p.E; i += 32) sh[i] = 0;
-  __syncwarp();
+  for (int i = tid; i < keys + p.E; i += blockDim.x) sh[i] = 0;
   const int n = p.T * p.k;
   const int b = blockIdx.x;
   const int base = b * kDispBlock;
   const int end = min(n, base + kDispBlock);
-  // keys of the whole block first (independent loads, all in flight), ranked in order below
+  // keys of the whole block first, loaded by all threads; one warp ranks them in order below
   int32_t* key_s = sh + keys + p.E;   // [kDispBlock]
   int32_t* e_s = key_s + kDispBlock;  // [kDispBlock]
-  for (int i = base + lane; i < end; i += 32) {
+  for (int i = base + tid; i < end; i += blockDim.x) {
     int key = -1, e = -1;
     const bool skipped = p.skip && p.skip[i];
     const int64_t ev = p.idx[i];
@@ -299,7 +298,8 @@ __global__ void __launch_bounds__(32) dispatch_count_kernel(DispatchParams p) {
     key_s[i - base] = key;
     e_s[i - base] = e;
   }
-  __syncwarp();
+  __syncthreads();
+  if (tid >= 32) return;
   for (int c = base; c < end; c += 32) {
     const int i = c + lane;
     int key = -1, e = -1;
@@ -488,23 +488,23 @@ cudaError_t launch_router(const void* h, const void* wr, const float* bias, int 
                           uint8_t* level, uint8_t* skip, cudaStream_t s) {
   const int tpb = T <= 8 ? T : 8;
   dim3 grid((E + 7) / 8, (T + tpb - 1) / tpb);
-  // few (token, expert) logits: one expert x 8 tokens per warp (8 experts per block) keeps every SM
+  // few (token, expert) logits: one expert x 4 tokens per warp (8 experts per block) keeps every SM
   // busy; many: 4 x 8 per warp (8 x 32 per block) cuts the L2 re-reads of token and router rows
   const bool big = (int64_t)T * E >= 65536;
-  const dim3 g16 = big ? dim3((E + 7) / 8, (T + 31) / 32) : dim3((E + 7) / 8, (T + 7) / 8);
+  const dim3 g16 = big ? dim3((E + 7) / 8, (T + 31) / 32) : dim3((E + 7) / 8, (T + 3) / 4);
   if (act_type == MOEB200_F16) {
     if (big)
       router_logits_kernel<__half, 4, 8, 2><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
                                                                 static_cast<const __half*>(wr), T, H, E, logits);
     else
-      router_logits_kernel<__half, 1, 8, 8><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
+      router_logits_kernel<__half, 1, 4, 8><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
                                                                 static_cast<const __half*>(wr), T, H, E, logits);
   } else if (act_type == MOEB200_BF16) {
     if (big)
       router_logits_kernel<__nv_bfloat16, 4, 8, 2><<<g16, 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
     else
-      router_logits_kernel<__nv_bfloat16, 1, 8, 8><<<g16, 256, 0, s>>>(
+      router_logits_kernel<__nv_bfloat16, 1, 4, 8><<<g16, 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
   } else
     router_logits_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(h), static_cast<const float*>(wr), T, H,
@@ -527,7 +527,7 @@ cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, ui
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
   const int keys = p.E * p.P;
   const size_t sh = (size_t)(keys + p.E + 2 * kDispBlock) * sizeof(int32_t);
-  dispatch_count_kernel<<<p.nblk, 32, sh, s>>>(p);
+  dispatch_count_kernel<<<p.nblk, kDispLoadThreads, sh, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   dispatch_scan_kernel<<<1, 1024, 0, s>>>(p);

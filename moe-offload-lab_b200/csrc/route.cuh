@@ -7,6 +7,7 @@ namespace moeb200 {
 
 constexpr int kDispBlock = 1024;  // pairs per dispatch block
 constexpr int kMaxKeys = 4096;    // max E * P (and E) handled by one dispatch
+constexpr int kDispLoadThreads = 256;  // threads of a dispatch-count block (one warp ranks)
 
 struct PolicyDev {
   int32_t mode;  // 0 hi, 1 lo, 2 hobbit, 3 threshold

@@ -20,6 +20,7 @@ from __future__ import annotations
 
 from collections import OrderedDict
 
+import numpy as np
 import torch
 
 from . import ops
@@ -89,6 +90,7 @@ class ColdExperts:
         self.last_use: dict[tuple[str, int], torch.cuda.Event] = {}
         self.uploaded_bytes = 0
         self.uploads = 0
+        self._codes: dict[int, np.ndarray] = {}
 
     def add_cold(self, layer: int, expert: int, prec: str, blob: torch.Tensor) -> None:
         """Register a record held on the host (pinned uint8 tensor; pinned here if it is not)."""
@@ -99,7 +101,17 @@ class ColdExperts:
         if prec not in self.plans:
             raise ValueError(f"no device slots for precision {prec}")
         self.host[(layer, expert, prec)] = blob if blob.is_pinned() else blob.pin_memory()
+        self._codes.pop(layer, None)
         self.rt.remove_record(layer, expert, prec)
+
+    def _cold_codes(self, layer: int, E: int, P: int) -> np.ndarray:
+        """expert * P + slot of every host-held record of `layer` (cached per layer)."""
+        c = self._codes.get(layer)
+        if c is None:
+            c = np.array(sorted(e * P + self.rt.precisions.index(p) for (l_, e, p) in self.host if l_ == layer),
+                         np.int64)
+            self._codes[layer] = c
+        return c
 
     def reset(self) -> None:
         """Drop every uploaded record (their table entries go back to not resident)."""
@@ -113,22 +125,19 @@ class ColdExperts:
         rt = self.rt
         T, k = idx.shape
         P = rt.n_prec
-        idx_h = idx.cpu()
-        lv_h = level.cpu() if level is not None else torch.zeros(T, k, dtype=torch.uint8)
-        sk_h = skip.cpu().bool() if skip is not None else torch.zeros(T, k, dtype=torch.bool)
-        from .runtime import level_to_slot
-
-        cold_pair = torch.zeros(T, k, dtype=torch.bool)
+        idx_h = idx.cpu().numpy()
+        lv_h = level.cpu().numpy().astype(np.int64) if level is not None else np.zeros((T, k), np.int64)
+        sk_h = skip.cpu().numpy().astype(bool) if skip is not None else np.zeros((T, k), bool)
+        # precision slot of every pair (moelab/policy.py:188-192) and its (expert, slot) code
+        slot = np.minimum(lv_h, P - 1) if P >= 3 else np.where(lv_h == 0, 0, P - 1)
+        code = idx_h.astype(np.int64) * P + slot
+        cold_code = self._cold_codes(layer, rt.num_experts, P)
+        cold_pair = np.isin(code, cold_code) & ~sk_h
         needed: dict[str, list] = {p: [] for p in self.plans}
-        for t in range(T):
-            for j in range(k):
-                if sk_h[t, j]:
-                    continue
-                prec = rt.precisions[level_to_slot(int(lv_h[t, j]), P)]
-                key = (layer, int(idx_h[t, j]), prec)
-                if key in self.host:
-                    cold_pair[t, j] = True
-                    needed[prec].append(key)
+        for c in np.unique(code[cold_pair]).tolist():
+            e, sl = divmod(int(c), P)
+            needed[rt.precisions[sl]].append((layer, e, rt.precisions[sl]))
+        cold_pair = torch.from_numpy(cold_pair)
         if not cold_pair.any():
             return rt.run_layer(layer, x, idx, w, level=level, skip=skip, out=out)
         table = rt._table(layer)
