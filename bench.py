@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
+    ap.add_argument("--policy", default=None, choices=["hi", "lo"],
+                    help="--ncu mode: every pair at the most precise (hi) or least precise (lo) record")
     ap.add_argument("--extra", default="c0,c2,c3,c3p,c4", help="single-layer configs measured beside the headline")
     return ap.parse_args()
 
@@ -577,6 +579,8 @@ def main():
     cfg = dict(CONFIGS[args.config] if args.ncu else CFG1)
     if args.layers:
         cfg["layers"] = args.layers
+    if args.ncu and args.policy:
+        cfg["policy"] = dict(mode=args.policy)
     from moeb200 import ops as _ops
 
     _ops.set_path(args.path)
@@ -622,6 +626,13 @@ def main():
     dn_bytes_launch = rb["down_total"] / L
     up_gbs = up_bytes_launch / (up_ms / 1e3) / 1e9
     dn_gbs = dn_bytes_launch / (dn_ms / 1e3) / 1e9
+    # DRAM bytes (read + write) of one gate/up launch from the committed ncu capture of this workload
+    traffic, traffic_src = None, None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists() and world == 1 and T == CFG1["T"]:
+        rec = json.loads(tf.read_text()).get("gemv_up_c1_T64")
+        if rec:
+            traffic, traffic_src = rec["bytes"], rec["source"]
 
     # sweep of other decode batches (device-resident value only)
     sweep = {}
@@ -690,7 +701,8 @@ def main():
             "int4_fp16_record_gbs": (rb["up"] + rb["down"]) / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "gemv up (gate/up dequant GEMV + SwiGLU)",
                          "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": up_gbs / hbm_peak,
-                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": up_bytes_launch,
+                         "peak_kind": peak_kind, "traffic": traffic, "traffic_source": traffic_src,
+                         "bytes_per_launch": up_bytes_launch,
                          "launch_ms": up_ms, "down_achieved": dn_gbs, "down_launch_ms": dn_ms},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},

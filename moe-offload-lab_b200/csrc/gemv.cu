@@ -157,10 +157,7 @@ struct Scales {
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t v = lds_u16(row[rt][hh] + 2 * gi);
-        s[rt][hh] = v | (v << 16);
-      }
+      for (int hh = 0; hh < 2; ++hh) s[rt][hh] = prmt(lds_u16(row[rt][hh] + 2 * gi), 0u, 0x1010);  // (s, s)
   }
 };
 
@@ -398,6 +395,9 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
     brow[nb] = bbase + (g + 8 * nb) * bstride + LOFF * t * 2;
   }
   const uint32_t lo = LOFF * t * W2 / 2;  // the lane's first byte inside a chunk
+  // group of each chunk, advanced without divisions (a chunk never straddles a group)
+  const int cpg = (I4 || I8) ? gs / CH : 1;
+  int gi = (I4 || I8) ? col0 / gs - g0 : 0, cc = (I4 || I8) ? (col0 % gs) / CH : 0;
 #pragma unroll 2
   for (int ci = 0; ci < nch; ++ci) {
     uint32_t xb[NB][NW];
@@ -413,15 +413,19 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
     const uint32_t o = ci * (CH * W2 / 2) + lo;
     const uint32_t so0 = swz(o, g), so1 = swz(o + 16, g);
     if constexpr (I4) {
-      chunk_int4<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, (col0 + ci * CH) / gs - g0, tot);
+      chunk_int4<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (I8) {
-      chunk_int8<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, (col0 + ci * CH) / gs - g0, tot);
+      chunk_int8<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (WT == 2) {
       chunk_float<AT, float, NB, WPL>(wr, so0, so1, xb, tot);
     } else if constexpr (WT == 1) {
       chunk_float<AT, __nv_bfloat16, NB, WPL>(wr, so0, so1, xb, tot);
     } else {
       chunk_float<AT, __half, NB, WPL>(wr, so0, so1, xb, tot);
+    }
+    if (++cc == cpg) {
+      cc = 0;
+      ++gi;
     }
   }
 }

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict
   for (int r = 0; r < RE; ++r)
 #pragma unroll
     for (int q = 0; q < RT; ++q) acc[r][q] = 0.f;
+#pragma unroll 4
   for (int c = lane * 8; c < H; c += 256) {
     float wf[RE][8];
 #pragma unroll
