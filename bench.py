@@ -260,10 +260,14 @@ class Stack:
         return step
 
     def launches_per_step(self) -> int:
-        # per layer: router logits, router top-k (+ levels), dispatch (count, scan, scatter),
-        # gate/up GEMV, down GEMV, finalize; expert parallel: + pack, unpack, combine, no finalize
-        # shared expert: gate kernel, gate/up, down, finalize
-        return self.cfg["layers"] * ((10 if self.ep else 8) + (4 if self.shared else 0))
+        # per layer: router logits, router top-k (+ levels), dispatch (one fused kernel when the
+        # layer's pairs fit one 1024-pair block, else count, scan, scatter), gate/up GEMV, down GEMV,
+        # finalize; expert parallel: + pack, unpack, combine, no finalize; shared expert: gate
+        # kernel, gate/up, down, finalize
+        T = self.xs[0].shape[0] * self.world
+        disp = 1 if T * self.cfg["k"] <= 1024 else 3
+        base = 2 + disp + 2 + (3 if self.ep else 1)
+        return self.cfg["layers"] * (base + (4 if self.shared else 0))
 
     def gathered_routing(self, li: int):
         """idx, level, skip of every rank's tokens for layer li (numpy), outside any timed region."""

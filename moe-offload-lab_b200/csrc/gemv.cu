@@ -8,11 +8,12 @@
 //
 // One persistent CTA per SM works through jobs = (work item, 256 weight rows, K split). Eight
 // consumer warps own 32 rows each (up: 16 gate rows and the matching 16 up rows, so SwiGLU happens
-// in registers); a producer warp streams the job's K range through a ring of shared-memory stages
-// with 1-D bulk TMA copies: a stage holds one 256-byte segment of each of the 256 rows (padded row
-// stride, conflict-free fragment reads) and the same columns of the item's token rows, and the
-// job's group scales go to a double-buffered scale area with cp.async. Consumers dequantise in
-// registers straight into mma.sync m16n8k16 A fragments and multiply them with up to 8*NB tokens:
+// in registers). A producer warp streams the job's K range through two shared-memory stages: per
+// stage, tensor-map TMA loads (the map retargeted to the record on the device) bring a 128-byte
+// swizzled tile of one 256-byte segment of each of the 256 rows, and 1-D bulk copies the same
+// columns of the item's token rows; the job's whole scale rows go to a double-buffered scale area
+// with one or two bulk copies. Consumers dequantise in registers straight into mma.sync m16n8k16
+// A fragments and multiply them with up to 8*NB tokens:
 //   fp16 activations, int4/int8 records: the weight is dequantised together with its scale in
 //     fp16, w = fp16((q - 8) * s) (the exact (q - 8) times s, rounded once: the value moelab's
 //     materialize gives), and accumulated in fp32 across all groups;
@@ -125,16 +126,6 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   return r;
 }
 
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-// The mbarrier receives one arrival once every cp.async issued so far by this thread has landed.
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -445,17 +436,26 @@ struct Job {
   int32_t k_lo, k_hi;        // input columns of this K split
   int32_t step_cols, nsteps;
   int32_t rstride, sstride;  // bytes per weight row / scale row in the record
-  int32_t g0, ngr, sst;      // first group, groups of the split, scale-area row stride
+  int32_t g0, ngr, sst;      // first group held (0), groups per scale row, scale-area row stride
 };
 
+__device__ __forceinline__ int job_item(int job, int rb_per_item, int ks_n) { return job / (rb_per_item * ks_n); }
+
+// Item of a job (a global load: callers fetch it one job ahead).
+__device__ __forceinline__ Item load_item(const GemvParams& p, int job, int n_jobs, int rb_per_item, int ks_n) {
+  Item it{};
+  if (job < n_jobs) it = p.items[job_item(job, rb_per_item, ks_n)];
+  return it;
+}
+
 template <bool UP>
-__device__ __forceinline__ void describe_job(const GemvParams& p, int job, int rb_per_item, int ks_n, Job& d) {
+__device__ __forceinline__ void describe_job(const GemvParams& p, int job, const Item& it, int rb_per_item, int ks_n,
+                                             Job& d) {
   const int per_item = rb_per_item * ks_n;
   const int item = job / per_item;
   const int rem = job - item * per_item;
   const int ks = rem / rb_per_item;
   const int rb = rem - ks * rb_per_item;
-  const Item it = p.items[item];
   const LayoutDev L = p.lay[it.slot];
   const int K = UP ? p.H : p.I;
   const bool isint = L.wtype == MOEB200_I4 || L.wtype == MOEB200_I8;
@@ -483,30 +483,9 @@ __device__ __forceinline__ void describe_job(const GemvParams& p, int job, int r
     d.r0 = rb * kGemvJobRows;
     d.nrow = min(kGemvJobRows, p.H - d.r0);
   }
-  d.g0 = isint ? d.k_lo / d.gs : 0;
-  d.ngr = isint ? (d.k_hi - d.k_lo + d.gs - 1) / d.gs : 0;
-  d.sst = isint ? gemv_s_stride(d.ngr) : 0;
-}
-
-// Record row of stage slot m (m < 256) of a job, or -1 if the slot is unused. Slots 32w..32w+31
-// belong to consumer warp w: up = 16 gate rows then the 16 matching up rows; down = 32 rows.
-template <bool UP>
-__device__ __forceinline__ int slot_row(const Job& d, int I, int m) {
-  const int w = m >> 5, i = m & 31;
-  if (UP) {
-    const int gr = 16 * w + (i & 15);
-    if (gr >= d.nrow) return -1;
-    return (i < 16 ? 0 : I) + d.r0 + gr;
-  }
-  const int r = 32 * w + i;
-  return r < d.nrow ? d.r0 + r : -1;
-}
-
-// Row of the job's scale area that holds record row `row` (up: gate rows first, up rows at 128).
-template <bool UP>
-__device__ __forceinline__ int scale_slot(const Job& d, int I, int row) {
-  if (UP) return row >= I ? kGemvJobRows / 2 + (row - I - d.r0) : row - d.r0;
-  return row - d.r0;
+  d.g0 = 0;  // scale areas hold whole scale rows: groups are indexed absolutely
+  d.ngr = isint ? K / d.gs : 0;
+  d.sst = d.sstride;
 }
 
 // ---- TMA with tensor maps ------------------------------------------------------------------------------
@@ -570,7 +549,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       mbar_init(&empty[s], kGemvCons);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sfull[s], 32);
+      mbar_init(&sfull[s], 1);
       mbar_init(&sempty[s], kGemvCons);
     }
     fence_mbar_init();
@@ -587,41 +566,38 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // ---------------- producer warp ----------------
     uint32_t it = 0, sj = 0, jn = 0;
     bool ok = true;
+    Item nxt = load_item(p, blockIdx.x, n_jobs, rb_per_item, ks_n);
     for (int job = blockIdx.x; job < n_jobs && ok; job += gridDim.x) {
       Job d;
-      describe_job<UP>(p, job, rb_per_item, ks_n, d);
+      describe_job<UP>(p, job, nxt, rb_per_item, ks_n, d);
+      nxt = load_item(p, job + gridDim.x, n_jobs, rb_per_item, ks_n);  // in flight during this job
       if (d.nsteps == 0) continue;
       // tensor map of the job's weight field (a ring of four per CTA: the copies that used a slot
       // four jobs ago have landed, the stage ring being two deep)
       const uint64_t gdesc = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * 4 + (jn & 3)) * 128;
       retarget_tmap(tm.m[d.slot], smem_u32(sdesc), gdesc, d.q, lane);
       ++jn;
+      // token rows of the item (one per lane)
+      const AT* brow = nullptr;
+      if (lane < d.ntok) {
+        const int j = d.start + lane;
+        brow = UP ? static_cast<const AT*>(p.x) + (int64_t)(p.pos[j] / p.k) * p.H
+                  : static_cast<const AT*>(p.h) + (int64_t)j * p.I;
+      }
       if (d.ngr > 0) {
-        // the job's scale area: every used row's groups [g0, g0 + ngr)
+        // the job's scale area: whole scale rows of its gate (or down) rows at row 0 and of its up
+        // rows at row 128 -- contiguous blocks of the record, one bulk copy each
         const int par = sj & 1;
         if (sj >= 2) ok = mbar_wait(&sempty[par], ((sj >> 1) - 1) & 1, p.status);
         if (!ok) break;
-        const uint32_t sa = smem_u32(sarea + par * p.s_bytes);
-        const int nb2 = d.ngr * 2;
-        for (int m = lane; m < kGemvJobRows; m += 32) {
-          const int row = slot_row<UP>(d, p.I, m);
-          if (row < 0) continue;
-          const uint8_t* src = d.s + (int64_t)row * d.sstride + 2 * d.g0;
-          const uint32_t dst = sa + scale_slot<UP>(d, p.I, row) * d.sst;
-          const uintptr_t a = reinterpret_cast<uintptr_t>(src);
-          if ((a % 16) == 0 && nb2 % 16 == 0) {
-            for (int b = 0; b < nb2; b += 16) cp_async16(dst + b, src + b);
-          } else if ((a % 4) == 0 && nb2 % 4 == 0) {
-            for (int b = 0; b < nb2; b += 4) cp_async4(dst + b, src + b);
-          } else {  // odd group counts (small shapes): plain copies
-            for (int b = 0; b < nb2; b += 2) {
-              const uint16_t v = *reinterpret_cast<const uint16_t*>(src + b);
-              asm volatile("st.shared.u16 [%0], %1;" ::"r"(dst + b), "h"(v) : "memory");
-            }
-          }
+        if (lane == 0) {
+          uint8_t* sa = sarea + par * p.s_bytes;
+          const uint32_t blk = (uint32_t)(d.nrow * d.sstride);
+          mbar_arrive_expect_tx(&sfull[par], UP ? 2 * blk : blk);
+          bulk_g2s(sa, d.s + (int64_t)d.r0 * d.sstride, blk, &sfull[par]);
+          if (UP)
+            bulk_g2s(sa + (kGemvJobRows / 2) * d.sstride, d.s + (int64_t)(p.I + d.r0) * d.sstride, blk, &sfull[par]);
         }
-        __threadfence_block();  // plain stores of this lane before its arrival
-        cp_async_arrive(&sfull[par]);
         ++sj;
       }
       for (int step = 0; step < d.nsteps; ++step, ++it) {
@@ -647,12 +623,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
           }
         }
         __syncwarp();
-        if (lane < d.ntok) {
-          const int j = d.start + lane;
-          const AT* src = UP ? static_cast<const AT*>(p.x) + (int64_t)(p.pos[j] / p.k) * p.H
-                             : static_cast<const AT*>(p.h) + (int64_t)j * p.I;
-          bulk_g2s(stages + sidx * p.stage_bytes + kGemvWBytes + lane * p.b_stride, src + col0, bseg, &full[sidx]);
-        }
+        if (lane < d.ntok)
+          bulk_g2s(stages + sidx * p.stage_bytes + kGemvWBytes + lane * p.b_stride, brow + col0, bseg, &full[sidx]);
       }
     }
     // the CTA must not exit with copies in flight: wait for the last stages issued (consumed
@@ -677,10 +649,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const int R = UP ? rt * 128 + 16 * warp + g + 8 * hh : 32 * warp + 16 * rt + g + 8 * hh;
       rowoff[rt][hh] = R * 128;
     }
+  Item nxt = load_item(p, blockIdx.x, n_jobs, rb_per_item, ks_n);
   for (int job = blockIdx.x; job < n_jobs && !failed; job += gridDim.x) {
     Job d;
-    describe_job<UP>(p, job, rb_per_item, ks_n, d);
+    describe_job<UP>(p, job, nxt, rb_per_item, ks_n, d);
+    nxt = load_item(p, job + gridDim.x, n_jobs, rb_per_item, ks_n);  // in flight during this job
     if (d.nsteps == 0) continue;
+    // the down epilogue's token and weight of each of the lane's fragment tokens, loaded now
+    int etok[NB][2];
+    float ew[NB][2];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        etok[nb][e] = -1;
+        ew[nb][e] = 0.f;
+        const int tk = 8 * nb + 2 * t + e;
+        if (!UP && tk < d.ntok) {
+          const int pos = p.pos[d.start + tk];
+          etok[nb][e] = pos / p.k;
+          ew[nb][e] = p.wflat[pos];
+        }
+      }
     const bool mine = UP ? 16 * warp < d.nrow : 32 * warp < d.nrow;  // this warp has rows in the job
     Scales S{};
     int par = 0;
@@ -692,8 +682,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int row = slot_row<UP>(d, p.I, 32 * warp + 16 * rt + g + 8 * hh);
-          S.row[rt][hh] = sa + (row < 0 ? 0 : scale_slot<UP>(d, p.I, row) * d.sst);
+          // scale-area row of the lane's row: up = gate rows at 0.., up rows at 128..; down = rows
+          const int m = UP ? rt * (kGemvJobRows / 2) + 16 * warp + g + 8 * hh : 32 * warp + 16 * rt + g + 8 * hh;
+          S.row[rt][hh] = sa + m * d.sst;
         }
     }
     float tot[2][NB][4];
@@ -767,10 +758,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
               static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
             }
           } else {
-            const int pos = p.pos[j];
-            const int tok = pos / p.k;
-            const float wv = p.wflat[pos];
-            float* arow = p.acc + (int64_t)tok * p.H + d.r0 + 32 * warp;
+            float* arow = p.acc + (int64_t)etok[nb][i & 1] * p.H + d.r0 + 32 * warp;
+            const float wv = ew[nb][i & 1];
             red_add_f32(arow + rrow, wv * tot[0][nb][i]);
             red_add_f32(arow + 16 + rrow, wv * tot[1][nb][i]);
           }
@@ -885,14 +874,14 @@ bool split_ok(const moeb200_layout* L, int nlay, int K, bool up, int ks) {
 // bytes of alignment slack); returns its bytes.
 int phase_smem(GemvParams& p, const moeb200_layout* lays, int nlay, int nb, int K, bool up, int ks) {
   int bst = 0, sst = 0;
-  const int kc = std::min(K, split_cols(K, ks));
   for (int i = 0; i < nlay; ++i) {
     bst = std::max(bst, gemv_b_stride(lays[i].wtype));
-    if (is_int_type(lays[i].wtype)) {
+    if (is_int_type(lays[i].wtype)) {  // a job's scale area holds whole scale rows
       const int gs = up ? lays[i].gs_up : lays[i].gs_dn;
-      sst = std::max(sst, gemv_s_stride((kc + gs - 1) / gs));
+      sst = std::max(sst, K / gs * 2);
     }
   }
+  (void)ks;
   p.b_stride = bst;
   p.b_rows = 8 * nb;
   p.stage_bytes = (kGemvWBytes + p.b_rows * bst + 1023) / 1024 * 1024;

@@ -74,13 +74,6 @@ __host__ __device__ inline int gemv_b_stride(int wtype) {
   return kStepBytes * 8 / gemv_wbits(wtype) * 2 + 16;
 }
 
-// Bytes of one row of a job's scale area: ngroups fp16 scales padded to an odd multiple of 16.
-__host__ __device__ inline int gemv_s_stride(int ngroups) {
-  int s = (ngroups * 2 + 15) / 16 * 16;
-  if ((s / 16) % 2 == 0) s += 16;
-  return s;
-}
-
 // host launchers (gemv.cu)
 // Plans split-K and the shared-memory geometry of the two GEMV phases, then launches gate/up and
 // down (with trace marks around them). nb: token blocks of 8 per item (1 or 2).

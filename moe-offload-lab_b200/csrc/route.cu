@@ -269,6 +269,53 @@ __device__ __forceinline__ int slot_of(int level, int P) {
   return level == 0 ? 0 : P - 1;
 }
 
+// One warp ranks the n pairs of a dispatch block in order, 32 at a time: each pair's rank among the
+// earlier pairs with the same key (expert*P + slot, and expert); cnt_k/cnt_e count the pairs so far.
+__device__ __forceinline__ void rank_in_order(int lane, int n, const int32_t* key_s, const int32_t* e_s,
+                                              int32_t* cnt_k, int32_t* cnt_e, int32_t* rank_k, int32_t* rank_e) {
+  for (int c = 0; c < n; c += 32) {
+    const int i = c + lane;
+    int key = -1, e = -1;
+    if (i < n) {
+      key = key_s[i];
+      e = e_s[i];
+    }
+    const uint32_t lt = (1u << lane) - 1u;
+    const uint32_t mk = __match_any_sync(0xffffffffu, key);
+    const uint32_t me = __match_any_sync(0xffffffffu, e);
+    int rk = 0, re = 0;
+    if (key >= 0) {
+      rk = cnt_k[key] + __popc(mk & lt);
+      re = cnt_e[e] + __popc(me & lt);
+    }
+    __syncwarp();
+    // the highest lane of each group publishes the new count
+    if (key >= 0 && (mk >> lane) == 1u) cnt_k[key] = rk + 1;
+    if (e >= 0 && (me >> lane) == 1u) cnt_e[e] = re + 1;
+    __syncwarp();
+    if (i < n) {
+      rank_k[i] = key >= 0 ? rk : -1;
+      rank_e[i] = re;
+    }
+  }
+}
+
+// Key (expert*P + slot) and expert of pair i, or -1 for a dropped pair (skipped, or routed to an
+// expert outside [e_lo, e_hi)); an index outside [0, E) sets the status word.
+__device__ __forceinline__ void pair_key(const DispatchParams& p, int i, int& key, int& e) {
+  key = -1;
+  e = -1;
+  const bool skipped = p.skip && p.skip[i];
+  const int64_t ev = p.idx[i];
+  if (ev < 0 || ev >= p.E) {
+    if (p.status) atomicExch(p.status, kDevBadIndex);
+  } else if (!skipped && ev >= p.e_lo && ev < p.e_hi) {
+    e = (int)ev;
+    const int lv = p.level ? p.level[i] : 0;
+    key = e * p.P + slot_of(lv, p.P);
+  }
+}
+
 // D1: one warp per block of kDispBlock pairs, processed in order 32 at a time. Each pair gets its
 // rank among the earlier pairs of the block with the same key (expert, and expert*P + slot).
 __global__ void __launch_bounds__(kDispLoadThreads) dispatch_count_kernel(DispatchParams p) {
@@ -286,46 +333,14 @@ __global__ void __launch_bounds__(kDispLoadThreads) dispatch_count_kernel(Dispat
   int32_t* key_s = sh + keys + p.E;   // [kDispBlock]
   int32_t* e_s = key_s + kDispBlock;  // [kDispBlock]
   for (int i = base + tid; i < end; i += blockDim.x) {
-    int key = -1, e = -1;
-    const bool skipped = p.skip && p.skip[i];
-    const int64_t ev = p.idx[i];
-    if (ev < 0 || ev >= p.E) {
-      if (p.status) atomicExch(p.status, kDevBadIndex);
-    } else if (!skipped && ev >= p.e_lo && ev < p.e_hi) {
-      e = (int)ev;
-      const int lv = p.level ? p.level[i] : 0;
-      key = e * p.P + slot_of(lv, p.P);
-    }
+    int key, e;
+    pair_key(p, i, key, e);
     key_s[i - base] = key;
     e_s[i - base] = e;
   }
   __syncthreads();
   if (tid >= 32) return;
-  for (int c = base; c < end; c += 32) {
-    const int i = c + lane;
-    int key = -1, e = -1;
-    if (i < end) {
-      key = key_s[i - base];
-      e = e_s[i - base];
-    }
-    const uint32_t lt = (1u << lane) - 1u;
-    const uint32_t mk = __match_any_sync(0xffffffffu, key);
-    const uint32_t me = __match_any_sync(0xffffffffu, e);
-    int rk = 0, re = 0;
-    if (key >= 0) {
-      rk = cnt_k[key] + __popc(mk & lt);
-      re = cnt_e[e] + __popc(me & lt);
-    }
-    __syncwarp();
-    // the highest lane of each group publishes the new count
-    if (key >= 0 && (mk >> lane) == 1u) cnt_k[key] = rk + 1;
-    if (e >= 0 && (me >> lane) == 1u) cnt_e[e] = re + 1;
-    __syncwarp();
-    if (i < end) {
-      p.rank_k[i] = key >= 0 ? rk : -1;
-      p.rank_e[i] = re;
-    }
-  }
+  rank_in_order(lane, end - base, key_s, e_s, cnt_k, cnt_e, p.rank_k + base, p.rank_e + base);
   __syncwarp();
   for (int i = lane; i < keys; i += 32) p.blk_k[(int64_t)b * keys + i] = cnt_k[i];
   for (int i = lane; i < p.E; i += 32) p.blk_e[(int64_t)b * p.E + i] = cnt_e[i];
@@ -368,48 +383,59 @@ __device__ int32_t block_exclusive_scan(int32_t (&v)[PER], int32_t* sh_warp) {
   return total;
 }
 
-// D2: one block of 1024 threads. Turns per-block counts into per-(block, key) prefixes, writes the
-// per-key counts and first positions, and builds the work items.
-__global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
-  __shared__ int32_t sh_warp[32];
+// Per-key totals, first positions (exclusive scans) and work items, by one block of 1024 threads.
+// With cnt_k/cnt_e (a single dispatch block whose counts are in shared memory) the totals are read
+// there and the first positions are also left in offk_s/offe_s; otherwise the per-block counts in
+// global memory are turned into per-(block, key) prefixes on the way.
+__device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const int32_t* cnt_e, int32_t* offk_s,
+                            int32_t* offe_s, int32_t* sh_warp) {
   const int keys = p.E * p.P;
   const int tid = threadIdx.x;
   if (tid == 0 && p.miss) *p.miss = 0;
   __syncthreads();
   constexpr int PER = kMaxKeys / 1024;
-  // per key: exclusive prefix over the dispatch blocks (8 independent loads in flight), totals
   int32_t tot_k[PER], tot_e[PER], nit[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int key = tid * PER + i;
     int32_t run = 0;
-    if (key < keys)
-      for (int b0 = 0; b0 < p.nblk; b0 += 8) {
-        int32_t cv[8];
+    if (key < keys) {
+      if (cnt_k) {
+        run = cnt_k[key];
+      } else {
+        for (int b0 = 0; b0 < p.nblk; b0 += 8) {  // 8 independent loads in flight
+          int32_t cv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_k[(int64_t)(b0 + u) * keys + key] : 0;
+          for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_k[(int64_t)(b0 + u) * keys + key] : 0;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (b0 + u < p.nblk) {
-            p.blk_k[(int64_t)(b0 + u) * keys + key] = run;
-            run += cv[u];
-          }
+          for (int u = 0; u < 8; ++u)
+            if (b0 + u < p.nblk) {
+              p.blk_k[(int64_t)(b0 + u) * keys + key] = run;
+              run += cv[u];
+            }
+        }
       }
+    }
     tot_k[i] = key < keys ? run : 0;
     int32_t rune = 0;
     const int e = tid * PER + i;
-    if (e < p.E)
-      for (int b0 = 0; b0 < p.nblk; b0 += 8) {
-        int32_t cv[8];
+    if (e < p.E) {
+      if (cnt_e) {
+        rune = cnt_e[e];
+      } else {
+        for (int b0 = 0; b0 < p.nblk; b0 += 8) {
+          int32_t cv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_e[(int64_t)(b0 + u) * p.E + e] : 0;
+          for (int u = 0; u < 8; ++u) cv[u] = b0 + u < p.nblk ? p.blk_e[(int64_t)(b0 + u) * p.E + e] : 0;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (b0 + u < p.nblk) {
-            p.blk_e[(int64_t)(b0 + u) * p.E + e] = rune;
-            rune += cv[u];
-          }
+          for (int u = 0; u < 8; ++u)
+            if (b0 + u < p.nblk) {
+              p.blk_e[(int64_t)(b0 + u) * p.E + e] = rune;
+              rune += cv[u];
+            }
+        }
       }
+    }
     tot_e[i] = e < p.E ? rune : 0;
     // work items: only for keys whose expert record is resident
     int32_t ni = 0;
@@ -437,6 +463,7 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
     if (key < keys) {
       p.counts_k[key] = tot_k[i];
       p.offs_k[key] = off_k[i];
+      if (offk_s) offk_s[key] = off_k[i];
       if (nit[i] > 0) {
         const int ex = key / p.P, sl = key % p.P;
         const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
@@ -459,11 +486,51 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
     if (e < p.E) {
       p.counts_e[e] = tot_e[i];
       p.offs_e[e] = off_e[i];
+      if (offe_s) offe_s[e] = off_e[i];
     }
   }
   if (tid == 0) {
     if (p.n_items) *p.n_items = n_items;
     if (p.n_kept) *p.n_kept = n_kept;
+  }
+}
+
+// D2: one block of 1024 threads over the per-block counts of D1.
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
+  __shared__ int32_t sh_warp[32];
+  finish_keys(p, nullptr, nullptr, nullptr, nullptr, sh_warp);
+}
+
+// D1+D2+D3 in one block of 1024 threads when all pairs fit one dispatch block (T*k <= kDispBlock):
+// keys, in-order ranks (one warp), totals/positions/items, scatter -- counts and ranks stay in
+// shared memory.
+__global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) {
+  extern __shared__ int32_t sh[];
+  __shared__ int32_t sh_warp[32];
+  const int keys = p.E * p.P;
+  int32_t* cnt_k = sh;                 // [keys]
+  int32_t* cnt_e = cnt_k + keys;       // [E]
+  int32_t* offk = cnt_e + p.E;         // [keys]
+  int32_t* offe = offk + keys;         // [E]
+  int32_t* key_s = offe + p.E;         // [kDispBlock]
+  int32_t* e_s = key_s + kDispBlock;   // [kDispBlock]
+  int32_t* rk_s = e_s + kDispBlock;    // [kDispBlock]
+  int32_t* re_s = rk_s + kDispBlock;   // [kDispBlock]
+  const int tid = threadIdx.x;
+  const int n = p.T * p.k;
+  for (int i = tid; i < keys + p.E; i += blockDim.x) sh[i] = 0;
+  if (tid < n) pair_key(p, tid, key_s[tid], e_s[tid]);
+  __syncthreads();
+  if (tid < 32) rank_in_order(tid, n, key_s, e_s, cnt_k, cnt_e, rk_s, re_s);
+  __syncthreads();
+  finish_keys(p, cnt_k, cnt_e, offk, offe, sh_warp);
+  __syncthreads();
+  if (tid < n) {
+    const int key = key_s[tid];
+    if (key >= 0) {
+      p.pos_k[offk[key] + rk_s[tid]] = tid;
+      p.pos_e[offe[e_s[tid]] + re_s[tid]] = tid;
+    }
   }
 }
 
@@ -527,6 +594,13 @@ cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, ui
 
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
   const int keys = p.E * p.P;
+  if (p.nblk == 1) {
+    const size_t shf = (size_t)(2 * (keys + p.E) + 4 * kDispBlock) * sizeof(int32_t);
+    cudaError_t e = cudaFuncSetAttribute(dispatch_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shf);
+    if (e != cudaSuccess) return e;
+    dispatch_fused_kernel<<<1, 1024, shf, s>>>(p);
+    return cudaGetLastError();
+  }
   const size_t sh = (size_t)(keys + p.E + 2 * kDispBlock) * sizeof(int32_t);
   dispatch_count_kernel<<<p.nblk, kDispLoadThreads, sh, s>>>(p);
   cudaError_t e = cudaGetLastError();
