@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
                     help="--ncu mode: every pair at the most precise (hi) or least precise (lo) record")
     ap.add_argument("--extra", default="c0,c2,c3,c3p,c4", help="single-layer configs measured beside the headline")
@@ -168,7 +170,7 @@ class Clocks:
 class Stack:
     """The 16-layer MoE stack of config 1 with every record resident on the device."""
 
-    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0, ep: bool = False):
+    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0, ep: bool = False, exchange: str = "p2p"):
         import moeb200
         from moeb200 import format as F
         from moeb200 import ops
@@ -189,7 +191,7 @@ class Stack:
             from moeb200.ep import ExpertParallel
 
             self.world = dist.get_world_size()
-            self.ep = ExpertParallel(self.rt)
+            self.ep = ExpertParallel(self.rt, exchange=exchange)
         self.e_lo, self.e_hi = (self.ep.e_lo, self.ep.e_hi) if self.ep else (0, E)
         g = torch.Generator(device=dev).manual_seed(seed)
         self.wr = []
@@ -588,7 +590,7 @@ def main():
     from moeb200 import ops as _ops
 
     _ops.set_path(args.path)
-    stack = Stack(cfg, dev, seed=0, ep=world > 1)
+    stack = Stack(cfg, dev, seed=0, ep=world > 1, exchange=args.exchange)
     T = args.batch if not args.ncu or args.config == "c1" else cfg["T"]
     if args.ncu:
         step = stack.make_device_step(T)
@@ -697,8 +699,9 @@ def main():
             "config": {"workload": f"c1 OLMoE-1B-7B 16-layer MoE stack decode, T={T}/GPU, "
                                    "fp16/int4 by router prob >= 0.1, all experts resident",
                        "global_batch": T * world, "layers": L, "experts": CFG1["E"], "top_k": CFG1["k"],
-                       "hidden": H, "inter": CFG1["I"], "parallelism": f"ep{world} (experts in contiguous blocks, NCCL all_gather dispatch + "
-                                      "all_to_all combine)" if world > 1 else "1gpu",
+                       "hidden": H, "inter": CFG1["I"], "parallelism": (f"ep{world} (experts in contiguous blocks; dispatch/combine " + (
+                           "through peer memory over NVLink: CUDA IPC buffers, flag handshakes)"
+                           if args.exchange == "p2p" else "by NCCL all_gather + all_to_all)")) if world > 1 else "1gpu",
                        "l2": "no flush: each step streams ~%.1f GB of records (> 126 MB L2)" % (
                            (rb["up"] + rb["down"]) / 1e9),
                        "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks"},
@@ -722,6 +725,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        if stack.ep is not None:
+            stack.ep.close()
         dist.destroy_process_group()
 
 

@@ -198,6 +198,34 @@ int moeb200_ep_pack(const void* x, const int64_t* idx, const float* w, const uin
                     int32_t T, int32_t H, int32_t k, int32_t act_type, void* rows, void* stream);
 int moeb200_ep_unpack(const void* rows, int32_t n, int32_t H, int32_t k, int32_t act_type, void* x, int64_t* idx,
                       float* w, uint8_t* level, uint8_t* skip, void* stream);
+/* ---- peer-memory exchange (expert parallelism without collectives) ------------------------------
+ * Buffers a rank's peers map with CUDA IPC: moeb200_peer_alloc returns zeroed device memory and its
+ * 64-byte IPC handle; a peer maps it with moeb200_peer_open (and unmaps with moeb200_peer_close).
+ * A peer group describes, for every rank s < G, the device addresses (as mapped in this process) of
+ * rank s's packed exchange rows [T, moeb200_ep_row_bytes], its fp32 partial sums [G*T, H] and its
+ * flags int32 [2][G]; epoch is this rank's call counter and status its status word (device int32,
+ * zero at setup). Per layer: moeb200_ep_pack into the own rows, moeb200_ep_signal(0), moeb200_ep_gather
+ * (waits for every rank's rows, reads them over NVLink, unpacks to [G*T] arrays), the owned experts'
+ * moeb200_experts_forward_part into the own partial sums, moeb200_ep_signal(1),
+ * moeb200_ep_combine_peers (waits for every rank's partial sums, adds this rank's tokens' rows in
+ * rank order, casts once). Waits are bounded: on timeout the status word is set. Every rank must run
+ * the same sequence of calls with the same T. */
+typedef struct {
+  int32_t G, rank, T, H, k, _pad;
+  const int64_t* rows;   /* [G] device array */
+  const int64_t* parts;  /* [G] device array */
+  const int64_t* flags;  /* [G] device array */
+  int32_t* epoch;        /* [1] device */
+  int32_t* status;       /* [1] device */
+} moeb200_peer_group;
+int moeb200_peer_alloc(size_t bytes, void** ptr, void* handle);
+int moeb200_peer_open(const void* handle, void** ptr);
+int moeb200_peer_close(void* ptr);
+int moeb200_peer_free(void* ptr);
+int moeb200_ep_signal(const moeb200_peer_group* group, int32_t which, void* stream);
+int moeb200_ep_gather(const moeb200_peer_group* group, int32_t act_type, void* x, int64_t* idx, float* w,
+                      uint8_t* level, uint8_t* skip, void* stream);
+int moeb200_ep_combine_peers(const moeb200_peer_group* group, int32_t act_type, void* out, int32_t add, void* stream);
 
 /* ---- shared expert ---------------------------------------------------------------------------
  * Replaces the shared-expert branch of Qwen3NextSparseMoeBlock.forward

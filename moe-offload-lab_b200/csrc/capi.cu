@@ -126,7 +126,7 @@ int check_shapes(int H, int I) {
 // Split-K planning of the GEMV phases: a split covers a multiple of kSplitCols input columns (a
 // multiple of every group size and pipeline step), and is only used for small pair counts (the
 // pre-activation buffer is sized for kMaxSplitPairs pairs).
-constexpr int kMaxSplitPairs = 256;
+constexpr int kMaxSplitPairs = 2048;
 
 
 struct ForwardWs {
@@ -163,7 +163,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
   w.pre = c.take<float>((size_t)std::min(n, kMaxSplitPairs) * 2 * I);
   w.cnt = c.take<int32_t>((size_t)std::min(n, kMaxSplitPairs) * (I / 16));
-  w.tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
+  w.tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
   return w;
@@ -186,9 +186,12 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
     const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>(sms, tiles));
     const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>(sms, tiles_dn));
     CUDA_TRY(trace_mark(0, s));
-    CUDA_TRY(launch_gemm_up(gp, act, grid_up, s));
+    cudaError_t e = launch_gemm_up(gp, lays, nlay, act, n_pairs, grid_up, s);
+    if (e == cudaErrorInvalidConfiguration)
+      return fail(MOEB200_ERR_UNSUPPORTED, "GEMM: the record layouts need more shared memory than a CTA has");
+    CUDA_TRY(e);
     CUDA_TRY(trace_mark(1, s));
-    CUDA_TRY(launch_gemm_down(gp, act, grid_dn, s));
+    CUDA_TRY(launch_gemm_down(gp, lays, nlay, act, n_pairs, grid_dn, s));
     CUDA_TRY(trace_mark(2, s));
     if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
     return MOEB200_OK;
@@ -482,7 +485,7 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<uint8_t>((size_t)n * layout->inter * 2);
   c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * layout->inter);
   c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (layout->inter / 16));
-  c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
+  c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   c.take<float>((size_t)layout->hidden);
   return c.off;
 }
@@ -508,7 +511,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
   float* pre = c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * I);
   int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (I / 16));
-  uint8_t* tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
+  uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)H);
   table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
   CUDA_TRY(cudaGetLastError());
@@ -672,7 +675,7 @@ size_t moeb200_shared_expert_workspace(const moeb200_layout* layout, int32_t T) 
   c.take<uint8_t>((size_t)T * layout->inter * 2);
   c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * layout->inter);
   c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (layout->inter / 16));
-  c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
+  c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   c.take<float>((size_t)T * layout->hidden);
   return c.off;
 }
@@ -708,7 +711,7 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   uint8_t* hbuf = c.take<uint8_t>((size_t)T * I * 2);
   float* pre = c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * I);
   int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (I / 16));
-  uint8_t* tmaps = c.take<uint8_t>((size_t)4 * kGemvMaxGrid * 128);
+  uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)T * H);
   const LayoutOffs lo{layout->off_gu_q, is_int(layout->wtype) ? layout->off_gu_s : 0, layout->off_dn_q,
                       is_int(layout->wtype) ? layout->off_dn_s : 0};

@@ -8,19 +8,32 @@
 //   down : D[r, j] = sum_c Wd[r, c] * h[j, c];  acc[tok_j, r] += w_j * D[r, j]   (fp32 reduction = combine)
 //
 // A tile is (work item, 128 weight rows); an item holds up to 128 routed pairs of one (expert,
-// precision), so N = pairs rounded up to 16. Roles per CTA (one CTA per SM, persistent):
-//   warps 0-7  dequantise the int4/int8/float record rows of each 64-column k-block into bf16/fp16
-//              in 128-byte-swizzled K-major shared tiles, with the same rounding as moelab's
-//              materialize in the activation dtype: (q - 8) exact, times the fp16 scale converted to
-//              the activation type, one rounding;
-//   warp 12    gathers the N token rows (or h rows) of each k-block with cp.async into the B tile;
+// precision), so N = pairs rounded up to 16. One CTA per SM works through its tiles with five roles
+// connected by shared-memory rings and mbarriers:
+//   warp 14    (TMA producer) points a tensor map at each tile's record (tensormap.replace on the
+//              device) and streams the tile's raw weight bytes through the RAW ring -- one unit is
+//              128 bytes of each of the 128 (up: 2 x 128) rows, a 128-byte-swizzled TMA box -- and
+//              the tile's whole scale rows into a double-buffered scale area (bulk copies). The ring
+//              runs ahead across tile boundaries, so DRAM latency is hidden by the ring depth;
+//   warps 0-7  dequantise each 64-column k-block from the raw ring into the A ring: 128-byte-swizzled
+//              K-major bf16/fp16 tiles, with the rounding of moelab's materialize in the activation
+//              dtype ((q - 8) exact, times the fp16 scale converted to the activation type, one
+//              rounding; float records converted, or copied when the types agree);
+//   warp 12    fills the B ring: the N token rows of the k-block gathered with cp.async (up), or one
+//              TMA box of the item's contiguous h rows (down);
 //   warp 13    allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accumulate) from one thread,
-//              committing each stage back to the producers and each finished tile to the epilogue;
-//   warps 8-11 read the accumulators with tcgen05.ld (double-buffered TMEM) and run the epilogue.
-// Every wait is bounded (status word + early exit), the TMEM is freed on every path.
+//              committing each A and B stage back to its producer and each finished tile to the
+//              epilogue (two TMEM accumulator buffers);
+//   warps 8-11 read the accumulators with tcgen05.ld and run the epilogue (up: SwiGLU into h; down:
+//              the router-weighted fp32 reduction into acc, token rows and weights of the tile held
+//              in registers and broadcast with shuffles).
+// Every wait is bounded (status word + early exit), copies in flight are waited for before exit,
+// and the TMEM is freed on every path.
+#include <algorithm>
 #include <type_traits>
 
 #include "gemv.cuh"
+#include "tma.cuh"
 
 namespace moeb200 {
 
@@ -29,21 +42,40 @@ namespace {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // k-block: one 128-byte swizzle row of 16-bit values
 constexpr int NMAX = 128;        // max tokens per item (MMA N)
-constexpr int kThreads = 14 * 32;
 constexpr int kDqWarps = 8;
 constexpr int kEpiWarp0 = 8;
 constexpr int kLoadWarp = 12;
 constexpr int kMmaWarp = 13;
-constexpr int kTileBytes = BM * 128;  // one 128 x 64 16-bit tile = 16 KB (also the B tile)
+constexpr int kTmaWarp = 14;
+constexpr int kThreads = 15 * 32;
+constexpr int kTileBytes = BM * 128;  // one 128 x 64 16-bit operand tile = 128 rows x 128 raw bytes = 16 KB
+constexpr int kMaxSmem = 227 * 1024;
 
-template <bool UP>
-struct Geo {
-  static constexpr int NA = UP ? 2 : 1;               // A tiles per stage (gate + up)
-  static constexpr int STAGES = UP ? 4 : 6;
-  static constexpr int STAGE_BYTES = (NA + 1) * kTileBytes;
-  static constexpr int TMEM_COLS = UP ? 512 : 256;    // two accumulator buffers
-  static constexpr int BUF_COLS = UP ? 256 : 128;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Tensor maps of a launch: per precision slot the phase's weight field (uint8 [rows][row bytes],
+// 128 x 128 boxes, retargeted per tile), and for the down phase h [pairs][I] (64 x 128 boxes).
+struct alignas(64) TcMaps {
+  CUtensorMap w[4];
+  CUtensorMap h;
+};
+
+// Ring depths and shared-memory offsets of a launch (planned on the host).
+struct TcGeo {
+  int32_t a_st, b_st, r_st;  // A (dequantised), B (tokens / h) and RAW ring depths
+  int32_t lag;               // up: cp.async groups the B loader keeps in flight
+  int32_t tmap_ring;         // tensor-map slots the producer cycles through (r_st + 1)
+  uint32_t a_off, b_off, r_off, s_off, d_off, bar_off;
+  uint32_t s_bytes;          // one scale buffer
+};
+
+// A ring cursor: slot and phase parity, advanced in the order every party walks the ring.
+struct Ring {
+  uint32_t slot = 0, phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++slot == (uint32_t)n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
 };
 
 // ---- tcgen05 / proxy primitives -----------------------------------------------------------------
@@ -101,10 +133,25 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// wait until at most n (0..4) of this thread's cp.async groups are pending
+__device__ __forceinline__ void cp_async_wait_n(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    default: cp_async_wait<4>(); break;
+  }
+}
 
-__device__ __forceinline__ uint4 ldg16(const void* p) {
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint16_t lds_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
   return v;
 }
 
@@ -177,25 +224,42 @@ __device__ __forceinline__ void dq_int8_chunk(uint32_t w0, uint32_t w1, uint16_t
   }
 }
 
-// ---- kernel -------------------------------------------------------------------------------------------
-struct TcTile;
-template <typename AT, bool UP, int STAGES, int STAGE_BYTES>
-__device__ __forceinline__ bool dq_int4_tile(const TcTile& d, int nkb, int tile_i, int row, int c0, uint32_t& st,
-                                             uint32_t sbase, uint64_t* empty, uint64_t* full_a, int32_t* status,
-                                             int lane);
+// 8 16-bit record values (one 16-byte vector) in the activation type
+template <typename AT, int WT>
+__device__ __forceinline__ void cvt_f16x8(const uint4& v, uint32_t (&o)[4]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  constexpr bool same = (WT == MOEB200_F16) == std::is_same<AT, __half>::value;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (same) {
+      o[i] = w[i];
+    } else {
+      float lo, hi;
+      if constexpr (WT == MOEB200_F16) {
+        lo = __half2float(__ushort_as_half((uint16_t)(w[i] & 0xffff)));
+        hi = __half2float(__ushort_as_half((uint16_t)(w[i] >> 16)));
+      } else {
+        lo = __uint_as_float(w[i] << 16);
+        hi = __uint_as_float(w[i] & 0xffff0000u);
+      }
+      o[i] = Dq<AT>::pack_f32(lo, hi);
+    }
+  }
+}
 
+// ---- tiles ----------------------------------------------------------------------------------------
 struct TcTile {
-  int item, r0, ntok, n, start, slot;
-  const uint8_t* q[2];  // first weight row of each A tile
-  const uint8_t* s[2];  // first scale row of each A tile (integer records)
-  int64_t rstride;
-  int sstride, gs, wtype;
+  int item, r0, ntok, n, start, slot, wtype, gs, units, sstride;
+  const uint8_t* q;  // weight field of the phase (float records: the matrix itself)
+  const uint8_t* s;  // scale field (integer records)
 };
+
+__device__ __forceinline__ bool is_int_w(int wt) { return wt == MOEB200_I4 || wt == MOEB200_I8; }
 
 template <bool UP>
 __device__ __forceinline__ void tc_describe(const GemvParams& p, int tile, int rb_per_item, TcTile& d) {
   d.item = tile / rb_per_item;
-  const int rb = tile % rb_per_item;
+  const int rb = tile - d.item * rb_per_item;
   const Item it = p.items[d.item];
   const LayoutDev L = p.lay[it.slot];
   d.slot = it.slot;
@@ -205,231 +269,204 @@ __device__ __forceinline__ void tc_describe(const GemvParams& p, int tile, int r
   d.r0 = rb * BM;
   d.wtype = L.wtype;
   const int K = UP ? p.H : p.I;
-  const int wb = L.wtype == MOEB200_I4 ? 4 : L.wtype == MOEB200_I8 ? 8 : L.wtype == MOEB200_F32 ? 32 : 16;
-  d.rstride = (int64_t)K * wb / 8;
+  d.units = (K * gemv_wbits(L.wtype) / 8 + 127) >> 7;
   d.gs = UP ? L.gs_up : L.gs_dn;
-  const bool isint = L.wtype == MOEB200_I4 || L.wtype == MOEB200_I8;
-  d.sstride = isint ? (K / d.gs) * 2 : 0;
-  const uint8_t* q = reinterpret_cast<const uint8_t*>(UP ? it.p_guq : it.p_dnq);
-  const uint8_t* s = reinterpret_cast<const uint8_t*>(UP ? it.p_gus : it.p_dns);
-  d.q[0] = q + (int64_t)d.r0 * d.rstride;
-  d.s[0] = s + (int64_t)d.r0 * d.sstride;
-  if (UP) {
-    d.q[1] = q + (int64_t)(p.I + d.r0) * d.rstride;
-    d.s[1] = s + (int64_t)(p.I + d.r0) * d.sstride;
-  } else {
-    d.q[1] = d.q[0];
-    d.s[1] = d.s[0];
-  }
+  d.sstride = is_int_w(L.wtype) ? (K / d.gs) * 2 : 0;
+  d.q = reinterpret_cast<const uint8_t*>(UP ? it.p_guq : it.p_dnq);
+  d.s = reinterpret_cast<const uint8_t*>(UP ? it.p_gus : it.p_dns);
 }
 
-// Raw source bytes of one thread's slice of a k-block (up to 128 bytes = 8 x 16).
-struct Raw {
-  uint4 v[8];
+// Shared-memory rings of a CTA (shared-window addresses and barrier arrays).
+struct Rings {
+  uint32_t a, b, r, s, d;  // ring bases, scale areas, tensor-map staging
+  uint64_t *afull, *aempty, *bfull, *bempty, *rfull, *rempty, *sfull, *sempty, *accf, *acce, *done;
+  uint32_t* tmem_slot;
 };
 
-// UP: thread = one full row (8 chunks) of tile (warp / 4). DOWN: thread = half a row (4 chunks).
-template <bool UP>
-__device__ __forceinline__ void dq_coords(int dq_tid, int& tile, int& row, int& c0, int& nch) {
-  if (UP) {
-    tile = dq_tid >> 7;
-    row = dq_tid & 127;
-    c0 = 0;
-    nch = 8;
-  } else {
-    tile = 0;
-    row = dq_tid >> 1;
-    c0 = (dq_tid & 1) * 4;
-    nch = 4;
-  }
-}
-
-template <bool UP>
-__device__ __forceinline__ void dq_load(const TcTile& d, int kb, int tile, int row, int c0, Raw& raw) {
-  const uint8_t* rowp = d.q[tile] + (int64_t)row * d.rstride;
-  constexpr int NCH = UP ? 8 : 4;
-  switch (d.wtype) {
-    case MOEB200_I4: {  // 4 bytes per chunk
-      const uint8_t* src = rowp + kb * 32 + c0 * 4;
-#pragma unroll
-      for (int i = 0; i < NCH / 4; ++i) raw.v[i] = ldg16(src + 16 * i);
-      break;
+// ---- dequantisation of one tile: RAW ring -> A ring ------------------------------------------------
+// Thread (part, row, c0): up: part 0/1 = gate/up rows, every 8-column chunk of its row; down: two
+// threads per row, chunks c0..c0+3. Units of the RAW ring are waited in order; a k-block lies in the
+// last unit waited (16-bit and narrower records) or in the last two (fp32 records).
+template <typename AT, bool UP, int WT>
+__device__ __forceinline__ bool dq_tile(const TcTile& d, const TcGeo& g, const Rings& R, int nkb, int part, int row,
+                                     int c0, uint32_t sarea, Ring& ar, Ring& rw, Ring& rr, int32_t* status,
+                                     int lane) {
+  constexpr int NA = UP ? 2 : 1;
+  constexpr int WB = WT == MOEB200_I4 ? 4 : WT == MOEB200_I8 ? 8 : WT == MOEB200_F32 ? 32 : 16;
+  constexpr int BPK = BK * WB / 8;  // raw bytes of a row per k-block
+  constexpr int NCH = UP ? 8 : 4;   // 8-column chunks per thread and k-block
+  constexpr int CB = WB;            // raw bytes of a chunk
+  constexpr int NV = NCH * CB / 16; // 16-byte raw vectors per thread and k-block
+  constexpr bool INT = WT == MOEB200_I4 || WT == MOEB200_I8;
+  const uint32_t rslot = NA * kTileBytes;
+  const uint32_t rrow = R.r + part * kTileBytes + row * 128;
+  const uint32_t abase = R.a + part * kTileBytes;
+  const int rsw = row & 7;
+  const uint32_t srow = sarea + (part * BM + row) * d.sstride;
+  const bool one_scale = INT && (d.gs % BK == 0);
+  int waited = 0, released = 0;
+  uint32_t cur = 0, prev = 0;  // RAW slot offsets of the last two units waited
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int lo = kb * BPK;
+    const int need = min(d.units, (lo + BPK + 127) >> 7);
+    while (waited < need) {
+      if (!mbar_wait(&R.rfull[rw.slot], rw.phase, status)) return false;
+      prev = cur;
+      cur = rw.slot * rslot;
+      rw.next(g.r_st);
+      ++waited;
     }
-    case MOEB200_I8: {  // 8 bytes per chunk
-      const uint8_t* src = rowp + kb * 64 + c0 * 8;
-#pragma unroll
-      for (int i = 0; i < NCH / 2; ++i) raw.v[i] = ldg16(src + 16 * i);
-      break;
+    if (!mbar_wait(&R.aempty[ar.slot], ar.phase ^ 1u, status)) return false;
+    const uint32_t atile = abase + ar.slot * (NA * kTileBytes);
+    uint32_t s2 = 0;
+    uint16_t s16 = 0;
+    if constexpr (INT) {
+      if (one_scale) {
+        s16 = lds_u16(srow + ((kb * BK) / d.gs) * 2);
+        s2 = scale2<AT>(s16);
+      }
     }
-    case MOEB200_F32: {  // 32 bytes per chunk: loaded and converted in dq_store
-      break;
-    }
-    default: {  // 16-bit floats: 16 bytes per chunk
-      const uint8_t* src = rowp + kb * 128 + c0 * 16;
+    auto raw = [&](int o) {  // 16 bytes at byte o of the row
+      const uint32_t ub = ((o >> 7) == waited - 1) ? cur : prev;
+      return lds128(rrow + ub + ((((o & 127) >> 4) ^ rsw) << 4));
+    };
+    if constexpr (WT == MOEB200_F32) {
 #pragma unroll
-      for (int i = 0; i < NCH; ++i) raw.v[i] = ldg16(src + 16 * i);
-      break;
-    }
-  }
-}
-
-template <typename AT, bool UP>
-__device__ __forceinline__ void dq_store(const TcTile& d, int kb, int tile, int row, int c0, const Raw& raw,
-                                         uint32_t atile) {
-  constexpr int NCH = UP ? 8 : 4;
-  const bool isint = d.wtype == MOEB200_I4 || d.wtype == MOEB200_I8;
-  const uint16_t* srow = isint ? reinterpret_cast<const uint16_t*>(d.s[tile] + (int64_t)row * d.sstride) : nullptr;
-#pragma unroll
-  for (int ci = 0; ci < NCH; ++ci) {
-    const int c = c0 + ci;
-    uint32_t o[4];
-    if (d.wtype == MOEB200_I4) {
-      const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw.v[ci / 4]);
-      const uint16_t s16 = __ldg(srow + (kb * BK + c * 8) / d.gs);
-      dq_int4_chunk<AT>(wv[ci % 4], scale2<AT>(s16), o);
-    } else if (d.wtype == MOEB200_I8) {
-      const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw.v[ci / 2]);
-      const uint16_t s16 = __ldg(srow + (kb * BK + c * 8) / d.gs);
-      dq_int8_chunk<AT>(wv[(ci % 2) * 2], wv[(ci % 2) * 2 + 1], s16, o);
-    } else if (d.wtype == MOEB200_F32) {
-      const float* f = reinterpret_cast<const float*>(d.q[tile] + (int64_t)row * d.rstride) + kb * BK + c * 8;
-      const float4 a = __ldg(reinterpret_cast<const float4*>(f));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(f + 4));
-      o[0] = Dq<AT>::pack_f32(a.x, a.y);
-      o[1] = Dq<AT>::pack_f32(a.z, a.w);
-      o[2] = Dq<AT>::pack_f32(b.x, b.y);
-      o[3] = Dq<AT>::pack_f32(b.z, b.w);
+      for (int ci = 0; ci < NCH; ++ci) {
+        const int c = c0 + ci;
+        const uint4 v0 = raw(lo + c * CB), v1 = raw(lo + c * CB + 16);
+        sts16(swz(atile, row, c), Dq<AT>::pack_f32(__uint_as_float(v0.x), __uint_as_float(v0.y)),
+              Dq<AT>::pack_f32(__uint_as_float(v0.z), __uint_as_float(v0.w)),
+              Dq<AT>::pack_f32(__uint_as_float(v1.x), __uint_as_float(v1.y)),
+              Dq<AT>::pack_f32(__uint_as_float(v1.z), __uint_as_float(v1.w)));
+      }
     } else {
-      const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw.v[ci]);
-      const bool same = (d.wtype == MOEB200_F16) == std::is_same<AT, __half>::value;
-      if (same) {
-        o[0] = wv[0];
-        o[1] = wv[1];
-        o[2] = wv[2];
-        o[3] = wv[3];
-      } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float lo, hi;
-          if (d.wtype == MOEB200_F16) {
-            lo = __half2float(__ushort_as_half((uint16_t)(wv[i] & 0xffff)));
-            hi = __half2float(__ushort_as_half((uint16_t)(wv[i] >> 16)));
-          } else {
-            lo = __uint_as_float(wv[i] << 16);
-            hi = __uint_as_float(wv[i] & 0xffff0000u);
+      for (int vi = 0; vi < NV; ++vi) {
+        const uint4 v = raw(lo + c0 * CB + 16 * vi);
+        if constexpr (WT == MOEB200_I4) {
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int c = c0 + vi * 4 + q;
+            if (!one_scale) s2 = scale2<AT>(lds_u16(srow + ((kb * BK + c * 8) / d.gs) * 2));
+            uint32_t out[4];
+            dq_int4_chunk<AT>(w[q], s2, out);
+            sts16(swz(atile, row, c), out[0], out[1], out[2], out[3]);
           }
-          o[i] = Dq<AT>::pack_f32(lo, hi);
+        } else if constexpr (WT == MOEB200_I8) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int c = c0 + vi * 2 + q;
+            if (!one_scale) s16 = lds_u16(srow + ((kb * BK + c * 8) / d.gs) * 2);
+            uint32_t out[4];
+            dq_int8_chunk<AT>(q ? v.z : v.x, q ? v.w : v.y, s16, out);
+            sts16(swz(atile, row, c), out[0], out[1], out[2], out[3]);
+          }
+        } else {
+          uint32_t out[4];
+          cvt_f16x8<AT, WT>(v, out);
+          sts16(swz(atile, row, c0 + vi), out[0], out[1], out[2], out[3]);
         }
       }
     }
-    sts16(swz(atile, row, c), o[0], o[1], o[2], o[3]);
-  }
-}
-
-// int4 records whose groups span whole 64-column k-blocks: the thread's raw bytes are loaded two to
-// three k-blocks ahead of their dequantisation, one scale per row per k-block.
-template <typename AT, bool UP, int STAGES, int STAGE_BYTES>
-__device__ __forceinline__ bool dq_int4_tile(const TcTile& d, int nkb, int tile_i, int row, int c0, uint32_t& st,
-                                             uint32_t sbase, uint64_t* empty, uint64_t* full_a, int32_t* status,
-                                             int lane) {
-  constexpr int NV = UP ? 2 : 1;   // 16-byte vectors per k-block (32 or 16 raw bytes)
-  constexpr int NCH = UP ? 8 : 4;  // 8-column chunks per k-block
-  const uint8_t* rowp = d.q[tile_i] + (int64_t)row * d.rstride + c0 * 4;
-  const uint16_t* srow = reinterpret_cast<const uint16_t*>(d.s[tile_i] + (int64_t)row * d.sstride);
-  const int kpg = d.gs / BK;  // k-blocks per scale group
-  constexpr int MB = 2;       // k-blocks per prefetch macro block
-  uint4 raw[MB][NV], nraw[MB][NV];
-  uint16_t sc[MB], nsc[MB];
-#pragma unroll
-  for (int u = 0; u < MB; ++u) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) raw[u][i] = ldg16(rowp + u * 32 + i * 16);
-    sc[u] = __ldg(srow + u / kpg);
-  }
-  for (int kb0 = 0; kb0 < nkb; kb0 += MB) {
-    const bool more = kb0 + MB < nkb;
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < MB; ++u) {
-#pragma unroll
-        for (int i = 0; i < NV; ++i) nraw[u][i] = ldg16(rowp + (kb0 + MB + u) * 32 + i * 16);
-        nsc[u] = __ldg(srow + (kb0 + MB + u) / kpg);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < MB; ++u, ++st) {
-      const int s = st % STAGES;
-      if (!mbar_wait(&empty[s], ((st / STAGES) & 1u) ^ 1u, status)) return false;
-      const uint32_t atile = sbase + s * STAGE_BYTES + tile_i * kTileBytes;
-      const uint32_t s2 = scale2<AT>(sc[u]);
-#pragma unroll
-      for (int ci = 0; ci < NCH; ++ci) {
-        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw[u][ci / 4]);
-        uint32_t o[4];
-        dq_int4_chunk<AT>(wv[ci % 4], s2, o);
-        sts16(swz(atile, row, c0 + ci), o[0], o[1], o[2], o[3]);
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[s]);
-    }
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < MB; ++u) {
-#pragma unroll
-        for (int i = 0; i < NV; ++i) raw[u][i] = nraw[u][i];
-        sc[u] = nsc[u];
-      }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&R.afull[ar.slot]);
+    ar.next(g.a_st);
+    const int hi = lo + BPK;
+    while (released < waited && ((released + 1) * 128 <= hi || kb == nkb - 1)) {
+      if (lane == 0) mbar_arrive(&R.rempty[rr.slot]);
+      rr.next(g.r_st);
+      ++released;
     }
   }
   return true;
 }
 
+
 template <typename AT, bool UP>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const GemvParams p) {
-  using G = Geo<UP>;
+__device__ __forceinline__ bool dq_dispatch(const TcTile& d, const TcGeo& g, const Rings& R, int nkb, int part, int row,
+                                            int c0, uint32_t sarea, Ring& ar, Ring& rw, Ring& rr, int32_t* status,
+                                            int lane) {
+  switch (d.wtype) {
+    case MOEB200_I4: return dq_tile<AT, UP, MOEB200_I4>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, status, lane);
+    case MOEB200_I8: return dq_tile<AT, UP, MOEB200_I8>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, status, lane);
+    case MOEB200_F16: return dq_tile<AT, UP, MOEB200_F16>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, status, lane);
+    case MOEB200_BF16:
+      return dq_tile<AT, UP, MOEB200_BF16>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, status, lane);
+    default: return dq_tile<AT, UP, MOEB200_F32>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, status, lane);
+  }
+}
+
+// Waits (bounded, no status) for the last min(issued, depth) completions of a ring's full barriers:
+// the issuing warp must not exit with its copies still landing.
+__device__ __forceinline__ void drain(uint64_t* full, uint32_t issued, int depth) {
+  const uint32_t dd = (uint32_t)depth;
+  for (uint32_t q = issued > dd ? issued - dd : 0; q < issued; ++q) mbar_wait(&full[q % dd], (q / dd) & 1u, nullptr);
+}
+
+template <typename AT, bool UP>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const GemvParams p, const TcGeo g, const __grid_constant__ TcMaps tm) {
+  constexpr int NA = UP ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sgen + G::STAGES * G::STAGE_BYTES);
-  uint64_t* full_a = bars;                     // [STAGES] 8 dequant-warp arrivals
-  uint64_t* full_b = bars + G::STAGES;         // [STAGES] 1 loader arrival
-  uint64_t* empty = bars + 2 * G::STAGES;      // [STAGES] 1 tcgen05.commit
-  uint64_t* acc_full = bars + 3 * G::STAGES;   // [2] 1 tcgen05.commit
-  uint64_t* acc_empty = acc_full + 2;          // [2] 4 epilogue-warp arrivals
-  uint64_t* done_bar = acc_empty + 2;          // [1] final commit before freeing TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  Rings R;
+  R.a = sbase + g.a_off;
+  R.b = sbase + g.b_off;
+  R.r = sbase + g.r_off;
+  R.s = sbase + g.s_off;
+  R.d = sbase + g.d_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sgen + g.bar_off);
+  R.afull = bars;
+  R.aempty = R.afull + g.a_st;
+  R.bfull = R.aempty + g.a_st;
+  R.bempty = R.bfull + g.b_st;
+  R.rfull = R.bempty + g.b_st;
+  R.rempty = R.rfull + g.r_st;
+  R.sfull = R.rempty + g.r_st;
+  R.sempty = R.sfull + 2;
+  R.accf = R.sempty + 2;
+  R.acce = R.accf + 2;
+  R.done = R.acce + 2;
+  R.tmem_slot = reinterpret_cast<uint32_t*>(R.done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (UP && p.zero_acc) {
-    const int64_t n = (int64_t)p.T * p.H;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-      p.acc[i] = 0.f;
-  }
-
   if (threadIdx.x == 0) {
-    for (int s = 0; s < G::STAGES; ++s) {
-      mbar_init(&full_a[s], kDqWarps);
-      mbar_init(&full_b[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < g.a_st; ++s) {
+      mbar_init(&R.afull[s], kDqWarps);
+      mbar_init(&R.aempty[s], 1);
+    }
+    for (int s = 0; s < g.b_st; ++s) {
+      mbar_init(&R.bfull[s], 1);
+      mbar_init(&R.bempty[s], 1);
+    }
+    for (int s = 0; s < g.r_st; ++s) {
+      mbar_init(&R.rfull[s], 1);
+      mbar_init(&R.rempty[s], kDqWarps);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&R.sfull[b], 1);
+      mbar_init(&R.sempty[b], kDqWarps);
+      mbar_init(&R.accf[b], 1);
+      mbar_init(&R.acce[b], 4);
     }
-    mbar_init(done_bar, 1);
+    mbar_init(R.done, 1);
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "n"(G::TMEM_COLS));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(R.tmem_slot)),
+                 "n"(UP ? 512 : 256));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *R.tmem_slot;
+  constexpr int BUF_COLS = UP ? 256 : 128;  // one accumulator buffer (up: gate | up)
 
   const int n_items = *p.n_items;
   const int rb_per_item = (UP ? p.I : p.H) / BM;
@@ -438,168 +475,246 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const GemvParams p
   bool ok = true;
 
   if (warp < kDqWarps) {
-    // ---------------- dequant producers ----------------
-    int tile_i, row, c0, nch;
-    dq_coords<UP>(threadIdx.x, tile_i, row, c0, nch);
-    uint32_t st = 0;
+    // ---------------- dequantisers ----------------
+    const int tid = threadIdx.x;
+    const int part = UP ? tid >> 7 : 0;
+    const int row = UP ? tid & 127 : tid >> 1;
+    const int c0 = UP ? 0 : (tid & 1) * 4;
+    Ring ar, rw, rr;
+    uint32_t sj = 0;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
       TcTile d;
       tc_describe<UP>(p, tile, rb_per_item, d);
-      if (d.wtype == MOEB200_I4 && d.gs % BK == 0 && nkb % 2 == 0) {
-        if (!dq_int4_tile<AT, UP, G::STAGES, G::STAGE_BYTES>(d, nkb, tile_i, row, c0, st, sbase, empty, full_a,
-                                                             p.status, lane)) {
-          ok = false;
-          break;
-        }
-        continue;
+      const bool isint = is_int_w(d.wtype);
+      uint32_t sarea = 0;
+      if (isint) {
+        const int par = sj & 1;
+        if (!mbar_wait(&R.sfull[par], (sj >> 1) & 1u, p.status)) { ok = false; break; }
+        sarea = R.s + par * g.s_bytes;
       }
-      Raw cur;
-      dq_load<UP>(d, 0, tile_i, row, c0, cur);
-      for (int kb = 0; kb < nkb; ++kb, ++st) {
-        Raw nxt;
-        if (kb + 1 < nkb) dq_load<UP>(d, kb + 1, tile_i, row, c0, nxt);
-        const int s = st % G::STAGES;
-        if (!mbar_wait(&empty[s], ((st / G::STAGES) & 1u) ^ 1u, p.status)) { ok = false; break; }
-        const uint32_t atile = sbase + s * G::STAGE_BYTES + tile_i * kTileBytes;
-        dq_store<AT, UP>(d, kb, tile_i, row, c0, cur, atile);
-        fence_proxy_async();
+      ok = dq_dispatch<AT, UP>(d, g, R, nkb, part, row, c0, sarea, ar, rw, rr, p.status, lane);
+      if (isint) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
-        if (kb + 1 < nkb) cur = nxt;
+        if (lane == 0) mbar_arrive(&R.sempty[sj & 1]);
+        ++sj;
       }
     }
-  } else if (warp == kLoadWarp) {
-    // ---------------- B loader: token rows (up) or h rows (down), cp.async into SW128 tiles -------
-    constexpr int LAG = G::STAGES - 2;
-    uint32_t st = 0;
-    uint32_t pending = 0;  // steps issued but not yet signalled
+  } else if (warp == kTmaWarp) {
+    // ---------------- TMA producer: raw weight units and scale rows ----------------
+    Ring rw;
+    uint32_t issued = 0, sj = 0, jn = 0;
+    const uint64_t tmap0 = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)blockIdx.x * kTmapSlots * 128;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
       TcTile d;
       tc_describe<UP>(p, tile, rb_per_item, d);
-      // per-lane rows: lane handles rows lane, lane+32, ... of the N-row B tile
-      const AT* rowp[NMAX / 32];
-#pragma unroll
-      for (int i = 0; i < NMAX / 32; ++i) {
-        const int j = lane + 32 * i;
-        if (j < d.ntok) {
-          if (UP) {
-            const int tok = p.pos[d.start + j] / p.k;
-            rowp[i] = static_cast<const AT*>(p.x) + (int64_t)tok * p.H;
-          } else {
-            rowp[i] = static_cast<const AT*>(p.h) + (int64_t)(d.start + j) * p.I;
-          }
-        } else {
-          rowp[i] = static_cast<const AT*>(UP ? p.x : p.h);  // zero-filled (src size 0)
+      // a tensor-map slot is reused after tmap_ring = r_st + 1 tiles: at most r_st units (so at most
+      // r_st tiles) can still be landing, so the copies through the slot have completed
+      const uint64_t gdesc = tmap0 + (uint64_t)(jn % (uint32_t)g.tmap_ring) * 128;
+      ++jn;
+      retarget_tmap(tm.w[d.slot], R.d, gdesc, d.q, lane);
+      if (is_int_w(d.wtype)) {
+        const int par = sj & 1;
+        if (sj >= 2 && !mbar_wait(&R.sempty[par], ((sj >> 1) - 1) & 1u, p.status)) { ok = false; break; }
+        if (lane == 0) {
+          const uint32_t blk = (uint32_t)(BM * d.sstride);
+          uint8_t* sa = sgen + g.s_off + par * g.s_bytes;
+          mbar_arrive_expect_tx(&R.sfull[par], NA * blk);
+          bulk_g2s(sa, d.s + (int64_t)d.r0 * d.sstride, blk, &R.sfull[par]);
+          if (UP) bulk_g2s(sa + blk, d.s + (int64_t)(p.I + d.r0) * d.sstride, blk, &R.sfull[par]);
         }
+        ++sj;
       }
-      for (int kb = 0; kb < nkb; ++kb, ++st) {
-        const int s = st % G::STAGES;
-        if (!mbar_wait(&empty[s], ((st / G::STAGES) & 1u) ^ 1u, p.status)) { ok = false; break; }
-        const uint32_t btile = sbase + s * G::STAGE_BYTES + G::NA * kTileBytes;
+      for (int u = 0; u < d.units; ++u) {
+        if (!mbar_wait(&R.rempty[rw.slot], rw.phase ^ 1u, p.status)) { ok = false; break; }
+        if (lane == 0) {
+          const uint32_t dst = R.r + rw.slot * (NA * kTileBytes);
+          mbar_arrive_expect_tx(&R.rfull[rw.slot], NA * kTileBytes);
+          tma2d(dst, gdesc, u * 128, d.r0, &R.rfull[rw.slot]);
+          if (UP) tma2d(dst + kTileBytes, gdesc, u * 128, p.I + d.r0, &R.rfull[rw.slot]);
+        }
+        __syncwarp();
+        rw.next(g.r_st);
+        ++issued;
+      }
+    }
+    if (lane == 0) {
+      drain(R.rfull, issued, g.r_st);
+      if (sj) drain(R.sfull, sj, 2);
+    }
+    __syncwarp();
+  } else if (warp == kLoadWarp) {
+    // ---------------- B ring: token rows (up, cp.async gather) or h rows (down, TMA) ----------------
+    Ring bw, bs;
+    uint32_t issued = 0;
+    int pending = 0;
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      TcTile d;
+      tc_describe<UP>(p, tile, rb_per_item, d);
+      if constexpr (UP) {
+        // per-lane rows: lane handles rows lane, lane+32, ... of the N-row B tile
+        const AT* rowp[NMAX / 32];
 #pragma unroll
         for (int i = 0; i < NMAX / 32; ++i) {
           const int j = lane + 32 * i;
-          if (j < d.n) {
-            const uint32_t bytes = j < d.ntok ? 16u : 0u;
+          rowp[i] = static_cast<const AT*>(p.x);  // zero-filled (src size 0)
+          if (j < d.ntok) rowp[i] += (int64_t)(p.pos[d.start + j] / p.k) * p.H;
+        }
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&R.bempty[bw.slot], bw.phase ^ 1u, p.status)) { ok = false; break; }
+          const uint32_t btile = R.b + bw.slot * kTileBytes;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) cp_async16(swz(btile, j, c), rowp[i] + kb * BK + c * 8, bytes);
+          for (int i = 0; i < NMAX / 32; ++i) {
+            const int j = lane + 32 * i;
+            if (j < d.n) {
+              const uint32_t bytes = j < d.ntok ? 16u : 0u;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) cp_async16(swz(btile, j, c), rowp[i] + kb * BK + c * 8, bytes);
+            }
+          }
+          cp_async_commit();
+          bw.next(g.b_st);
+          if (++pending > g.lag) {
+            cp_async_wait_n(g.lag);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&R.bfull[bs.slot]);
+            bs.next(g.b_st);
+            --pending;
           }
         }
-        cp_async_commit();
-        ++pending;
-        if (pending > (uint32_t)LAG) {
-          cp_async_wait<LAG>();
-          fence_proxy_async();
+      } else {
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&R.bempty[bw.slot], bw.phase ^ 1u, p.status)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&R.bfull[bw.slot], kTileBytes);
+            tma2d(R.b + bw.slot * kTileBytes, reinterpret_cast<uint64_t>(&tm.h), kb * BK, d.start, &R.bfull[bw.slot]);
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full_b[(st - LAG) % G::STAGES]);
-          --pending;
+          bw.next(g.b_st);
+          ++issued;
         }
       }
     }
-    cp_async_wait<0>();
-    fence_proxy_async();
+    if constexpr (UP) {
+      cp_async_wait<0>();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0)
+        for (; pending > 0; --pending) {
+          mbar_arrive(&R.bfull[bs.slot]);
+          bs.next(g.b_st);
+        }
+    } else {
+      if (lane == 0) drain(R.bfull, issued, g.b_st);
+    }
     __syncwarp();
-    if (lane == 0)
-      for (uint32_t q = pending; q > 0; --q) mbar_arrive(&full_b[(st - q) % G::STAGES]);
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer (one thread) ----------------
     if (lane == 0) {
-      uint32_t st = 0, tcount = 0;
+      Ring ar, br;
+      uint32_t tcount = 0;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++tcount) {
         TcTile d;
         tc_describe<UP>(p, tile, rb_per_item, d);
         const int buf = tcount & 1;
-        if (!mbar_wait(&acc_empty[buf], ((tcount >> 1) & 1u) ^ 1u, p.status)) { ok = false; break; }
+        if (!mbar_wait(&R.acce[buf], ((tcount >> 1) & 1u) ^ 1u, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t idesc = idesc_f16(std::is_same<AT, __nv_bfloat16>::value, d.n);
-        const uint32_t d0 = tmem + buf * G::BUF_COLS;
-        for (int kb = 0; kb < nkb; ++kb, ++st) {
-          const int s = st % G::STAGES;
-          const uint32_t par = (st / G::STAGES) & 1u;
-          if (!mbar_wait(&full_a[s], par, p.status) || !mbar_wait(&full_b[s], par, p.status)) { ok = false; break; }
+        const uint32_t d0 = tmem + buf * BUF_COLS;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&R.afull[ar.slot], ar.phase, p.status) || !mbar_wait(&R.bfull[br.slot], br.phase, p.status)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          const uint32_t stage = sbase + s * G::STAGE_BYTES;
-          const uint32_t btile = stage + G::NA * kTileBytes;
+          const uint32_t astage = R.a + ar.slot * (NA * kTileBytes);
+          const uint32_t btile = R.b + br.slot * kTileBytes;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t bdesc = sw128_desc(btile + kk * 32);
             const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
-            tc_mma(d0, sw128_desc(stage + kk * 32), bdesc, idesc, accum);
-            if (UP) tc_mma(d0 + NMAX, sw128_desc(stage + kTileBytes + kk * 32), bdesc, idesc, accum);
+            tc_mma(d0, sw128_desc(astage + kk * 32), bdesc, idesc, accum);
+            if (UP) tc_mma(d0 + NMAX, sw128_desc(astage + kTileBytes + kk * 32), bdesc, idesc, accum);
           }
-          tc_commit(&empty[s]);
+          tc_commit(&R.aempty[ar.slot]);
+          tc_commit(&R.bempty[br.slot]);
+          ar.next(g.a_st);
+          br.next(g.b_st);
         }
         if (!ok) break;
-        tc_commit(&acc_full[buf]);
+        tc_commit(&R.accf[buf]);
       }
-      tc_commit(done_bar);
-      mbar_wait(done_bar, 0, p.status);
+      tc_commit(R.done);
+      mbar_wait(R.done, 0, p.status);
     }
     __syncwarp();
   } else {
     // ---------------- epilogue warps 8..11 ----------------
     const int q = warp - kEpiWarp0;  // TMEM lane quarter
     const int r_local = q * 32 + lane;
+    if (UP && p.zero_acc) {  // the down phase reduces into acc: clear it while the first tile runs
+      const int64_t n4 = (int64_t)p.T * p.H / 4;
+      float4* a4 = reinterpret_cast<float4*>(p.acc);
+      for (int64_t i = (int64_t)blockIdx.x * 128 + q * 32 + lane; i < n4; i += (int64_t)gridDim.x * 128)
+        a4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     uint32_t tcount = 0;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++tcount) {
       TcTile d;
       tc_describe<UP>(p, tile, rb_per_item, d);
       const int buf = tcount & 1;
-      if (!mbar_wait(&acc_full[buf], (tcount >> 1) & 1u, p.status)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + buf * G::BUF_COLS;
-      const int row = d.r0 + r_local;
-      for (int j0 = 0; j0 < d.n; j0 += 16) {
-        uint32_t a[16];
-        tmem_ld16(tb + j0, a);
-        if (UP) {
-          uint32_t u[16];
-          tmem_ld16(tb + NMAX + j0, u);
-          tmem_wait_ld();
+      // down: this lane's tokens (pairs lane + 32 i) as acc row offsets and router weights
+      int64_t toff[NMAX / 32];
+      float wj[NMAX / 32];
+      if constexpr (!UP) {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = j0 + jj;
-            if (j < d.ntok) {
-              const float hv = silu_mul(__uint_as_float(a[jj]), __uint_as_float(u[jj]));
-              static_cast<AT*>(p.h)[(int64_t)(d.start + j) * p.I + row] = from_f32<AT>(hv);
-            }
+        for (int i = 0; i < NMAX / 32; ++i) {
+          const int j = lane + 32 * i;
+          toff[i] = 0;
+          wj[i] = 0.f;
+          if (j < d.ntok) {
+            const int pos = p.pos[d.start + j];
+            toff[i] = (int64_t)(pos / p.k) * p.H;
+            wj[i] = p.wflat[pos];
           }
-        } else {
-          tmem_wait_ld();
+        }
+      }
+      if (!mbar_wait(&R.accf[buf], (tcount >> 1) & 1u, p.status)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + buf * BUF_COLS;
+      const int row = d.r0 + r_local;
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = j0 + jj;
-            if (j < d.ntok) {
-              const int pos = p.pos[d.start + j];
-              const int tok = pos / p.k;
-              red_add_f32(p.acc + (int64_t)tok * p.H + row, p.wflat[pos] * __uint_as_float(a[jj]));
+      for (int j0 = 0; j0 < NMAX; j0 += 16) {
+        if (j0 < d.n) {
+          uint32_t a[16];
+          tmem_ld16(tb + j0, a);
+          if constexpr (UP) {
+            uint32_t u[16];
+            tmem_ld16(tb + NMAX + j0, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = j0 + jj;
+              if (j < d.ntok) {
+                const float hv = silu_mul(__uint_as_float(a[jj]), __uint_as_float(u[jj]));
+                static_cast<AT*>(p.h)[(int64_t)(d.start + j) * p.I + row] = from_f32<AT>(hv);
+              }
+            }
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = j0 + jj;
+              const int64_t t = __shfl_sync(0xffffffffu, toff[j >> 5], j & 31);
+              const float w = __shfl_sync(0xffffffffu, wj[j >> 5], j & 31);
+              if (j < d.ntok) red_add_f32(p.acc + t + row, w * __uint_as_float(a[jj]));
             }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive(&R.acce[buf]);
     }
   }
 
@@ -607,29 +722,86 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const GemvParams p
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(G::TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(UP ? 512 : 256));
   }
 }
 
+// Ring depths for a phase: the first candidate whose shared memory fits one CTA.
+bool plan_geo(bool up, uint32_t s_bytes, TcGeo& g, int& smem) {
+  static const int cand_up[][3] = {{2, 4, 2}, {2, 3, 2}, {2, 2, 2}, {2, 2, 1}};
+  static const int cand_dn[][3] = {{4, 4, 5}, {3, 4, 4}, {3, 3, 3}, {2, 2, 2}, {2, 2, 1}};
+  const int na = up ? 2 : 1;
+  const int nc = up ? 4 : 5;
+  for (int i = 0; i < nc; ++i) {
+    const int* c = up ? cand_up[i] : cand_dn[i];
+    g.a_st = c[0];
+    g.b_st = c[1];
+    g.r_st = c[2];
+    g.a_off = 0;
+    g.b_off = g.a_off + (uint32_t)(g.a_st * na * kTileBytes);
+    g.r_off = g.b_off + (uint32_t)(g.b_st * kTileBytes);
+    g.s_off = g.r_off + (uint32_t)(g.r_st * na * kTileBytes);
+    g.s_bytes = s_bytes;
+    g.d_off = g.s_off + 2 * s_bytes;
+    g.bar_off = g.d_off + 128;
+    const uint32_t nbars = 2 * (g.a_st + g.b_st + g.r_st) + 9;
+    smem = (int)(g.bar_off + nbars * 8 + 16 + 1024);
+    if (smem <= kMaxSmem) {
+      g.lag = g.b_st - 1;
+      g.tmap_ring = g.r_st + 1;
+      return true;
+    }
+  }
+  return false;
+}
+
 template <typename AT, bool UP>
-cudaError_t launch_tc_t(const GemvParams& p, int grid, cudaStream_t s) {
+cudaError_t launch_tc_t(const GemvParams& p, const TcGeo& g, const TcMaps& tm, int smem, int grid, cudaStream_t s) {
   auto kern = gemm_tc_kernel<AT, UP>;
-  const int smem = Geo<UP>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, smem, s>>>(p);
+  kern<<<grid, kThreads, smem, s>>>(p, g, tm);
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_phase(const GemvParams& p, const moeb200_layout* lays, int nlay, int act, int n_pairs,
+                              bool up, int grid, cudaStream_t s) {
+  const int K = up ? p.H : p.I;
+  const int na = up ? 2 : 1;
+  uint32_t sst = 0;
+  for (int i = 0; i < nlay; ++i) {
+    const int wt = lays[i].wtype;
+    if (wt == MOEB200_I4 || wt == MOEB200_I8) sst = std::max<uint32_t>(sst, (uint32_t)(K / (up ? lays[i].gs_up : lays[i].gs_dn) * 2));
+  }
+  const uint32_t s_bytes = (uint32_t)((na * BM * sst + 127) / 128 * 128);
+  TcGeo g{};
+  int smem = 0;
+  if (!plan_geo(up, s_bytes, g, smem)) return cudaErrorInvalidConfiguration;
+  TcMaps tm{};
+  for (int i = 0; i < nlay; ++i) {
+    cudaError_t e = tma_weight_template(&tm.w[i], K * gemv_wbits(lays[i].wtype) / 8, up ? 2 * p.I : p.H, BM, p.tmap_ws);
+    if (e != cudaSuccess) return e;
+  }
+  if (!up) {
+    cudaError_t e = tma_rows16_map(&tm.h, p.h, p.I, std::max(n_pairs, 1), BM, act);
+    if (e != cudaSuccess) return e;
+  }
+  if (act == MOEB200_BF16)
+    return up ? launch_tc_t<__nv_bfloat16, true>(p, g, tm, smem, grid, s)
+              : launch_tc_t<__nv_bfloat16, false>(p, g, tm, smem, grid, s);
+  return up ? launch_tc_t<__half, true>(p, g, tm, smem, grid, s) : launch_tc_t<__half, false>(p, g, tm, smem, grid, s);
 }
 
 }  // namespace
 
-cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s) {
-  return act_type == MOEB200_BF16 ? launch_tc_t<__nv_bfloat16, true>(p, grid, s) : launch_tc_t<__half, true>(p, grid, s);
+cudaError_t launch_gemm_up(const GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int n_pairs,
+                           int grid, cudaStream_t s) {
+  return launch_gemm_phase(p, lays, nlay, act_type, n_pairs, true, grid, s);
 }
 
-cudaError_t launch_gemm_down(const GemvParams& p, int act_type, int grid, cudaStream_t s) {
-  return act_type == MOEB200_BF16 ? launch_tc_t<__nv_bfloat16, false>(p, grid, s)
-                                  : launch_tc_t<__half, false>(p, grid, s);
+cudaError_t launch_gemm_down(const GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int n_pairs,
+                             int grid, cudaStream_t s) {
+  return launch_gemm_phase(p, lays, nlay, act_type, n_pairs, false, grid, s);
 }
 
 }  // namespace moeb200

@@ -14,25 +14,19 @@
 // columns of the item's token rows; the job's whole scale rows go to a double-buffered scale area
 // with one or two bulk copies. Consumers dequantise in registers straight into mma.sync m16n8k16
 // A fragments and multiply them with up to 8*NB tokens:
-//   fp16 activations, int4/int8 records: the weight is dequantised together with its scale in
-//     fp16, w = fp16((q - 8) * s) (the exact (q - 8) times s, rounded once: the value moelab's
-//     materialize gives), and accumulated in fp32 across all groups;
-//   bf16 activations: (q - 8) is exact in bf16; the fp16 scale multiplies the fp32 partial of each
-//     group (bf16 cannot hold the scale exactly);
+//   int4/int8 records: (q - 8) (int8: q) is exact in fp16 and bf16; the tensor cores sum its exact
+//     products with the activations of one scale group in fp32, and the group's fp32 partial is
+//     multiplied by its fp16 scale (exact in fp32) -- one rounding fewer than materialising
+//     w = (q - 8) * s in the activation dtype first, and no per-weight scale multiply;
 //   float records: converted to the activation type when the types differ.
 // Small batches split K over jobs: the up phase then adds fp32 partial pre-activations into
 // pre[j, 0:2I] (gate | up) and the job whose split of a row block arrives last (a per-(item, row
 // block) counter) forms h = silu(gate) * up for its rows, so the down phase always reads h.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
-#include <map>
-#include <mutex>
-#include <tuple>
 #include <type_traits>
 
 #include "gemv.cuh"
+#include "tma.cuh"
 
 namespace moeb200 {
 
@@ -120,12 +114,6 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -143,12 +131,6 @@ struct Scales {
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh)
         s[rt][hh] = __half2float(__ushort_as_half((unsigned short)lds_u16(row[rt][hh] + 2 * gi)));
-  }
-  __device__ __forceinline__ void h2(int gi, uint32_t (&s)[2][2]) const {
-#pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) s[rt][hh] = prmt(lds_u16(row[rt][hh] + 2 * gi), 0u, 0x1010);  // (s, s)
   }
 };
 
@@ -172,8 +154,8 @@ __device__ __forceinline__ void fold_scaled(float (&tot)[2][NB][4], const float 
 // xb[nb]: the lane's activation words of the chunk (token g + 8*nb).
 
 // int4: chunk = 32*WPL columns, lane t holds columns [c + 8*WPL*t, +8*WPL) as WPL words per row.
-// SCALED (fp16 activations): weights dequantised with their scale, MMAs straight into tot.
-template <typename AT, int NB, int WPL, bool SCALED>
+// The exact (q - 8) products of a group are summed in fp32 and the group's partial is scaled once.
+template <typename AT, int NB, int WPL>
 __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
                                            const uint32_t (&xb)[NB][4 * WPL], const Scales& S, int gi,
                                            float (&tot)[2][NB][4]) {
@@ -182,37 +164,7 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
-  if constexpr (SCALED) {
-    uint32_t s2[2][2];
-    S.h2(gi, s2);
-#pragma unroll
-    for (int j = 0; j < WPL; ++j) {
-      uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
-#pragma unroll
-      for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          Dq<__half>::int4x8(wa[rt][hh][j], p04[rt][hh], p15[rt][hh], p26[rt][hh], p37[rt][hh]);
-          p04[rt][hh] = hmul2(p04[rt][hh], s2[rt][hh]);
-          p15[rt][hh] = hmul2(p15[rt][hh], s2[rt][hh]);
-          p26[rt][hh] = hmul2(p26[rt][hh], s2[rt][hh]);
-          p37[rt][hh] = hmul2(p37[rt][hh], s2[rt][hh]);
-        }
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const uint32_t x0 = xb[nb][4 * j], x1 = xb[nb][4 * j + 1], x2 = xb[nb][4 * j + 2], x3 = xb[nb][4 * j + 3];
-        const uint32_t b00 = prmt(x0, x2, 0x5410), b01 = prmt(x0, x2, 0x7632);  // (c, c+4), (c+1, c+5)
-        const uint32_t b10 = prmt(x1, x3, 0x5410), b11 = prmt(x1, x3, 0x7632);  // (c+2, c+6), (c+3, c+7)
-#pragma unroll
-        for (int rt = 0; rt < 2; ++rt) {
-          const uint32_t a0[4] = {p04[rt][0], p04[rt][1], p15[rt][0], p15[rt][1]};
-          const uint32_t a1[4] = {p26[rt][0], p26[rt][1], p37[rt][0], p37[rt][1]};
-          MmaOp<__half>::run(tot[rt][nb], a0, b00, b01);
-          MmaOp<__half>::run(tot[rt][nb], a1, b10, b11);
-        }
-      }
-    }
-  } else {
+  {
     float d[2][NB][2][4];
 #pragma unroll
     for (int j = 0; j < WPL; ++j) {
@@ -248,7 +200,7 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
 }
 
 // int8: chunk = 16*WPL columns, lane t holds columns [c + 4*WPL*t, +4*WPL) as WPL words per row.
-template <typename AT, int NB, int WPL, bool SCALED>
+template <typename AT, int NB, int WPL>
 __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
                                            const uint32_t (&xb)[NB][2 * WPL], const Scales& S, int gi,
                                            float (&tot)[2][NB][4]) {
@@ -257,29 +209,7 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
-  if constexpr (SCALED) {
-    uint32_t s2[2][2];
-    S.h2(gi, s2);
-#pragma unroll
-    for (int m = 0; m < WPL; ++m) {
-      uint32_t p01[2][2], p23[2][2];
-#pragma unroll
-      for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          Dq<__half>::int8x4(wa[rt][hh][m], p01[rt][hh], p23[rt][hh]);
-          p01[rt][hh] = hmul2(p01[rt][hh], s2[rt][hh]);
-          p23[rt][hh] = hmul2(p23[rt][hh], s2[rt][hh]);
-        }
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int rt = 0; rt < 2; ++rt) {
-          const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
-          MmaOp<__half>::run(tot[rt][nb], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
-        }
-    }
-  } else {
+  {
     float d[2][NB][2][4];
 #pragma unroll
     for (int m = 0; m < WPL; ++m) {
@@ -371,7 +301,6 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
   constexpr int LOFF = I4 ? 8 * WPL : 4 * WPL;  // lane column offset inside a chunk
   constexpr int WT = KIND == kF32w2 || KIND == kF32w1 ? 2 : (KIND == kBF16w4 || KIND == kBF16w2 || KIND == kBF16w1) ? 1 : 0;
   constexpr int W2 = I4 ? 1 : I8 ? 2 : WT == 2 ? 8 : 4;  // weight bytes per column, times 2
-  constexpr bool SCALED = std::is_same<AT, __half>::value;
   const int nch = ncols / CH;
   uint32_t wr[2][2];
 #pragma unroll
@@ -404,9 +333,9 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
     const uint32_t o = ci * (CH * W2 / 2) + lo;
     const uint32_t so0 = swz(o, g), so1 = swz(o + 16, g);
     if constexpr (I4) {
-      chunk_int4<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, gi, tot);
+      chunk_int4<AT, NB, WPL>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (I8) {
-      chunk_int8<AT, NB, WPL, SCALED>(wr, so0, so1, xb, S, gi, tot);
+      chunk_int8<AT, NB, WPL>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (WT == 2) {
       chunk_float<AT, float, NB, WPL>(wr, so0, so1, xb, tot);
     } else if constexpr (WT == 1) {
@@ -488,36 +417,6 @@ __device__ __forceinline__ void describe_job(const GemvParams& p, int job, const
   d.sst = d.sstride;
 }
 
-// ---- TMA with tensor maps ------------------------------------------------------------------------------
-__device__ __forceinline__ void tma2d(uint32_t dst, uint64_t tmap, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(dst),
-      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// The producer warp points one of its CTA's four global tensor-map slots at a record: the template
-// is staged in shared memory, its global address replaced, and the result copied out with a
-// release fence for the tensor-map proxy; the issuing lane then acquires it before using it.
-__device__ __forceinline__ void retarget_tmap(const CUtensorMap& tmpl, uint32_t sdesc, uint64_t gdesc,
-                                              const void* base, int lane) {
-  const uint32_t v = reinterpret_cast<const uint32_t*>(&tmpl)[lane];
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(sdesc + 4 * lane), "r"(v) : "memory");
-  __syncwarp();
-  if (lane == 0)
-    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(sdesc),
-                 "l"(reinterpret_cast<uint64_t>(base))
-                 : "memory");
-  __syncwarp();
-  asm volatile("tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::
-                   "l"(gdesc),
-               "r"(sdesc)
-               : "memory");
-  if (lane == 0) asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(gdesc) : "memory");
-  __syncwarp();
-}
-
 // ---- the kernel -----------------------------------------------------------------------------------------
 template <typename AT, int NB, bool UP, bool SPLIT>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p, const __grid_constant__ TmaTemplates tm) {
@@ -574,7 +473,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       if (d.nsteps == 0) continue;
       // tensor map of the job's weight field (a ring of four per CTA: the copies that used a slot
       // four jobs ago have landed, the stage ring being two deep)
-      const uint64_t gdesc = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * 4 + (jn & 3)) * 128;
+      const uint64_t gdesc = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (jn & 3)) * 128;
       retarget_tmap(tm.m[d.slot], smem_u32(sdesc), gdesc, d.q, lane);
       ++jn;
       // token rows of the item (one per lane)
@@ -825,41 +724,6 @@ cudaError_t launch_phase(const GemvParams& p, const TmaTemplates& tm, int nb, in
   return nb == 2 ? launch_t<AT, 2, UP, false>(p, tm, grid, smem, s) : launch_t<AT, 1, UP, false>(p, tm, grid, smem, s);
 }
 
-// Tensor-map template of a weight field: uint8 [rows][row_bytes], boxes of 128 bytes x box_rows,
-// 128-byte swizzle. The address is a placeholder (16-byte aligned device memory): every job swaps
-// in its record's address. Templates are cached per shape.
-cudaError_t weight_template(CUtensorMap* out, int row_bytes, int rows, int box_rows, void* placeholder) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, int, int>, CUtensorMap> cache;
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_tuple(row_bytes, rows, box_rows);
-  auto f = cache.find(key);
-  if (f != cache.end()) {
-    *out = f->second;
-    return cudaSuccess;
-  }
-  if (!encode) {
-    cudaDriverEntryPointQueryResult q{};
-    void* fn = nullptr;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
-  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1u, 1u};
-  CUtensorMap m;
-  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, placeholder, dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  cache[key] = m;
-  *out = m;
-  return cudaSuccess;
-}
-
 bool is_int_type(int wt) { return wt == MOEB200_I4 || wt == MOEB200_I8; }
 
 // A K split must cover whole groups and whole chunks: kSplitCols is a multiple of every group size.
@@ -896,10 +760,11 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   const int rows = up ? p.I : p.H;
   const int rpj = up ? kGemvJobRows / 2 : kGemvJobRows;
   const int64_t jobs1 = (int64_t)max_items * ((rows + rpj - 1) / rpj);
-  // split K while the jobs would not give every SM two of them (up: only with room for pre)
+  // split K while the jobs would not give every SM four of them (jobs of different records differ
+  // several-fold in bytes; more, smaller jobs balance the CTAs; up: only with room for pre)
   int ks = 1;
   const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
-  while (can_split && ks < 8 && jobs1 * ks < 2ll * sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
+  while (can_split && ks < 8 && jobs1 * ks < 4ll * sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
   if (up)
     p.ksplit_up = ks;
   else
@@ -909,7 +774,7 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   TmaTemplates tm{};
   for (int i = 0; i < nlay; ++i) {
     const int row_bytes = K * gemv_wbits(lays[i].wtype) / 8;
-    cudaError_t e = weight_template(&tm.m[i], row_bytes, up ? 2 * p.I : p.H, up ? kGemvJobRows / 2 : kGemvJobRows,
+    cudaError_t e = tma_weight_template(&tm.m[i], row_bytes, up ? 2 * p.I : p.H, up ? kGemvJobRows / 2 : kGemvJobRows,
                                     p.tmap_ws);
     if (e != cudaSuccess) return e;
   }

@@ -63,6 +63,7 @@ constexpr int kSplitCols = 512;  // K splits are multiples of this many columns
 
 constexpr int kGemvWBytes = kGemvJobRows * kStepBytes;  // weight tile of a stage (two 128-byte halves)
 constexpr int kGemvMaxGrid = 160;                        // tensor-map slots are carved for this many CTAs
+constexpr int kTmapSlots = 16;  // 128-byte tensor-map slots per CTA in the tensor-map workspace
 
 __host__ __device__ inline int gemv_wbits(int wtype) {
   return wtype == MOEB200_I4 ? 4 : wtype == MOEB200_I8 ? 8 : wtype == MOEB200_F32 ? 32 : 16;
@@ -86,7 +87,10 @@ cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_t
 cudaError_t trace_mark(int which, cudaStream_t s);
 int num_sms_cached();
 // tcgen05 grouped GEMM (gemm_tc.cu): items of up to 128 pairs, I and H multiples of 128
-cudaError_t launch_gemm_up(const GemvParams& p, int act_type, int grid, cudaStream_t s);
-cudaError_t launch_gemm_down(const GemvParams& p, int act_type, int grid, cudaStream_t s);
+// (n_pairs: rows of h, the B operand of the down phase)
+cudaError_t launch_gemm_up(const GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int n_pairs,
+                           int grid, cudaStream_t s);
+cudaError_t launch_gemm_down(const GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int n_pairs,
+                             int grid, cudaStream_t s);
 
 }  // namespace moeb200

@@ -389,6 +389,8 @@ __device__ int32_t block_exclusive_scan(int32_t (&v)[PER], int32_t* sh_warp) {
 // global memory are turned into per-(block, key) prefixes on the way.
 __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const int32_t* cnt_e, int32_t* offk_s,
                             int32_t* offe_s, int32_t* sh_warp) {
+  __shared__ int32_t tot_s[kMaxKeys];    // pairs per key
+  __shared__ int32_t offk_sh[kMaxKeys];  // first sorted position per key
   const int keys = p.E * p.P;
   const int tid = threadIdx.x;
   if (tid == 0 && p.miss) *p.miss = 0;
@@ -437,13 +439,23 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
       }
     }
     tot_e[i] = e < p.E ? rune : 0;
-    // work items: only for keys whose expert record is resident
+    if (key < keys) tot_s[key] = run;
+  }
+  __syncthreads();
+  // work items, numbered slot-major (every slot-0 record's items first: the largest records, so a
+  // round-robin of jobs over the CTAs hands the heavy ones out first); only resident records
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int m = tid * PER + i;  // slot-major index sl * E + ex
     int32_t ni = 0;
-    if (p.items != nullptr && key < keys && run > 0) {
-      const int ex = key / p.P, sl = key % p.P;
-      const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 1;
-      if (rec != 0) ni = (run + p.nt - 1) / p.nt;
-      else if (p.miss) atomicAdd(p.miss, run);
+    if (p.items != nullptr && m < keys) {
+      const int sl = m / p.E, ex = m % p.E;
+      const int32_t run = tot_s[ex * p.P + sl];
+      if (run > 0) {
+        const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 1;
+        if (rec != 0) ni = (run + p.nt - 1) / p.nt;
+        else if (p.miss) atomicAdd(p.miss, run);
+      }
     }
     nit[i] = ni;
   }
@@ -463,25 +475,36 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
     if (key < keys) {
       p.counts_k[key] = tot_k[i];
       p.offs_k[key] = off_k[i];
+      offk_sh[key] = off_k[i];
       if (offk_s) offk_s[key] = off_k[i];
-      if (nit[i] > 0) {
-        const int ex = key / p.P, sl = key % p.P;
-        const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
-        const LayoutOffs lo = p.offs[sl];
-        for (int m = 0; m < nit[i]; ++m) {
-          Item it;
-          it.p_guq = rec + lo.gu_q;
-          it.p_gus = rec + lo.gu_s;
-          it.p_dnq = rec + lo.dn_q;
-          it.p_dns = rec + lo.dn_s;
-          it.slot = sl;
-          it.start = off_k[i] + m * p.nt;
-          it.ntok = min(p.nt, tot_k[i] - m * p.nt);
-          it._pad = ex;
-          p.items[off_i[i] + m] = it;
-        }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int m = tid * PER + i;
+    if (nit[i] > 0) {
+      const int sl = m / p.E, ex = m % p.E;
+      const int key = ex * p.P + sl;
+      const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
+      const LayoutOffs lo = p.offs[sl];
+      const int32_t run = tot_s[key];
+      for (int q = 0; q < nit[i]; ++q) {
+        Item it;
+        it.p_guq = rec + lo.gu_q;
+        it.p_gus = rec + lo.gu_s;
+        it.p_dnq = rec + lo.dn_q;
+        it.p_dns = rec + lo.dn_s;
+        it.slot = sl;
+        it.start = offk_sh[key] + q * p.nt;
+        it.ntok = min(p.nt, run - q * p.nt);
+        it._pad = ex;
+        p.items[off_i[i] + q] = it;
       }
     }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
     const int e = tid * PER + i;
     if (e < p.E) {
       p.counts_e[e] = tot_e[i];

@@ -1,0 +1,51 @@
+// Tensor-map TMA shared by the GEMV and the tcgen05 GEMM: 2-D tiled loads completed on mbarriers,
+// device-side retargeting of a tensor map to one record, and the host-side encoders of the maps.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace moeb200 {
+
+// 2-D tiled load of box (x, y) of `tmap` into shared memory at `dst`, completing its bytes on `bar`.
+// x is in elements of the map's type and must give a 16-byte aligned start.
+__device__ __forceinline__ void tma2d(uint32_t dst, uint64_t tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// One warp points a global tensor-map slot at a record: the template is staged in shared memory
+// (128 bytes at sdesc), its global address replaced, and the result copied out with a release
+// fence for the tensor-map proxy; lane 0 then acquires it before issuing loads through it.
+__device__ __forceinline__ void retarget_tmap(const CUtensorMap& tmpl, uint32_t sdesc, uint64_t gdesc,
+                                              const void* base, int lane) {
+  const uint32_t v = reinterpret_cast<const uint32_t*>(&tmpl)[lane];
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(sdesc + 4 * lane), "r"(v) : "memory");
+  __syncwarp();
+  if (lane == 0)
+    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(sdesc),
+                 "l"(reinterpret_cast<uint64_t>(base))
+                 : "memory");
+  __syncwarp();
+  asm volatile("tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::
+                   "l"(gdesc),
+               "r"(sdesc)
+               : "memory");
+  if (lane == 0) asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(gdesc) : "memory");
+  __syncwarp();
+}
+
+// Host: tensor-map template of a weight field, uint8 [rows][row_bytes] read in boxes of 128 bytes x
+// box_rows with 128-byte swizzle. The address is a placeholder (16-byte aligned device memory): the
+// kernels swap in each record's address. Cached per shape.
+cudaError_t tma_weight_template(CUtensorMap* out, int row_bytes, int rows, int box_rows, void* placeholder);
+
+// Host: tensor map of a row-major 16-bit matrix [rows][cols] at `base`, boxes of 64 columns x
+// box_rows with 128-byte swizzle (the K-major operand layout of the tensor cores).
+cudaError_t tma_rows16_map(CUtensorMap* out, const void* base, int cols, int rows, int box_rows, int act_type);
+
+}  // namespace moeb200

@@ -37,6 +37,14 @@ class ExpertTable(C.Structure):
                 ("table", C.c_void_p)]
 
 
+class PeerGroup(C.Structure):
+    """moeb200_peer_group: device tables of every rank's mapped exchange buffers."""
+
+    _fields_ = [("G", C.c_int32), ("rank", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("k", C.c_int32),
+                ("_pad", C.c_int32), ("rows", C.c_void_p), ("parts", C.c_void_p), ("flags", C.c_void_p),
+                ("epoch", C.c_void_p), ("status", C.c_void_p)]
+
+
 _P = C.c_void_p
 _SIGS = {
     "moeb200_version": (C.c_char_p, []),
@@ -69,6 +77,13 @@ _SIGS = {
     "moeb200_shared_expert": (C.c_int, [C.POINTER(Layout), _P, _P, _P, C.c_int32, C.c_int32, _P, C.c_int32, _P,
                                         C.c_size_t, _P]),
     "moeb200_shared_expert_workspace": (C.c_size_t, [C.POINTER(Layout), C.c_int32]),
+    "moeb200_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), _P]),
+    "moeb200_peer_open": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
+    "moeb200_peer_close": (C.c_int, [_P]),
+    "moeb200_peer_free": (C.c_int, [_P]),
+    "moeb200_ep_signal": (C.c_int, [C.POINTER(PeerGroup), C.c_int32, _P]),
+    "moeb200_ep_gather": (C.c_int, [C.POINTER(PeerGroup), C.c_int32, _P, _P, _P, _P, _P, _P]),
+    "moeb200_ep_combine_peers": (C.c_int, [C.POINTER(PeerGroup), C.c_int32, _P, C.c_int32, _P]),
     "moeb200_check_workspace": (C.c_int, [_P, C.POINTER(C.c_int32), _P]),
 }
 

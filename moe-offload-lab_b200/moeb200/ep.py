@@ -1,4 +1,4 @@
-"""Expert parallelism for the B200 MoE layer over NCCL (no moelab counterpart: moelab runs on one GPU).
+"""Expert parallelism for the B200 MoE layer (no moelab counterpart: moelab runs on one GPU).
 
 Experts are split in contiguous blocks over the G ranks of a process group: rank r owns
 experts [r*E//G, (r+1)*E//G) and holds only their records. Every rank routes its own T tokens
@@ -6,21 +6,30 @@ experts [r*E//G, (r+1)*E//G) and holds only their records. Every rank routes its
 host synchronisation, so the whole decode step stays capturable in one CUDA graph:
 
   dispatch  every rank packs each token's hidden row with its routing (top-k indices, weights,
-            precision levels, skip flags) into one exchange row; one all_gather gives every rank
-            all G*T rows, which are unpacked into the arrays the expert kernels read.
+            precision levels, skip flags) into one exchange row; every rank receives all G*T rows
+            and unpacks them into the arrays the expert kernels read.
   experts   the owned experts over the G*T gathered tokens (pairs routed elsewhere are dropped);
             the down phase reduces straight into an fp32 partial-sum buffer [G*T, H].
-  combine   one all_to_all_single sends rows [g*T, (g+1)*T) of the partial sums to rank g; each
-            rank adds the G partials of its tokens in rank order 0..G-1 and casts once.
+  combine   rank g receives rows [g*T, (g+1)*T) of every rank's partial sums, adds the G partials
+            of its tokens in rank order 0..G-1 and casts once.
 
+Two exchanges implement dispatch and combine:
+  "p2p" (default on GPUs): every rank's exchange rows and partial sums live in buffers its peers map
+        with CUDA IPC; flag words (release/acquire at system scope, bounded waits) order them, the
+        gather kernel reads the peers' rows over NVLink and unpacks them, the combine kernel reads
+        the peers' partial rows of this rank's tokens and adds them in rank order -- no collective
+        call, five kernels per layer, all capturable in a CUDA graph;
+  "nccl": all_gather_into_tensor + all_to_all_single through torch.distributed (also runs on gloo
+        with CPU tensors when an ``ops`` object with CPU versions of the kernels is passed: tests).
 Every rank must call with the same T (a rank with fewer tokens pads with rows whose skip flags are
-set). The collectives are NCCL over NVLink/NVSwitch on a GPU box; the same code runs on gloo with
-CPU tensors when an ``ops`` object providing CPU versions of the four kernels is passed (tests).
+set).
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
+
+import ctypes as C
 
 import torch
 import torch.distributed as dist
@@ -92,21 +101,93 @@ class _Bufs:
     recv: torch.Tensor
 
 
+class PeerExchange:
+    """This rank's exchange buffers (packed rows [T, row_bytes], fp32 partial sums [G*T, H], flags
+    int32 [2][G]) allocated with moeb200_peer_alloc, the peers' buffers mapped with CUDA IPC, and the
+    moeb200_peer_group that points the exchange kernels at all of them. Creating one is a collective
+    (the IPC handles travel through the process group)."""
+
+    def __init__(self, group, world: int, rank: int, T: int, H: int, k: int, dtype: torch.dtype, device):
+        from . import _lib
+        from . import ops as O
+
+        L = _lib.lib()
+        self.world, self.rank, self.T, self.H, self.k = world, rank, T, H, k
+        self.row_bytes = O.ep_row_bytes(H, k, dtype)
+        sizes = {"rows": T * self.row_bytes, "parts": world * T * H * 4, "flags": 2 * world * 4}
+        self.local: dict[str, int] = {}
+        handles = {}
+        for name, nbytes in sizes.items():
+            ptr, h = C.c_void_p(), (C.c_char * 64)()
+            _lib.check(L.moeb200_peer_alloc(nbytes, C.byref(ptr), h))
+            self.local[name] = ptr.value
+            handles[name] = bytes(h)
+        allh: list = [None] * world
+        dist.all_gather_object(allh, handles, group=group)
+        self.opened: list[int] = []
+        mapped = {name: [0] * world for name in sizes}
+        for s in range(world):
+            for name in sizes:
+                if s == rank:
+                    mapped[name][s] = self.local[name]
+                    continue
+                ptr = C.c_void_p()
+                _lib.check(L.moeb200_peer_open(allh[s][name], C.byref(ptr)))
+                mapped[name][s] = ptr.value
+                self.opened.append(ptr.value)
+        self.tabs = {name: torch.tensor(mapped[name], dtype=torch.int64, device=device) for name in sizes}
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        g = _lib.PeerGroup()
+        g.G, g.rank, g.T, g.H, g.k = world, rank, T, H, k
+        g.rows, g.parts, g.flags = (self.tabs["rows"].data_ptr(), self.tabs["parts"].data_ptr(),
+                                    self.tabs["flags"].data_ptr())
+        g.epoch, g.status = self.epoch.data_ptr(), self.status.data_ptr()
+        self.group_c = g
+        self.group = group
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, wait for every rank to do the same, free this rank's buffers."""
+        from . import _lib
+
+        L = _lib.lib()
+        torch.cuda.synchronize()
+        for ptr in self.opened:
+            L.moeb200_peer_close(C.c_void_p(ptr))
+        self.opened = []
+        dist.barrier(group=self.group)
+        for ptr in self.local.values():
+            L.moeb200_peer_free(C.c_void_p(ptr))
+        self.local = {}
+
+
 class ExpertParallel:
     """One rank of an expert-parallel MoE layer group.
 
     runtime: a B200Runtime holding the records of the experts this rank owns (`self.e_lo` ..
     `self.e_hi`); other experts' records are not needed on this rank.
+    exchange: "p2p" (peer memory, the default with CUDA tensors) or "nccl" (collectives).
     """
 
-    def __init__(self, runtime, group=None, ops=None):
+    def __init__(self, runtime, group=None, ops=None, exchange: str | None = None):
         self.runtime = runtime
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.e_lo, self.e_hi = partition(runtime.num_experts, self.world, self.rank)
         self.ops = ops if ops is not None else CudaOps()
+        if exchange is None:
+            exchange = "nccl" if ops is not None else "p2p"
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
+        self.exchange = exchange
         self._bufs: dict[tuple, _Bufs] = {}
+        self._peers: dict[tuple, PeerExchange] = {}
+
+    def close(self) -> None:
+        for px in self._peers.values():
+            px.close()
+        self._peers = {}
 
     def owns(self, expert: int) -> bool:
         return self.e_lo <= expert < self.e_hi
@@ -146,16 +227,56 @@ class ExpertParallel:
         if level is None and skip is None:
             level, skip = self.runtime.levels(layer, w)
         b = self._buffers(T, H, k, x2.dtype, x2.device)
+        if out is None:
+            out = torch.empty_like(x2)
+        if self.exchange == "p2p":
+            self._run_p2p(layer, x2, idx, w, level, skip, b, out.view(T, H))
+            return out.view_as(x)
         self.ops.pack(x2, idx, w, level, skip, b.rows)
         dist.all_gather_into_tensor(b.rows_all, b.rows, group=self.group)
         self.ops.unpack(b.rows_all, H, k, x2.dtype, b.x_all, b.idx_all, b.w_all, b.level_all, b.skip_all)
         self.ops.local(self.runtime, layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all,
                        b.skip_all, b.part)
         dist.all_to_all_single(b.recv, b.part, group=self.group)
-        if out is None:
-            out = torch.empty_like(x2)
         self.ops.combine(b.recv.view(self.world, T, H), out.view(T, H))
         return out.view_as(x)
+
+    def _run_p2p(self, layer, x2, idx, w, level, skip, b: _Bufs, out) -> None:
+        from . import _lib
+        from . import ops as O
+
+        T, H = x2.shape
+        k = idx.shape[1]
+        key = (T, H, k, x2.dtype, str(x2.device))
+        px = self._peers.get(key)
+        if px is None:
+            px = PeerExchange(self.group, self.world, self.rank, T, H, k, x2.dtype, x2.device)
+            self._peers[key] = px
+        L = _lib.lib()
+        st = O._stream(x2.device)
+        act = O._act(x2.dtype)
+        g = C.byref(px.group_c)
+        _lib.check(L.moeb200_ep_pack(O._ptr(x2), O._ptr(idx), O._ptr(w), O._ptr(level), O._ptr(skip), T, H, k, act,
+                                     C.c_void_p(px.local["rows"]), st))
+        _lib.check(L.moeb200_ep_signal(g, 0, st))
+        _lib.check(L.moeb200_ep_gather(g, act, O._ptr(b.x_all), O._ptr(b.idx_all), O._ptr(b.w_all),
+                                       O._ptr(b.level_all), O._ptr(b.skip_all), st))
+        rt = self.runtime
+        rt._table(layer)
+        n = self.world * T
+        nbytes = L.moeb200_experts_workspace(C.byref(rt._ctables[layer]), n, k)
+        ws = O.workspace(nbytes, x2.device, slot=0)
+        _lib.check(L.moeb200_experts_forward_part(C.byref(rt._ctables[layer]), self.e_lo, self.e_hi, O._ptr(b.x_all),
+                                                  act, n, O._ptr(b.idx_all), O._ptr(b.w_all), k, O._ptr(b.level_all),
+                                                  O._ptr(b.skip_all), C.c_void_p(px.local["parts"]),
+                                                  O._ptr(rt.miss), O._ptr(ws), ws.numel(), st))
+        _lib.check(L.moeb200_ep_signal(g, 1, st))
+        _lib.check(L.moeb200_ep_combine_peers(g, act, O._ptr(out), 0, st))
+
+    def status(self) -> int:
+        """Largest status word of this rank's peer exchanges (0 = every wait ended); synchronises."""
+        torch.cuda.synchronize()
+        return max([int(px.status.item()) for px in self._peers.values()] or [0])
 
 
 class B200EPExperts(nn.Module):

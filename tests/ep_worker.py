@@ -36,7 +36,7 @@ def main():
     pol = ops.PolicySpec("threshold", thr=0.3)
     full_rt = B200Runtime(precs, lays, E, dev, pol, layers=[0])
     ep_rt = B200Runtime(precs, lays, E, dev, pol, layers=[0])
-    ep = ExpertParallel(ep_rt)
+    ep = ExpertParallel(ep_rt, exchange=sys.argv[2] if len(sys.argv) > 2 else "p2p")
     for p in precs:
         for e in range(E):
             full_rt.add_record(0, e, p, recs[p][e])
@@ -47,16 +47,20 @@ def main():
     wv, idx = torch.topk(torch.randn(T, E, generator=g, device=dev).softmax(-1), k, dim=-1)
     lvl, skip = full_rt.levels(0, wv)
     out = ep.run_layer(0, x, idx, wv, lvl, skip)
+    out2 = ep.run_layer(0, x, idx, wv, lvl, skip).clone()  # a second call reuses the exchange buffers
     single = full_rt.run_layer(0, x, idx, wv, level=lvl, skip=skip)
     torch.cuda.synchronize()
     slot = np.vectorize(lambda v: O.level_to_slot(int(v), 2))(lvl.cpu().numpy().astype(np.int64))
     recs_np = [[b.cpu().numpy() for b in recs[p]] for p in precs]
     ref = O.moe_layer(act_np(x), idx.cpu().numpy(), wv.cpu().numpy(), slot, skip.cpu().numpy().astype(bool), recs_np,
                       [lays[p] for p in precs], E)
-    res = {"rank": rank, "owned": [ep.e_lo, ep.e_hi], "err_oracle": O.max_rel_err(act_np(out), ref),
-           "err_single": O.max_rel_err(act_np(out), act_np(single)), "miss": int(ep_rt.miss.item())}
+    res = {"rank": rank, "owned": [ep.e_lo, ep.e_hi], "exchange": ep.exchange,
+           "err_oracle": O.max_rel_err(act_np(out), ref), "err_single": O.max_rel_err(act_np(out), act_np(single)),
+           "err_repeat": O.max_rel_err(act_np(out2), act_np(out)), "miss": int(ep_rt.miss.item()),
+           "status": ep.status() if ep.exchange == "p2p" else 0}
     (out_dir / f"rank{rank}.json").write_text(json.dumps(res))
     dist.barrier()
+    ep.close()
     dist.destroy_process_group()
 
 

@@ -29,9 +29,9 @@ def make_records(prec: str, H: int, I: int, n: int, seed: int, device, std: floa
     return lay, blobs, [b.cpu().numpy() for b in blobs]
 
 
-def layer_records(precs, H, I, E, seed, device, std=0.02):
+def layer_records(precs, H, I, E, seed, device, std=0.02, group_size=64):
     """Per precision, E records of the SAME float experts (like a store with several precisions)."""
-    lays = {p: F.record_layout(p, H, I) for p in precs}
+    lays = {p: F.record_layout(p, H, I, group_size=group_size) for p in precs}
     g = torch.Generator(device=device).manual_seed(seed)
     recs = {p: [] for p in precs}
     for _ in range(E):

@@ -1,6 +1,7 @@
 """Expert-parallel kernels on the GPU: exchange rows byte-exact against the torch mirror of the
 format, owned-expert partial sums + rank-order combine equal to the single-GPU layer and the
-oracle, and (with two or more GPUs) the NCCL expert-parallel layer on 2 ranks."""
+oracle, and (with two or more GPUs) the expert-parallel layer on 2 ranks with the NCCL and with the
+peer-memory exchange."""
 
 from __future__ import annotations
 
@@ -112,15 +113,18 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_nccl_expert_parallel_two_ranks(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_expert_parallel_two_ranks(tmp_path, exchange):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=f"{ROOT}:{ROOT / 'moe-offload-lab_b200'}")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
-           str(ROOT / "tests" / "ep_worker.py"), str(tmp_path)]
+           str(ROOT / "tests" / "ep_worker.py"), str(tmp_path), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     for rank in range(2):
         res = json.loads((tmp_path / f"rank{rank}.json").read_text())
+        assert res["exchange"] == exchange
         assert res["err_oracle"] < TOL, res
         assert res["err_single"] < 4e-3, res
-        assert res["miss"] == 0, res
+        assert res["err_repeat"] < 4e-3, res  # the second call reuses the exchange buffers
+        assert res["miss"] == 0 and res["status"] == 0, res

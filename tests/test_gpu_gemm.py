@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 ACTS = {"fp16": torch.float16, "bf16": torch.bfloat16}
 
 CASES = [
-    # (name, H, I, E, k, T, precs, policy, act, renorm, bias)
+    # (name, H, I, E, k, T, precs, policy, act, renorm, bias[, group size])
     ("small_int4_bf16", 256, 128, 8, 2, 40, ["int4"], dict(mode="lo"), "bf16", False, False),
     ("small_fp16_fp16", 256, 128, 8, 2, 40, ["fp16"], dict(mode="hi"), "fp16", False, False),
     ("small_int8_bf16", 256, 128, 8, 2, 40, ["int8"], dict(mode="lo"), "bf16", False, False),
@@ -27,15 +27,27 @@ CASES = [
     ("olmoe_T512_mix", 2048, 1024, 64, 8, 512, ["fp16", "int4"], dict(mode="hobbit", t1=0.6), "fp16", False, False),
     ("qwen3next_T1024_int8_int4", 2048, 512, 512, 10, 1024, ["int8", "int4"], dict(mode="hobbit", t1=0.6), "bf16",
      True, True),
+    # float records in the other 16-bit type and in fp32 (converted by the dequant warps)
+    ("bf16_records_fp16_acts", 512, 256, 8, 2, 96, ["bf16"], dict(mode="hi"), "fp16", False, False),
+    ("fp32_records_bf16_acts", 512, 256, 8, 2, 96, ["fp32"], dict(mode="hi"), "bf16", False, False),
+    ("fp16_fp32_mix_fp16", 256, 128, 8, 2, 64, ["fp16", "fp32"], dict(mode="hobbit", t1=0.6), "fp16", False, False),
+    # int4 rows of 704 bytes (a half raw unit at the end of every row of the down matrix)
+    ("int4_I1408_bf16", 512, 1408, 8, 2, 80, ["int4"], dict(mode="lo"), "bf16", False, False),
+    # groups smaller than a k-block: a scale per 8-column chunk
+    ("int4_gs32_fp16", 512, 256, 8, 2, 80, ["int4"], dict(mode="lo"), "fp16", False, False, 32),
+    ("int8_gs16_bf16", 512, 256, 8, 2, 80, ["int8"], dict(mode="lo"), "bf16", False, False, 16),
+    ("int8_gs128_int4_fp16", 1024, 512, 16, 4, 200, ["int8", "int4"], dict(mode="hobbit", t1=0.6), "fp16", True,
+     False, 128),
 ]
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_gemm_path_matches_oracle(cuda_dev, case):
-    name, H, I, E, k, T, precs, pol, act, renorm, bias = case
+    name, H, I, E, k, T, precs, pol, act, renorm, bias = case[:11]
+    gs = case[11] if len(case) > 11 else 64
     dt = ACTS[act]
     lays, recs = layer_records(precs, H, I, E, seed=zlib.crc32(name.encode()) % 1000, device=cuda_dev,
-                               std=0.02 if H > 256 else 0.05)
+                               std=0.02 if H > 256 else 0.05, group_size=gs)
     rt = B200Runtime(precs, lays, E, cuda_dev, ops.PolicySpec(**pol), layers=[0])
     for p in precs:
         for e in range(E):
