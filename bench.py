@@ -74,7 +74,7 @@ def parse():
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+    ap.add_argument("--exchange", default="nccl", choices=["p2p", "nccl"],
                     help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
                     help="--ncu mode: every pair at the most precise (hi) or least precise (lo) record")

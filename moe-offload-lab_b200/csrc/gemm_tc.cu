@@ -10,21 +10,21 @@
 // A tile is (work item, 128 weight rows); an item holds up to 128 routed pairs of one (expert,
 // precision), so N = pairs rounded up to 16. One CTA per SM works through its tiles with five roles
 // connected by shared-memory rings and mbarriers:
-//   warp 14    (TMA producer) points a tensor map at each tile's record (tensormap.replace on the
+//   warp 22    (TMA producer) points a tensor map at each tile's record (tensormap.replace on the
 //              device) and streams the tile's raw weight bytes through the RAW ring -- one unit is
 //              128 bytes of each of the 128 (up: 2 x 128) rows, a 128-byte-swizzled TMA box -- and
 //              the tile's whole scale rows into a double-buffered scale area (bulk copies). The ring
 //              runs ahead across tile boundaries, so DRAM latency is hidden by the ring depth;
-//   warps 0-7  dequantise each 64-column k-block from the raw ring into the A ring: 128-byte-swizzled
+//   warps 0-15 dequantise each 64-column k-block from the raw ring into the A ring: 128-byte-swizzled
 //              K-major bf16/fp16 tiles, with the rounding of moelab's materialize in the activation
 //              dtype ((q - 8) exact, times the fp16 scale converted to the activation type, one
 //              rounding; float records converted, or copied when the types agree);
-//   warp 12    fills the B ring: the N token rows of the k-block gathered with cp.async (up), or one
+//   warp 20    fills the B ring: the N token rows of the k-block gathered with cp.async (up), or one
 //              TMA box of the item's contiguous h rows (down);
-//   warp 13    allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accumulate) from one thread,
+//   warp 21    allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accumulate) from one thread,
 //              committing each A and B stage back to its producer and each finished tile to the
 //              epilogue (two TMEM accumulator buffers);
-//   warps 8-11 read the accumulators with tcgen05.ld and run the epilogue (up: SwiGLU into h; down:
+//   warps 16-19 read the accumulators with tcgen05.ld and run the epilogue (up: SwiGLU into h; down:
 //              the router-weighted fp32 reduction into acc, token rows and weights of the tile held
 //              in registers and broadcast with shuffles).
 // Every wait is bounded (status word + early exit), copies in flight are waited for before exit,
@@ -42,12 +42,12 @@ namespace {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // k-block: one 128-byte swizzle row of 16-bit values
 constexpr int NMAX = 128;        // max tokens per item (MMA N)
-constexpr int kDqWarps = 8;
-constexpr int kEpiWarp0 = 8;
-constexpr int kLoadWarp = 12;
-constexpr int kMmaWarp = 13;
-constexpr int kTmaWarp = 14;
-constexpr int kThreads = 15 * 32;
+constexpr int kDqWarps = 16;
+constexpr int kEpiWarp0 = 16;  // epilogue warps 16..19: TMEM lane quarter = warp % 4
+constexpr int kLoadWarp = 20;
+constexpr int kMmaWarp = 21;
+constexpr int kTmaWarp = 22;
+constexpr int kThreads = 23 * 32;
 constexpr int kTileBytes = BM * 128;  // one 128 x 64 16-bit operand tile = 128 rows x 128 raw bytes = 16 KB
 constexpr int kMaxSmem = 227 * 1024;
 
@@ -147,6 +147,11 @@ __device__ __forceinline__ void cp_async_wait_n(int n) {
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
   return v;
 }
 __device__ __forceinline__ uint16_t lds_u16(uint32_t a) {
@@ -284,9 +289,12 @@ struct Rings {
 };
 
 // ---- dequantisation of one tile: RAW ring -> A ring ------------------------------------------------
-// Thread (part, row, c0): up: part 0/1 = gate/up rows, every 8-column chunk of its row; down: two
-// threads per row, chunks c0..c0+3. Units of the RAW ring are waited in order; a k-block lies in the
-// last unit waited (16-bit and narrower records) or in the last two (fp32 records).
+// Thread (part, row, c0): up: part 0/1 = gate/up rows, two threads per row (chunks c0..c0+3); down:
+// four threads per row (chunks c0, c0+1). Sixteen warps keep enough independent dequantisation in
+// flight: with eight, each warp's dependent chain of shared loads, conversions and stores (about 200
+// instructions per k-block) set the pace at ~2,400 cycles per k-block, five times the MMA time.
+// Units of the RAW ring are waited in order; a k-block lies in the last unit waited (16-bit and
+// narrower records) or in the last two (fp32 records).
 template <typename AT, bool UP, int WT>
 __device__ __forceinline__ bool dq_tile(const TcTile& d, const TcGeo& g, const Rings& R, int nkb, int part, int row,
                                      int c0, uint32_t sarea, Ring& ar, Ring& rw, Ring& rr, int32_t* status,
@@ -294,9 +302,9 @@ __device__ __forceinline__ bool dq_tile(const TcTile& d, const TcGeo& g, const R
   constexpr int NA = UP ? 2 : 1;
   constexpr int WB = WT == MOEB200_I4 ? 4 : WT == MOEB200_I8 ? 8 : WT == MOEB200_F32 ? 32 : 16;
   constexpr int BPK = BK * WB / 8;  // raw bytes of a row per k-block
-  constexpr int NCH = UP ? 8 : 4;   // 8-column chunks per thread and k-block
+  constexpr int NCH = UP ? 4 : 2;   // 8-column chunks per thread and k-block
   constexpr int CB = WB;            // raw bytes of a chunk
-  constexpr int NV = NCH * CB / 16; // 16-byte raw vectors per thread and k-block
+  constexpr int NV = NCH * CB / 16; // 16-byte raw vectors per thread and k-block (int4 down: half of one)
   constexpr bool INT = WT == MOEB200_I4 || WT == MOEB200_I8;
   const uint32_t rslot = NA * kTileBytes;
   const uint32_t rrow = R.r + part * kTileBytes + row * 128;
@@ -339,6 +347,20 @@ __device__ __forceinline__ bool dq_tile(const TcTile& d, const TcGeo& g, const R
               Dq<AT>::pack_f32(__uint_as_float(v0.z), __uint_as_float(v0.w)),
               Dq<AT>::pack_f32(__uint_as_float(v1.x), __uint_as_float(v1.y)),
               Dq<AT>::pack_f32(__uint_as_float(v1.z), __uint_as_float(v1.w)));
+      }
+    } else if constexpr (WT == MOEB200_I4 && NV == 0) {
+      // two chunks = 8 bytes
+      const int o = lo + c0 * CB;
+      const uint32_t ub = ((o >> 7) == waited - 1) ? cur : prev;
+      const uint2 v = lds64(rrow + ub + ((((o & 127) >> 4) ^ rsw) << 4) + (o & 15));
+      const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int c = c0 + q;
+        if (!one_scale) s2 = scale2<AT>(lds_u16(srow + ((kb * BK + c * 8) / d.gs) * 2));
+        uint32_t out[4];
+        dq_int4_chunk<AT>(w[q], s2, out);
+        sts16(swz(atile, row, c), out[0], out[1], out[2], out[3]);
       }
     } else {
 #pragma unroll
@@ -477,9 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kDqWarps) {
     // ---------------- dequantisers ----------------
     const int tid = threadIdx.x;
-    const int part = UP ? tid >> 7 : 0;
-    const int row = UP ? tid & 127 : tid >> 1;
-    const int c0 = UP ? 0 : (tid & 1) * 4;
+    const int part = UP ? tid >> 8 : 0;
+    const int row = UP ? (tid >> 1) & 127 : tid >> 2;
+    const int c0 = UP ? (tid & 1) * 4 : (tid & 3) * 2;
     Ring ar, rw, rr;
     uint32_t sj = 0;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
@@ -747,7 +769,9 @@ bool plan_geo(bool up, uint32_t s_bytes, TcGeo& g, int& smem) {
     const uint32_t nbars = 2 * (g.a_st + g.b_st + g.r_st) + 9;
     smem = (int)(g.bar_off + nbars * 8 + 16 + 1024);
     if (smem <= kMaxSmem) {
-      g.lag = g.b_st - 1;
+      // the loader signals stage kb after issuing kb + lag, which needs stage kb + lag - b_st free:
+      // lag = b_st - 2 leaves the MMA one stage of slack
+      g.lag = std::max(0, g.b_st - 2);
       g.tmap_ring = g.r_st + 1;
       return true;
     }
