@@ -135,19 +135,17 @@ struct Scales {
 };
 
 template <int NB>
-__device__ __forceinline__ void fold_scaled(float (&tot)[2][NB][4], const float (&d)[2][NB][2][4],
-                                            const float (&s)[2][2]) {
+__device__ __forceinline__ void fold_one(float (&tot)[2][NB][4], const float (&d)[2][NB][4], const float (&s)[2][2]) {
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
-      tot[rt][nb][0] = fmaf(s[rt][0], d[rt][nb][0][0] + d[rt][nb][1][0], tot[rt][nb][0]);
-      tot[rt][nb][1] = fmaf(s[rt][0], d[rt][nb][0][1] + d[rt][nb][1][1], tot[rt][nb][1]);
-      tot[rt][nb][2] = fmaf(s[rt][1], d[rt][nb][0][2] + d[rt][nb][1][2], tot[rt][nb][2]);
-      tot[rt][nb][3] = fmaf(s[rt][1], d[rt][nb][0][3] + d[rt][nb][1][3], tot[rt][nb][3]);
+      tot[rt][nb][0] = fmaf(s[rt][0], d[rt][nb][0], tot[rt][nb][0]);
+      tot[rt][nb][1] = fmaf(s[rt][0], d[rt][nb][1], tot[rt][nb][1]);
+      tot[rt][nb][2] = fmaf(s[rt][1], d[rt][nb][2], tot[rt][nb][2]);
+      tot[rt][nb][3] = fmaf(s[rt][1], d[rt][nb][3], tot[rt][nb][3]);
     }
 }
-
 // ---- one chunk per lane --------------------------------------------------------------------------------
 // wr[rt][hh]: shared address of the start of the lane's weight row g + 8*hh of row tile rt in the
 // weight tile; so0/so1: swizzled offsets of the lane's bytes of the chunk in those rows (ldw);
@@ -165,7 +163,7 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
   {
-    float d[2][NB][2][4];
+    float d[2][NB][4];
 #pragma unroll
     for (int j = 0; j < WPL; ++j) {
       uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
@@ -183,19 +181,17 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
         for (int rt = 0; rt < 2; ++rt) {
           const uint32_t a0[4] = {p04[rt][0], p04[rt][1], p15[rt][0], p15[rt][1]};
           const uint32_t a1[4] = {p26[rt][0], p26[rt][1], p37[rt][0], p37[rt][1]};
-          if (j == 0) {
-            MmaOp<AT>::first(d[rt][nb][0], a0, b00, b01);
-            MmaOp<AT>::first(d[rt][nb][1], a1, b10, b11);
-          } else {
-            MmaOp<AT>::run(d[rt][nb][0], a0, b00, b01);
-            MmaOp<AT>::run(d[rt][nb][1], a1, b10, b11);
-          }
+          if (j == 0)
+            MmaOp<AT>::first(d[rt][nb], a0, b00, b01);
+          else
+            MmaOp<AT>::run(d[rt][nb], a0, b00, b01);
+          MmaOp<AT>::run(d[rt][nb], a1, b10, b11);
         }
       }
     }
     float s[2][2];
     S.f32(gi, s);
-    fold_scaled<NB>(tot, d, s);
+    fold_one<NB>(tot, d, s);
   }
 }
 
@@ -210,7 +206,7 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
   {
-    float d[2][NB][2][4];
+    float d[2][NB][4];
 #pragma unroll
     for (int m = 0; m < WPL; ++m) {
       uint32_t p01[2][2], p23[2][2];
@@ -223,23 +219,15 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
         for (int rt = 0; rt < 2; ++rt) {
           const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
-          if (m < 2)
-            MmaOp<AT>::first(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
+          if (m == 0)
+            MmaOp<AT>::first(d[rt][nb], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
           else
-            MmaOp<AT>::run(d[rt][nb][m & 1], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
+            MmaOp<AT>::run(d[rt][nb], a, xb[nb][2 * m], xb[nb][2 * m + 1]);
         }
-    }
-    if (WPL == 1) {  // only the first accumulator set was written
-#pragma unroll
-      for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d[rt][nb][1][i] = 0.f;
     }
     float s[2][2];
     S.f32(gi, s);
-    fold_scaled<NB>(tot, d, s);
+    fold_one<NB>(tot, d, s);
   }
 }
 
