@@ -27,6 +27,20 @@ __device__ __forceinline__ float round_act(float v) {
 // accumulates the columns l*8 + 256*i + j in that order in its own fp32 FMA chain; an xor butterfly
 // over offsets 16..1 adds the 32 lane sums. The arithmetic of each logit is therefore the same for
 // every tile shape (bit-exact with the single-token form).
+// element j (0..7) of 8 packed 16-bit values, as fp32
+template <typename AT>
+__device__ __forceinline__ float elem8(const uint4& v, int j);
+template <>
+__device__ __forceinline__ float elem8<__nv_bfloat16>(const uint4& v, int j) {
+  const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+  return __uint_as_float((j & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+template <>
+__device__ __forceinline__ float elem8<__half>(const uint4& v, int j) {
+  const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+  return __half2float(__ushort_as_half((unsigned short)((j & 1) ? (w >> 16) : (w & 0xffffu))));
+}
+
 template <typename AT, int RE, int RT, int EG>
 __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict__ h, const AT* __restrict__ wr,
                                                             int T, int H, int E, float* __restrict__ logits) {
@@ -41,29 +55,28 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict
   for (int r = 0; r < RE; ++r)
 #pragma unroll
     for (int q = 0; q < RT; ++q) acc[r][q] = 0.f;
-#pragma unroll 4
+  // raw 16-byte words of the step, converted element by element (a tile of RE x RT keeps RE + RT
+  // words, not RE * 8 converted floats, in registers)
+#pragma unroll 2
   for (int c = lane * 8; c < H; c += 256) {
-    float wf[RE][8];
+    uint4 wv[RE], xv[RT];
 #pragma unroll
-    for (int r = 0; r < RE; ++r) {
-      uint4 wv = make_uint4(0u, 0u, 0u, 0u);
-      if (r < ne) wv = __ldg(reinterpret_cast<const uint4*>(wr + (int64_t)(e0 + r) * H + c));
-      const AT* wa = reinterpret_cast<const AT*>(&wv);
+    for (int r = 0; r < RE; ++r)
+      wv[r] = r < ne ? __ldg(reinterpret_cast<const uint4*>(wr + (int64_t)(e0 + r) * H + c)) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) wf[r][i] = to_f32<AT>(wa[i]);
-    }
+    for (int q = 0; q < RT; ++q)
+      xv[q] = q < nt ? __ldg(reinterpret_cast<const uint4*>(h + (int64_t)(t0 + q) * H + c)) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-    for (int q = 0; q < RT; ++q) {
-      if (q < nt) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(h + (int64_t)(t0 + q) * H + c));
-        const AT* xa = reinterpret_cast<const AT*>(&xv);
+    for (int j = 0; j < 8; ++j) {
+      float wf[RE], xf[RT];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xf = to_f32<AT>(xa[i]);
+      for (int r = 0; r < RE; ++r) wf[r] = elem8<AT>(wv[r], j);
 #pragma unroll
-          for (int r = 0; r < RE; ++r) acc[r][q] = fmaf(xf, wf[r][i], acc[r][q]);
-        }
-      }
+      for (int q = 0; q < RT; ++q) xf[q] = elem8<AT>(xv[q], j);
+#pragma unroll
+      for (int r = 0; r < RE; ++r)
+#pragma unroll
+        for (int q = 0; q < RT; ++q) acc[r][q] = fmaf(xf[q], wf[r], acc[r][q]);
     }
   }
 #pragma unroll
@@ -581,22 +594,30 @@ cudaError_t launch_router(const void* h, const void* wr, const float* bias, int 
   dim3 grid((E + 7) / 8, (T + tpb - 1) / tpb);
   // few (token, expert) logits: one expert x 4 tokens per warp (8 experts per block) keeps every SM
   // busy; many: 4 x 8 per warp (8 x 32 per block) cuts the L2 re-reads of token and router rows
+  // prefill-sized: 8 x 8 per warp (16 experts x 32 tokens per block) keeps 64 FMA chains per lane
+  const bool huge = (int64_t)T * E >= 262144;
   const bool big = (int64_t)T * E >= 65536;
-  const dim3 g16 = big ? dim3((E + 7) / 8, (T + 31) / 32) : dim3((E + 7) / 8, (T + 3) / 4);
+  const dim3 g16 = huge  ? dim3((E + 15) / 16, (T + 31) / 32)
+                   : big ? dim3((E + 7) / 8, (T + 31) / 32)
+                         : dim3((E + 7) / 8, (T + 3) / 4);
   if (act_type == MOEB200_F16) {
-    if (big)
-      router_logits_kernel<__half, 4, 8, 2><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
-                                                                static_cast<const __half*>(wr), T, H, E, logits);
+    const __half* ha = static_cast<const __half*>(h);
+    const __half* wa = static_cast<const __half*>(wr);
+    if (huge)
+      router_logits_kernel<__half, 8, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+    else if (big)
+      router_logits_kernel<__half, 4, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
     else
-      router_logits_kernel<__half, 1, 4, 8><<<g16, 256, 0, s>>>(static_cast<const __half*>(h),
-                                                                static_cast<const __half*>(wr), T, H, E, logits);
+      router_logits_kernel<__half, 1, 4, 8><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
   } else if (act_type == MOEB200_BF16) {
-    if (big)
-      router_logits_kernel<__nv_bfloat16, 4, 8, 2><<<g16, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
+    const __nv_bfloat16* ha = static_cast<const __nv_bfloat16*>(h);
+    const __nv_bfloat16* wa = static_cast<const __nv_bfloat16*>(wr);
+    if (huge)
+      router_logits_kernel<__nv_bfloat16, 8, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+    else if (big)
+      router_logits_kernel<__nv_bfloat16, 4, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
     else
-      router_logits_kernel<__nv_bfloat16, 1, 4, 8><<<g16, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
+      router_logits_kernel<__nv_bfloat16, 1, 4, 8><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
   } else
     router_logits_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(h), static_cast<const float*>(wr), T, H,
                                                   E, tpb, logits);

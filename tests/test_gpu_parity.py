@@ -81,7 +81,9 @@ def test_expert_ffn_int4_single(cuda_dev):
 @pytest.mark.parametrize("act", ["fp16", "bf16"])
 @pytest.mark.parametrize("T,E,k,renorm,bias", [(1, 64, 8, False, False), (37, 64, 8, False, False),
                                                (64, 128, 8, True, True), (5, 512, 10, True, True),
-                                               (300, 512, 10, True, False)])
+                                               (300, 512, 10, True, False),
+                                               # prefill tiles (8 experts x 8 tokens per warp), full and ragged
+                                               (2048, 128, 8, True, True), (600, 500, 10, True, False)])
 def test_router_matches_oracle(cuda_dev, act, T, E, k, renorm, bias):
     dt = ACTS[act]
     H = 2048
