@@ -301,7 +301,7 @@ class Stack:
 
         cfg = self.cfg
         P = len(cfg["precs"])
-        out = {"up": 0, "down": 0, "records": 0, "pairs": 0}
+        out = {"up": 0, "down": 0, "records": 0, "pairs": 0, "up_layers": [], "down_layers": []}
         gu_bytes, dn_bytes = {}, {}
         for p in cfg["precs"]:
             lay = self.lays[p]
@@ -329,10 +329,15 @@ class Stack:
                     slot = min(lv, P - 1) if P >= 3 else (0 if lv == 0 else P - 1)
                     used.add((int(idx[t, j]), slot))
                     out["pairs"] += 1
-            for (_, s) in used:
-                p = cfg["precs"][s]
-                out["up"] += gu_bytes[p]
-                out["down"] += dn_bytes[p]
+            pairs_l = out["pairs"] - sum(out.get("_pairs_prev", [0]))
+            out.setdefault("_pairs_prev", []).append(pairs_l)
+            up_l = sum(gu_bytes[cfg["precs"][s]] for (_, s) in used)
+            dn_l = sum(dn_bytes[cfg["precs"][s]] for (_, s) in used)
+            out["up"] += up_l
+            out["down"] += dn_l
+            # one gate/up launch: its records + the layer's token rows + the h rows it writes
+            out["up_layers"].append(up_l + T * H * 2 + pairs_l * I * 2)
+            out["down_layers"].append(dn_l + pairs_l * I * 2 + T * H * 4)
             out["records"] += len(used)
         for rec, lay, _, _ in self.shared:
             p = lay["precision"]
@@ -340,6 +345,7 @@ class Stack:
             out["down"] += dn_bytes[p]
             out["records"] += 1
             out["shared_pairs"] = out.get("shared_pairs", 0) + T
+        out.pop("_pairs_prev", None)
         n_pairs = out["pairs"] + out.get("shared_pairs", 0)
         out["up_total"] = out["up"] + cfg["layers"] * T * H * 2 + n_pairs * I * 2
         out["down_total"] = out["down"] + n_pairs * I * 2 + cfg["layers"] * T * H * 4
@@ -601,7 +607,9 @@ def main():
         step()
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
-        print(json.dumps({"ncu_step_done": True, "layers": cfg["layers"], "T": T}))
+        rb = stack.routing_bytes()
+        print(json.dumps({"ncu_step_done": True, "layers": cfg["layers"], "T": T,
+                          "up_alg_bytes_per_layer": rb["up_layers"], "down_alg_bytes_per_layer": rb["down_layers"]}))
         return
     H = CFG1["H"]
     torch.manual_seed(1234 + rank)
@@ -632,13 +640,17 @@ def main():
     dn_bytes_launch = rb["down_total"] / L
     up_gbs = up_bytes_launch / (up_ms / 1e3) / 1e9
     dn_gbs = dn_bytes_launch / (dn_ms / 1e3) / 1e9
-    # DRAM bytes (read + write) of one gate/up launch from the committed ncu capture of this workload
+    # DRAM bytes (read + write) of one gate/up launch: the committed ncu capture of this workload's
+    # layer 0 (a 2-layer stack), scaled from that launch's algorithmic bytes to this run's average
+    # launch (DRAM traffic follows the records a layer routes to)
     traffic, traffic_src = None, None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists() and world == 1 and T == CFG1["T"]:
         rec = json.loads(tf.read_text()).get("gemv_up_c1_T64")
         if rec:
-            traffic, traffic_src = rec["bytes"], rec["source"]
+            traffic = rec["dram_bytes"] * up_bytes_launch / rec["alg_bytes"]
+            traffic_src = (rec["source"] + f"; captured launch: {rec['dram_bytes']} DRAM bytes for {rec['alg_bytes']} "
+                           "algorithmic bytes, scaled to this run's average launch")
 
     # sweep of other decode batches (device-resident value only)
     sweep = {}
