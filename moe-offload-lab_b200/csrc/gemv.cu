@@ -454,16 +454,36 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     uint32_t it = 0, sj = 0, jn = 0;
     bool ok = true;
     Item nxt = load_item(p, blockIdx.x, n_jobs, rb_per_item, ks_n);
-    for (int job = blockIdx.x; job < n_jobs && ok; job += gridDim.x) {
-      Job d;
-      describe_job<UP>(p, job, nxt, rb_per_item, ks_n, d);
-      nxt = load_item(p, job + gridDim.x, n_jobs, rb_per_item, ks_n);  // in flight during this job
-      if (d.nsteps == 0) continue;
-      // tensor map of the job's weight field (a ring of four per CTA: the copies that used a slot
-      // four jobs ago have landed, the stage ring being two deep)
-      const uint64_t gdesc = reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (jn & 3)) * 128;
+    // describes the first non-empty job at index >= j (j advances to it); the item of the job after
+    // it is loaded meanwhile
+    auto next_job = [&](int& j, Job& out) -> bool {
+      for (; j < n_jobs; j += gridDim.x) {
+        describe_job<UP>(p, j, nxt, rb_per_item, ks_n, out);
+        nxt = load_item(p, j + gridDim.x, n_jobs, rb_per_item, ks_n);
+        if (out.nsteps > 0) return true;
+      }
+      return false;
+    };
+    // tensor maps of the jobs' weight fields: a ring of four per CTA. Each job's map is pointed at
+    // its record while the previous job streams (after that job's first stage is issued), so small
+    // jobs do not wait for the retarget; a slot is rewritten four jobs after its last use, when its
+    // copies have landed (the stage ring is two deep)
+    auto map_slot = [&](uint32_t n) {
+      return reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (n & 3)) * 128;
+    };
+    int job = blockIdx.x;
+    Job d;
+    bool has = next_job(job, d);
+    uint64_t gdesc = 0;
+    if (has) {
+      gdesc = map_slot(jn++);
       retarget_tmap(tm.m[d.slot], smem_u32(sdesc), gdesc, d.q, lane);
-      ++jn;
+    }
+    while (has && ok) {
+      int jnext = job + gridDim.x;
+      Job dn;
+      bool hn = false;
+      uint64_t gnext = 0;
       // token rows of the item (one per lane)
       const AT* brow = nullptr;
       if (lane < d.ntok) {
@@ -512,7 +532,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         __syncwarp();
         if (lane < d.ntok)
           bulk_g2s(stages + sidx * p.stage_bytes + kGemvWBytes + lane * p.b_stride, brow + col0, bseg, &full[sidx]);
+        if (step == 0) {  // the next job's map, while this job's first stage lands
+          hn = next_job(jnext, dn);
+          if (hn) {
+            gnext = map_slot(jn++);
+            retarget_tmap(tm.m[dn.slot], smem_u32(sdesc), gnext, dn.q, lane);
+          }
+        }
       }
+      d = dn;
+      job = jnext;
+      gdesc = gnext;
+      has = hn;
     }
     // the CTA must not exit with copies in flight: wait for the last stages issued (consumed
     // already in the normal flow; after a failed wait they may still be landing)
@@ -752,7 +783,7 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   // several-fold in bytes; more, smaller jobs balance the CTAs; up: only with room for pre)
   int ks = 1;
   const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
-  while (can_split && ks < 8 && jobs1 * ks < 4ll * sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
+  while (can_split && ks < 8 && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
   if (up)
     p.ksplit_up = ks;
   else
