@@ -78,7 +78,8 @@ def parse():
                     help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
                     help="--ncu mode: every pair at the most precise (hi) or least precise (lo) record")
-    ap.add_argument("--extra", default="c0,c2,c3,c3p,c4", help="single-layer configs measured beside the headline")
+    ap.add_argument("--extra", default="c0,c2,c3,c3p,c4,dense",
+                    help="single-layer configs (and the dense int8 GEMV) measured beside the headline")
     return ap.parse_args()
 
 
@@ -452,6 +453,34 @@ def h2d_peak_gbs(dev, nbytes: int = 256 << 20) -> float:
     return best
 
 
+def measure_dense(dev, steps: int, warmup: int, peaks: dict) -> dict:
+    """The dense int8 GEMV (B200QLinear decode path) on the OLMoE output head shape: 50304 x 2048
+    int8 gs64, one token, fp16 -- the largest dense layer read per decoded token (103 MB)."""
+    from moeb200 import format as Fmt
+    from moeb200 import ops
+
+    O, K, gs = 50304, 2048, 64
+    g = torch.Generator(device=dev).manual_seed(3)
+    w = torch.randn(O, K, generator=g, device=dev) * 0.02
+    q, s = Fmt.quantize(w, 8, gs)
+    del w
+    x = torch.randn(1, K, generator=g, device=dev).half()
+    y = torch.empty(1, O, dtype=torch.float16, device=dev)
+
+    def step():
+        ops.dense_int8_gemv(q, s, gs, x, out=y)
+
+    gr, ms = time_graph(step, steps, warmup, 1)
+    del gr
+    nbytes = q.numel() + s.numel() * 2 + K * 2 + O * 2
+    gbs = nbytes / (ms / 1e3) / 1e9
+    peak = peaks.get("hbm_gbs", 6650.0)
+    return {"workload": "dense int8 GEMV, OLMoE output head 50304x2048 gs64, T=1, fp16", "ms_per_call": ms,
+            "bytes_per_call": nbytes, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                                   "frac": gbs / peak},
+            "timing": "CUDA graph replay of one call (weights 103 MB > L2), CUDA events"}
+
+
 def measure_cold(cfg: dict, dev, steps: int, warmup: int) -> dict:
     """Config 4: every step routes T tokens, uploads the routed cold records from pinned host memory
     on a copy stream while the resident pairs run, then runs the uploaded pairs. Eager steps (one
@@ -696,6 +725,9 @@ def main():
 
     extra = {}
     for name in [c for c in args.extra.split(",") if c and world == 1]:
+        if name == "dense":
+            extra[name] = measure_dense(dev, max(20, args.steps), 5, peaks)
+            continue
         cfgx = CONFIGS[name]
         if cfgx.get("cold_frac"):
             extra[name] = measure_cold(cfgx, dev, max(5, args.steps // 2), 3)

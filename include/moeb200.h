@@ -227,6 +227,21 @@ int moeb200_ep_gather(const moeb200_peer_group* group, int32_t act_type, void* x
                       uint8_t* level, uint8_t* skip, void* stream);
 int moeb200_ep_combine_peers(const moeb200_peer_group* group, int32_t act_type, void* out, int32_t add, void* stream);
 
+/* ---- dense int8 layers ------------------------------------------------------------------------
+ * Replace moelab's QLinear (denseq.py:60-104), the non-expert nn.Linear layers quantised to int8
+ * with one fp16 scale per group of gs input columns (quant.py `quantize(w, 8, gs)`):
+ *   q [O, K] int8 (row-major), s [O, K/gs] fp16 bits.
+ * moeb200_dense_int8_gemv replaces the one-token Triton kernel `_gemv8` (denseq.py:34-57) for up to 8
+ * tokens: y[t, o] = act(sum_g s[o,g] * sum_{c in g} q[o,c] * x[t,c]) (fp32 accumulation), then
+ * + bias[o] in the activation type when bias (act_type, [O]) is not NULL. x [T, K], y [T, O];
+ * gs a multiple of 16 dividing K; q and x 16-byte aligned.
+ * moeb200_dense_int8_dequant is the prefill half (denseq.py:94-100 + quant.py:191-205): w [O, K] =
+ * act(q) * act(s) rounded once, the exact values of moelab's dequantize(q, s, 8, dtype). */
+int moeb200_dense_int8_gemv(const int8_t* q, const uint16_t* s, int32_t O, int32_t K, int32_t gs, const void* x,
+                            int32_t act_type, int32_t T, const void* bias, void* y, void* stream);
+int moeb200_dense_int8_dequant(const int8_t* q, const uint16_t* s, int32_t O, int32_t K, int32_t gs,
+                               int32_t act_type, void* w, void* stream);
+
 /* ---- shared expert ---------------------------------------------------------------------------
  * Replaces the shared-expert branch of Qwen3NextSparseMoeBlock.forward
  * (qwen3_next/modeling_qwen3_next.py:789-801), which runs beside the experts module:

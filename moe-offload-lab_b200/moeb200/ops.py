@@ -284,3 +284,36 @@ def check_workspace(ws: torch.Tensor) -> int:
     st = C.c_int32(0)
     _lib.check(_lib.lib().moeb200_check_workspace(_ptr(ws), C.byref(st), _stream(ws.device)))
     return st.value
+
+
+def dense_int8_gemv(q: torch.Tensor, s: torch.Tensor, group_size: int, x: torch.Tensor,
+                    bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [T, O] = x [T, K] @ dequant(q, s).T (+ bias) for T <= 8 tokens; q int8 [O, K], s fp16 [O, K/gs]."""
+    _need_cuda(q, s, x, bias, out)
+    O, K = q.shape
+    T = x.shape[0]
+    if q.dtype != torch.int8 or s.dtype != torch.float16 or s.shape != (O, K // group_size):
+        raise ValueError("q must be int8 [O, K] and s float16 [O, K/gs]")
+    if not (q.is_contiguous() and s.is_contiguous() and x.is_contiguous()) or x.shape[1] != K:
+        raise ValueError("q, s and x [T, K] must be contiguous")
+    if bias is not None and (bias.dtype != x.dtype or bias.shape != (O,) or not bias.is_contiguous()):
+        raise ValueError("bias must be contiguous [O] in the activation dtype")
+    if out is None:
+        out = torch.empty(T, O, dtype=x.dtype, device=x.device)
+    _lib.check(_lib.lib().moeb200_dense_int8_gemv(_ptr(q), _ptr(s), O, K, group_size, _ptr(x), _act(x.dtype), T,
+                                                  _ptr(bias), _ptr(out), _stream(x.device)))
+    return out
+
+
+def dense_int8_dequant(q: torch.Tensor, s: torch.Tensor, group_size: int, dtype: torch.dtype,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """w [O, K] in dtype = the exact values of moelab's dequantize(q, s, 8, dtype)."""
+    _need_cuda(q, s, out)
+    O, K = q.shape
+    if out is None:
+        out = torch.empty(O, K, dtype=dtype, device=q.device)
+    if not (q.is_contiguous() and s.is_contiguous() and out.is_contiguous()) or out.shape != (O, K):
+        raise ValueError("q, s and out must be contiguous, out [O, K]")
+    _lib.check(_lib.lib().moeb200_dense_int8_dequant(_ptr(q), _ptr(s), O, K, group_size, _act(out.dtype), _ptr(out),
+                                                     _stream(q.device)))
+    return out

@@ -485,6 +485,34 @@ def moe_layer(x: np.ndarray, idx: np.ndarray, w: np.ndarray, slot: np.ndarray | 
     return out
 
 
+# ---------------------------------------------------------------------------------------------
+# Dense int8 layers (moelab/denseq.py)
+# ---------------------------------------------------------------------------------------------
+
+def dense_int8_dequant(q: np.ndarray, scales: np.ndarray, dtype: str) -> np.ndarray:
+    """moelab's dequantize(q, s, 8, dtype) (quant.py:191-205) as float32 values: q and the fp16
+    scale are each converted to `dtype` (q exactly), and their product is rounded once to `dtype`."""
+    out_f, in_f = q.shape
+    gs = in_f // scales.shape[1]
+    qv = round_to(q.astype(np.float32), dtype)
+    sv = round_to(scales.astype(np.float32), dtype)
+    prod = qv.reshape(out_f, in_f // gs, gs) * sv[..., None]  # exact in fp32 (8-bit x 11-bit)
+    return round_to(prod.reshape(out_f, in_f), dtype)
+
+
+def dense_int8_linear(x: np.ndarray, q: np.ndarray, scales: np.ndarray, bias: np.ndarray | None,
+                      dtype: str) -> np.ndarray:
+    """QLinear.forward for one decode batch (denseq.py:89-102 with the GEMV `_gemv8`, 34-57): the
+    float32 dot products of the int8 weights times their group scales with x, rounded to the
+    activation dtype, then + bias in that dtype. Computed in float64 here (the kernel sums in fp32
+    in its own order; parity is a tolerance)."""
+    w = dequantize(q.view(np.int8) if q.dtype != np.int8 else q, scales, 8).astype(np.float64)
+    y = round_to((x.astype(np.float64) @ w.T).astype(np.float32), dtype)
+    if bias is not None:
+        y = round_to(y + round_to(bias, dtype), dtype)
+    return y
+
+
 def max_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
     """max |got - ref| / max |ref| -- the metric of the reference's kernel tests
     (tests/test_kernels.py:49)."""

@@ -215,6 +215,23 @@ for p in precs:
     out[f"layer/{p}"] = np.stack([b.numpy() for b in recs[p]])
 meta["cases"]["layer"] = {"T": T, "H": H, "I": I, "E": E, "k": k, "precs": precs}
 
+# -- dense int8 layers (moelab/denseq.py QLinear, CPU path: dequantize + F.linear) -----------------
+from moelab.denseq import QLinear  # noqa: E402
+from moelab.quant import dequantize  # noqa: E402
+
+torch.manual_seed(13)
+lin = torch.nn.Linear(256, 96, bias=True)
+ql = QLinear.from_linear(lin, "cpu", 64)
+out["dense/w"] = lin.weight.data.numpy()
+out["dense/q"], out["dense/s"] = ql.q.numpy(), ql.s.numpy()
+out["dense/bias"] = ql.bias.data.numpy()
+for name, dt in (("fp16", torch.float16), ("bf16", torch.bfloat16)):
+    out[f"dense/w_{name}"] = dequantize(ql.q, ql.s, 8, dt).view(torch.int16).numpy()
+xd = torch.randn(3, 256)
+out["dense/x"] = xd.numpy()
+out["dense/y_f32"] = ql(xd).detach().numpy()
+meta["cases"]["dense"] = {"O": 96, "K": 256, "gs": ql.group_size}
+
 np.savez_compressed(HERE / "golden.npz", **out)
 (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1))
 print("wrote", HERE / "golden.npz", sum(v.nbytes for v in out.values()) // 1024, "KiB raw")

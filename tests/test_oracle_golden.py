@@ -188,3 +188,27 @@ def test_layer_matches_reference_cpu_path(golden, golden_meta):
     slot = np.vectorize(lambda v: O.level_to_slot(int(v), len(precs)))(lvl)
     got = O.moe_layer(golden["layer/x"], golden["layer/idx"], golden["layer/w"], slot, None, recs, lays, m["E"])
     assert O.max_rel_err(got, golden["layer/ref"]) < 1e-5
+
+
+# -- dense int8 layers --------------------------------------------------------------------------------
+@pytest.mark.parametrize("name,dt", [("fp16", "float16"), ("bf16", "bfloat16")])
+def test_dense_dequant_matches_reference(golden, name, dt):
+    got = O.dense_int8_dequant(golden["dense/q"], golden["dense/s"], dt)
+    ref = golden[f"dense/w_{name}"]  # moelab dequantize(q, s, 8, dtype) bit patterns
+    bits = got.astype(np.float16).view(np.int16) if dt == "float16" else (O.f32_to_bf16_bits(got)).view(np.int16)
+    assert np.array_equal(bits, ref)
+
+
+def test_dense_linear_matches_reference_qlinear(golden):
+    q = golden["dense/q"]
+    # the oracle in float32 activations: the reference QLinear on the CPU (dequantise + F.linear)
+    got = O.dense_int8_linear(golden["dense/x"], q, golden["dense/s"], golden["dense/bias"], "float32")
+    ref = golden["dense/y_f32"]
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_dense_quantize_matches_reference(golden):
+    # QLinear.from_linear (denseq.py:81-87) quantises with absmax scales: quant.quantize(w, 8, gs)
+    q, s = O.quantize(golden["dense/w"], 8, 64, "absmax")
+    assert np.array_equal(q, golden["dense/q"])
+    assert np.array_equal(s.view(np.uint16), golden["dense/s"].view(np.uint16))
