@@ -242,6 +242,15 @@ int moeb200_dense_int8_gemv(const int8_t* q, const uint16_t* s, int32_t O, int32
 int moeb200_dense_int8_dequant(const int8_t* q, const uint16_t* s, int32_t O, int32_t K, int32_t gs,
                                int32_t act_type, void* w, void* stream);
 
+/* ---- record quantiser -------------------------------------------------------------------------
+ * moelab's quantize(w, bits, gs, method) (quant.py:104-127) on the device: w [O, K] (w_type F32, F16 or
+ * BF16) -> q (bits 8: int8 [O, K]; bits 4: uint8 [O, K/2], +8, low nibble = even column) and fp16
+ * scales s [O, K/gs]. method 0 = "absmax", 1 = "mse" (quant.py:64-93 scale search). fp32 arithmetic
+ * with IEEE division; the mse error sums are added in numpy's pairwise order. gs <= 256 (even for
+ * int4) dividing K. */
+int moeb200_quantize(const void* w, int32_t w_type, int32_t O, int32_t K, int32_t bits, int32_t gs, int32_t method,
+                     void* q, uint16_t* s, void* stream);
+
 /* ---- shared expert ---------------------------------------------------------------------------
  * Replaces the shared-expert branch of Qwen3NextSparseMoeBlock.forward
  * (qwen3_next/modeling_qwen3_next.py:789-801), which runs beside the experts module:

@@ -80,6 +80,8 @@ _SIGS = {
     "moeb200_dense_int8_gemv": (C.c_int, [_P, _P, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int32, _P,
                                           _P, _P]),
     "moeb200_dense_int8_dequant": (C.c_int, [_P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
+    "moeb200_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P,
+                                   _P]),
     "moeb200_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), _P]),
     "moeb200_peer_open": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
     "moeb200_peer_close": (C.c_int, [_P]),

@@ -190,6 +190,27 @@ def views(layout: dict, blob: torch.Tensor) -> dict[str, torch.Tensor]:
     return out
 
 
+def encode_record_device(layout: dict, gate_up: torch.Tensor, down: torch.Tensor,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+    """encode_record with the integer records quantised by the B200 quantiser (moeb200_quantize):
+    one kernel per matrix instead of the scale search's tensor passes; CUDA tensors only."""
+    from . import ops
+
+    spec = PRECISIONS[layout["precision"]]
+    if spec["kind"] == "float":
+        return encode_record(layout, gate_up, down, out)
+    buf = out if out is not None else torch.empty(layout["record_bytes"], dtype=torch.uint8, device=gate_up.device)
+    buf.zero_()
+    v = views(layout, buf)
+    method = layout.get("scale") or "absmax"
+    method = "absmax" if method == "gptq" else method
+    for name, w in (("gate_up", gate_up), ("down", down)):
+        q, s = ops.quantize(w.contiguous(), spec["bits"], layout["group_sizes"][name], method)
+        v[f"{name}.q"].copy_(q.view(v[f"{name}.q"].dtype))
+        v[f"{name}.s"].copy_(s)
+    return buf
+
+
 def encode_record(layout: dict, gate_up: torch.Tensor, down: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Record bytes from float weights, on the weights' device (moelab/store.py:122-150).
     `out` (uint8, record_bytes) is filled in place when given."""

@@ -317,3 +317,21 @@ def dense_int8_dequant(q: torch.Tensor, s: torch.Tensor, group_size: int, dtype:
     _lib.check(_lib.lib().moeb200_dense_int8_dequant(_ptr(q), _ptr(s), O, K, group_size, _act(out.dtype), _ptr(out),
                                                      _stream(q.device)))
     return out
+
+
+def quantize(w: torch.Tensor, bits: int, group_size: int, method: str = "absmax") -> tuple[torch.Tensor, torch.Tensor]:
+    """moelab's quantize(w, bits, gs, method) on the device: (q, fp16 scales [O, K/gs]); q is int8 [O, K]
+    (bits 8) or uint8 [O, K/2] (bits 4, two values per byte)."""
+    _need_cuda(w)
+    if w.dim() != 2 or not w.is_contiguous():
+        raise ValueError("w must be a contiguous [O, K] matrix")
+    O, K = w.shape
+    wt = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}.get(w.dtype)
+    if wt is None:
+        raise ValueError("w must be float32, float16 or bfloat16")
+    m = {"absmax": 0, "mse": 1}[method]
+    q = torch.empty(O, K if bits == 8 else K // 2, dtype=torch.int8 if bits == 8 else torch.uint8, device=w.device)
+    s = torch.empty(O, K // group_size, dtype=torch.float16, device=w.device)
+    _lib.check(_lib.lib().moeb200_quantize(_ptr(w), wt, O, K, bits, group_size, m, _ptr(q), _ptr(s),
+                                           _stream(w.device)))
+    return q, s
