@@ -37,6 +37,35 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch of the layer's kernel chain (router -> dispatch -> gate/up -> down
+// -> finalize). Each kernel is launched with programmatic stream serialization, so its CTAs may be
+// scheduled while the previous kernel on the stream drains; every CTA calls chain_wait() before it
+// touches global memory, which returns once the previous kernel has completed and its writes are
+// visible (immediately for a kernel launched without the attribute). Because every CTA waits, a
+// kernel completes only after its predecessor did, so ordering stays transitive along the stream.
+// chain_release() lets the next kernel be scheduled early; it does not publish any data.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void chain_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches kern<<<grid, block, smem, s>>>(args...) with programmatic stream serialization.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                  Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------------------------
 // mbarrier + 1-D bulk TMA
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -8,9 +8,9 @@
 //
 // One persistent CTA per SM works through jobs = (work item, 256 weight rows, K split). Eight
 // consumer warps own 32 rows each (up: 16 gate rows and the matching 16 up rows, so SwiGLU happens
-// in registers). A producer warp streams the job's K range through two shared-memory stages: per
-// stage, tensor-map TMA loads (the map retargeted to the record on the device) bring a 128-byte
-// swizzled tile of one 256-byte segment of each of the 256 rows, and 1-D bulk copies the same
+// in registers). A producer warp streams the job's K range through kGemvStages shared-memory stages:
+// per stage, tensor-map TMA loads (the map retargeted to the record on the device) bring a 128-byte
+// swizzled tile of one kStepBytes segment of each of the 256 rows, and 1-D bulk copies the same
 // columns of the item's token rows; the job's whole scale rows go to a double-buffered scale area
 // with one or two bulk copies. Consumers dequantise in registers straight into mma.sync m16n8k16
 // A fragments and multiply them with up to 8*NB tokens:
@@ -81,8 +81,8 @@ __device__ __forceinline__ void lds(uint32_t a, uint32_t (&w)[NW]) {
   }
 }
 
-// Weight words of one row from the swizzled weight tile: bytes [o, o + 4*NW) of the row's 256-byte
-// step, given the swizzled offsets of the 16-byte pieces that hold them (so0: first piece, so1:
+// Weight words of one row from the swizzled weight tile: bytes [o, o + 4*NW) of the row's
+// kStepBytes step, given the swizzled offsets of the 16-byte pieces that hold them (so0: first piece, so1:
 // second piece when the access spans 32 bytes).
 template <int NW>
 __device__ __forceinline__ void ldw(uint32_t row, uint32_t so0, uint32_t so1, uint32_t (&w)[NW]) {
@@ -101,9 +101,9 @@ __device__ __forceinline__ void ldw(uint32_t row, uint32_t so0, uint32_t so1, ui
   }
 }
 
-// Offset of byte o (o < 256) of a row's step inside the weight tile: the two 128-byte halves are
-// separate TMA boxes 32 KB apart; inside a half, 16-byte piece c of row R sits at piece c ^ (R % 8)
-// (128-byte swizzle). Every row a lane touches has R % 8 == g.
+// Offset of byte o (o < kStepBytes) of a row's step inside the weight tile: each 128 bytes of the
+// step are a separate TMA box column, 32 KB apart; inside a box, 16-byte piece c of row R sits at
+// piece c ^ (R % 8) (128-byte swizzle). Every row a lane touches has R % 8 == g.
 __device__ __forceinline__ uint32_t swz(uint32_t o, uint32_t g) {
   return ((o >> 7) << 15) | ((((o >> 4) & 7u) ^ g) << 4) | (o & 15u);
 }
@@ -134,12 +134,12 @@ struct Scales {
   }
 };
 
-template <int NB>
-__device__ __forceinline__ void fold_one(float (&tot)[2][NB][4], const float (&d)[2][NB][4], const float (&s)[2][2]) {
+template <int NB, int NA>
+__device__ __forceinline__ void fold_one(float (&tot)[2][NB][4], const float (&d)[2][NA][4], const float (&s)[2][2]) {
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
+    for (int nb = 0; nb < NA; ++nb) {
       tot[rt][nb][0] = fmaf(s[rt][0], d[rt][nb][0], tot[rt][nb][0]);
       tot[rt][nb][1] = fmaf(s[rt][0], d[rt][nb][1], tot[rt][nb][1]);
       tot[rt][nb][2] = fmaf(s[rt][1], d[rt][nb][2], tot[rt][nb][2]);
@@ -149,13 +149,14 @@ __device__ __forceinline__ void fold_one(float (&tot)[2][NB][4], const float (&d
 // ---- one chunk per lane --------------------------------------------------------------------------------
 // wr[rt][hh]: shared address of the start of the lane's weight row g + 8*hh of row tile rt in the
 // weight tile; so0/so1: swizzled offsets of the lane's bytes of the chunk in those rows (ldw);
-// xb[nb]: the lane's activation words of the chunk (token g + 8*nb).
+// xb[nb]: the lane's activation words of the chunk (token g + 8*nb). Only the first NA <= NB token
+// blocks are computed: a job whose item has at most 8 tokens skips the empty second block.
 
 // int4: chunk = 32*WPL columns, lane t holds columns [c + 8*WPL*t, +8*WPL) as WPL words per row.
 // The exact (q - 8) products of a group are summed in fp32 and the group's partial is scaled once.
-template <typename AT, int NB, int WPL>
+template <typename AT, int NB, int NA, int WPL>
 __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
-                                           const uint32_t (&xb)[NB][4 * WPL], const Scales& S, int gi,
+                                           const uint32_t (&xb)[NA][4 * WPL], const Scales& S, int gi,
                                            float (&tot)[2][NB][4]) {
   uint32_t wa[2][2][WPL];
 #pragma unroll
@@ -163,7 +164,7 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
   {
-    float d[2][NB][4];
+    float d[2][NA][4];
 #pragma unroll
     for (int j = 0; j < WPL; ++j) {
       uint32_t p04[2][2], p15[2][2], p26[2][2], p37[2][2];
@@ -173,7 +174,7 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
         for (int hh = 0; hh < 2; ++hh)
           Dq<AT>::int4x8(wa[rt][hh][j], p04[rt][hh], p15[rt][hh], p26[rt][hh], p37[rt][hh]);
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
+      for (int nb = 0; nb < NA; ++nb) {
         const uint32_t x0 = xb[nb][4 * j], x1 = xb[nb][4 * j + 1], x2 = xb[nb][4 * j + 2], x3 = xb[nb][4 * j + 3];
         const uint32_t b00 = prmt(x0, x2, 0x5410), b01 = prmt(x0, x2, 0x7632);
         const uint32_t b10 = prmt(x1, x3, 0x5410), b11 = prmt(x1, x3, 0x7632);
@@ -191,14 +192,14 @@ __device__ __forceinline__ void chunk_int4(const uint32_t (&wr)[2][2], uint32_t 
     }
     float s[2][2];
     S.f32(gi, s);
-    fold_one<NB>(tot, d, s);
+    fold_one<NB, NA>(tot, d, s);
   }
 }
 
 // int8: chunk = 16*WPL columns, lane t holds columns [c + 4*WPL*t, +4*WPL) as WPL words per row.
-template <typename AT, int NB, int WPL>
+template <typename AT, int NB, int NA, int WPL>
 __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
-                                           const uint32_t (&xb)[NB][2 * WPL], const Scales& S, int gi,
+                                           const uint32_t (&xb)[NA][2 * WPL], const Scales& S, int gi,
                                            float (&tot)[2][NB][4]) {
   uint32_t wa[2][2][WPL];
 #pragma unroll
@@ -206,7 +207,7 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) ldw<WPL>(wr[rt][hh], so0, so1, wa[rt][hh]);
   {
-    float d[2][NB][4];
+    float d[2][NA][4];
 #pragma unroll
     for (int m = 0; m < WPL; ++m) {
       uint32_t p01[2][2], p23[2][2];
@@ -215,7 +216,7 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) Dq<AT>::int8x4(wa[rt][hh][m], p01[rt][hh], p23[rt][hh]);
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
+      for (int nb = 0; nb < NA; ++nb)
 #pragma unroll
         for (int rt = 0; rt < 2; ++rt) {
           const uint32_t a[4] = {p01[rt][0], p01[rt][1], p23[rt][0], p23[rt][1]};
@@ -227,16 +228,16 @@ __device__ __forceinline__ void chunk_int8(const uint32_t (&wr)[2][2], uint32_t 
     }
     float s[2][2];
     S.f32(gi, s);
-    fold_one<NB>(tot, d, s);
+    fold_one<NB, NA>(tot, d, s);
   }
 }
 
 // Float records: WT is the stored element type; it is converted to the activation type when it
 // differs (the reference materialises records in the activation dtype). Chunk = 16*WPL columns,
 // lane t holds columns [c + 4*WPL*t, +4*WPL).
-template <typename AT, typename WT, int NB, int WPL>
+template <typename AT, typename WT, int NB, int NA, int WPL>
 __device__ __forceinline__ void chunk_float(const uint32_t (&wr)[2][2], uint32_t so0, uint32_t so1,
-                                            const uint32_t (&xb)[NB][2 * WPL], float (&tot)[2][NB][4]) {
+                                            const uint32_t (&xb)[NA][2 * WPL], float (&tot)[2][NB][4]) {
   constexpr int NWR = WPL * 4 * (int)sizeof(WT) / 4;  // weight words per row per lane per chunk
   uint32_t wv[2][2][NWR];
 #pragma unroll
@@ -264,7 +265,7 @@ __device__ __forceinline__ void chunk_float(const uint32_t (&wr)[2][2], uint32_t
         }
       }
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
+    for (int nb = 0; nb < NA; ++nb)
 #pragma unroll
       for (int rt = 0; rt < 2; ++rt) {
         const uint32_t a[4] = {ap[rt][0][0], ap[rt][1][0], ap[rt][0][1], ap[rt][1][1]};
@@ -275,7 +276,7 @@ __device__ __forceinline__ void chunk_float(const uint32_t (&wr)[2][2], uint32_t
 
 // ---- one stage: its chunks, the lane's activation words read from the stage's token rows ----------
 // rowoff[rt][hh]: offset of the lane's row in the weight tile (row index * 128).
-template <typename AT, int NB, int KIND>
+template <typename AT, int NB, int NA, int KIND>
 __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowoff)[2][2], uint32_t bbase,
                                           int bstride, int ntok, int ncols, int col0, int gs, int g0,
                                           const Scales& S, float (&tot)[2][NB][4], int g, int t) {
@@ -295,10 +296,10 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) wr[rt][hh] = wtile + rowoff[rt][hh];
-  uint32_t brow[NB];
-  bool bon[NB];
+  uint32_t brow[NA];
+  bool bon[NA];
 #pragma unroll
-  for (int nb = 0; nb < NB; ++nb) {
+  for (int nb = 0; nb < NA; ++nb) {
     bon[nb] = g + 8 * nb < ntok;
     brow[nb] = bbase + (g + 8 * nb) * bstride + LOFF * t * 2;
   }
@@ -308,9 +309,9 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
   int gi = (I4 || I8) ? col0 / gs - g0 : 0, cc = (I4 || I8) ? (col0 % gs) / CH : 0;
 #pragma unroll 2
   for (int ci = 0; ci < nch; ++ci) {
-    uint32_t xb[NB][NW];
+    uint32_t xb[NA][NW];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
+    for (int nb = 0; nb < NA; ++nb) {
       if (bon[nb]) {
         lds<NW>(brow[nb] + ci * CH * 2, xb[nb]);
       } else {
@@ -321,15 +322,15 @@ __device__ __forceinline__ void run_stage(uint32_t wtile, const uint32_t (&rowof
     const uint32_t o = ci * (CH * W2 / 2) + lo;
     const uint32_t so0 = swz(o, g), so1 = swz(o + 16, g);
     if constexpr (I4) {
-      chunk_int4<AT, NB, WPL>(wr, so0, so1, xb, S, gi, tot);
+      chunk_int4<AT, NB, NA, WPL>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (I8) {
-      chunk_int8<AT, NB, WPL>(wr, so0, so1, xb, S, gi, tot);
+      chunk_int8<AT, NB, NA, WPL>(wr, so0, so1, xb, S, gi, tot);
     } else if constexpr (WT == 2) {
-      chunk_float<AT, float, NB, WPL>(wr, so0, so1, xb, tot);
+      chunk_float<AT, float, NB, NA, WPL>(wr, so0, so1, xb, tot);
     } else if constexpr (WT == 1) {
-      chunk_float<AT, __nv_bfloat16, NB, WPL>(wr, so0, so1, xb, tot);
+      chunk_float<AT, __nv_bfloat16, NB, NA, WPL>(wr, so0, so1, xb, tot);
     } else {
-      chunk_float<AT, __half, NB, WPL>(wr, so0, so1, xb, tot);
+      chunk_float<AT, __half, NB, NA, WPL>(wr, so0, so1, xb, tot);
     }
     if (++cc == cpg) {
       cc = 0;
@@ -414,21 +415,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
-  if (UP && p.zero_acc) {  // the down phase reduces into acc; clear it first (grid-stride)
-    const int64_t n = (int64_t)p.T * p.H;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-      p.acc[i] = 0.f;
-  }
-
   uint8_t* stages = smem;
   uint8_t* sarea = smem + kGemvStages * p.stage_bytes;
   uint8_t* sdesc = sarea + 2 * p.s_bytes;  // 128-byte tensor-map staging of the producer
   uint64_t* bars = reinterpret_cast<uint64_t*>(sdesc + 128);
-  uint64_t* full = bars;        // [2] stage landed
-  uint64_t* empty = bars + 2;   // [2] stage consumed by every consumer warp
-  uint64_t* sfull = bars + 4;   // [2] scale area landed
-  uint64_t* sempty = bars + 6;  // [2] scale area released
-  int32_t* bcast = reinterpret_cast<int32_t*>(bars + 8);
+  uint64_t* full = bars;                      // [stages] stage landed
+  uint64_t* empty = bars + kGemvStages;       // [stages] stage consumed by every consumer warp
+  uint64_t* sfull = bars + 2 * kGemvStages;   // [2] scale area landed
+  uint64_t* sempty = sfull + 2;               // [2] scale area released
+  int32_t* bcast = reinterpret_cast<int32_t*>(sempty + 2);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemvStages; ++s) {
@@ -442,6 +437,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     fence_mbar_init();
   }
   __syncthreads();
+  // everything above touched shared memory only; the previous kernel's outputs are read below
+  chain_wait();
+  chain_release();
+
+  if (UP && p.zero_acc) {  // the down phase reduces into acc; clear it first (grid-stride)
+    const int64_t n = (int64_t)p.T * p.H;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+      p.acc[i] = 0.f;
+  }
 
   const int n_items = *p.n_items;
   const int rb_per_item = UP ? (p.I + kGemvJobRows / 2 - 1) / (kGemvJobRows / 2)
@@ -464,12 +468,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       }
       return false;
     };
-    // tensor maps of the jobs' weight fields: a ring of four per CTA. Each job's map is pointed at
-    // its record while the previous job streams (after that job's first stage is issued), so small
-    // jobs do not wait for the retarget; a slot is rewritten four jobs after its last use, when its
-    // copies have landed (the stage ring is two deep)
+    // tensor maps of the jobs' weight fields: a ring of kMapRing per CTA. Each job's map is pointed
+    // at its record while the previous job streams (after that job's first stage is issued), so
+    // small jobs do not wait for the retarget; a slot is rewritten kMapRing jobs after its last use,
+    // when every copy through it has landed (issuing a stage waits for the stage kGemvStages back,
+    // and every job issues at least one stage)
+    constexpr uint32_t kMapRing = 2 * kGemvStages;
+    static_assert(kMapRing <= kTmapSlots && kMapRing > kGemvStages, "tensor-map ring");
     auto map_slot = [&](uint32_t n) {
-      return reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (n & 3)) * 128;
+      return reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (n % kMapRing)) * 128;
     };
     int job = blockIdx.x;
     Job d;
@@ -518,15 +525,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         if (lane == 0) {
           // the weight tile: whole boxes land (rows or bytes past the tensor read as zeros)
           mbar_arrive_expect_tx(&full[sidx], kGemvWBytes + d.ntok * bseg);
-          const int xb = col0 * d.wbits / 8;  // first byte of the step in each row
-          if (UP) {
-            tma2d(wst, gdesc, xb, d.r0, &full[sidx]);                                   // gate rows -> R 0..127
-            tma2d(wst + kGemvWBytes / 2, gdesc, xb + 128, d.r0, &full[sidx]);
-            tma2d(wst + 128 * 128, gdesc, xb, p.I + d.r0, &full[sidx]);                 // up rows -> R 128..255
-            tma2d(wst + kGemvWBytes / 2 + 128 * 128, gdesc, xb + 128, p.I + d.r0, &full[sidx]);
-          } else {
-            tma2d(wst, gdesc, xb, d.r0, &full[sidx]);                                   // rows -> R 0..255
-            tma2d(wst + kGemvWBytes / 2, gdesc, xb + 128, d.r0, &full[sidx]);
+          const int xb = col0 * d.wbits / 8;  // first byte of the step in each row (a multiple of 128)
+#pragma unroll
+          for (int bc = 0; bc < kStepBytes / 128; ++bc) {
+            const uint32_t wc = wst + bc * kGemvBoxCol;
+            if (UP) {
+              tma2d(wc, gdesc, xb + 128 * bc, d.r0, &full[sidx]);                // gate rows -> R 0..127
+              tma2d(wc + 128 * 128, gdesc, xb + 128 * bc, p.I + d.r0, &full[sidx]);  // up rows -> R 128..255
+            } else {
+              tma2d(wc, gdesc, xb + 128 * bc, d.r0, &full[sidx]);                // rows -> R 0..255
+            }
           }
         }
         __syncwarp();
@@ -623,10 +631,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const uint32_t wtile = st0 + sidx * p.stage_bytes;
       const uint32_t bbase = wtile + kGemvWBytes;
       if (mine) {
+        // token blocks holding tokens of this job (NB = 2 kernels skip the second for items of <= 8)
+        const bool one = NB == 2 && d.ntok <= 8;
         switch (d.kind) {
-#define MOEB200_STAGE(K)                                                                                      \
-  case K:                                                                                                     \
-    run_stage<AT, NB, K>(wtile, rowoff, bbase, p.b_stride, d.ntok, ncols, col0, d.gs, d.g0, S, tot, g, t); \
+#define MOEB200_STAGE(K)                                                                                        \
+  case K:                                                                                                       \
+    if (one)                                                                                                    \
+      run_stage<AT, NB, 1, K>(wtile, rowoff, bbase, p.b_stride, d.ntok, ncols, col0, d.gs, d.g0, S, tot, g, t); \
+    else                                                                                                        \
+      run_stage<AT, NB, NB, K>(wtile, rowoff, bbase, p.b_stride, d.ntok, ncols, col0, d.gs, d.g0, S, tot, g, t); \
     break;
           MOEB200_STAGE(kI4w2)
           MOEB200_STAGE(kI4w1)
@@ -711,6 +724,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 
 template <typename AT>
 __global__ void finalize_kernel(const float* __restrict__ acc, AT* __restrict__ out, int64_t n, int add) {
+  chain_wait();
+  chain_release();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = acc[i];
     out[i] = from_f32<AT>(add ? to_f32<AT>(out[i]) + v : v);
@@ -720,6 +735,8 @@ __global__ void finalize_kernel(const float* __restrict__ acc, AT* __restrict__ 
 // out[i] = sum over s = 0..G-1, in that order, of parts[s*n + i] (+ out[i] when add), cast once.
 template <typename AT>
 __global__ void combine_parts_kernel(const float* __restrict__ parts, int G, int64_t n, AT* __restrict__ out, int add) {
+  chain_wait();
+  chain_release();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float v = 0.f;
     for (int g = 0; g < G; ++g) v += parts[(int64_t)g * n + i];
@@ -732,8 +749,7 @@ cudaError_t launch_t(const GemvParams& p, const TmaTemplates& tm, int grid, int 
   auto kern = gemv_kernel<AT, NB, UP, SPLIT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kGemvThreads, smem, s>>>(p, tm);
-  return cudaGetLastError();
+  return launch_chained(kern, dim3(grid), dim3(kGemvThreads), (size_t)smem, s, p, tm);
 }
 
 template <typename AT, bool UP>
@@ -753,7 +769,7 @@ bool split_ok(const moeb200_layout* L, int nlay, int K, bool up, int ks) {
   return true;
 }
 
-// Shared-memory geometry of a phase (2 stages, 2 scale areas, tensor-map staging, barriers, 1024
+// Shared-memory geometry of a phase (kGemvStages stages, 2 scale areas, tensor-map staging, barriers, 1024
 // bytes of alignment slack); returns its bytes.
 int phase_smem(GemvParams& p, const moeb200_layout* lays, int nlay, int nb, int K, bool up, int ks) {
   int bst = 0, sst = 0;
@@ -769,7 +785,8 @@ int phase_smem(GemvParams& p, const moeb200_layout* lays, int nlay, int nb, int 
   p.b_rows = 8 * nb;
   p.stage_bytes = (kGemvWBytes + p.b_rows * bst + 1023) / 1024 * 1024;
   p.s_bytes = (kGemvJobRows * sst + 127) / 128 * 128;
-  return kGemvStages * p.stage_bytes + 2 * p.s_bytes + 128 + 10 * 8 + 1024;
+  // barriers: full/empty per stage, sfull/sempty (2 each), the broadcast word (8 bytes)
+  return kGemvStages * p.stage_bytes + 2 * p.s_bytes + 128 + (2 * kGemvStages + 5) * 8 + 1024;
 }
 
 cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay, int act, int nb, int max_items,
@@ -830,27 +847,27 @@ cudaError_t launch_combine_parts(const float* parts, int G, int64_t n, int act_t
                                  cudaStream_t s) {
   const int threads = 256;
   const int64_t nblk = (n + threads - 1) / threads;
-  const int grid = (int)(nblk < 148 * 8 ? nblk : 148 * 8);
+  const dim3 grid((unsigned)(nblk < 148 * 8 ? nblk : 148 * 8));
   if (act_type == MOEB200_BF16)
-    combine_parts_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(parts, G, n, static_cast<__nv_bfloat16*>(out), add);
-  else if (act_type == MOEB200_F16)
-    combine_parts_kernel<__half><<<grid, threads, 0, s>>>(parts, G, n, static_cast<__half*>(out), add);
-  else
-    combine_parts_kernel<float><<<grid, threads, 0, s>>>(parts, G, n, static_cast<float*>(out), add);
-  return cudaGetLastError();
+    return launch_chained(combine_parts_kernel<__nv_bfloat16>, grid, dim3(threads), 0, s, parts, G, n,
+                          static_cast<__nv_bfloat16*>(out), add);
+  if (act_type == MOEB200_F16)
+    return launch_chained(combine_parts_kernel<__half>, grid, dim3(threads), 0, s, parts, G, n,
+                          static_cast<__half*>(out), add);
+  return launch_chained(combine_parts_kernel<float>, grid, dim3(threads), 0, s, parts, G, n,
+                        static_cast<float*>(out), add);
 }
 
 cudaError_t launch_finalize(const float* acc, void* out, int act_type, int64_t n, int add, cudaStream_t s) {
   const int threads = 256;
   const int64_t nblk = (n + threads - 1) / threads;
-  const int grid = (int)(nblk < 148 * 8 ? nblk : 148 * 8);
+  const dim3 grid((unsigned)(nblk < 148 * 8 ? nblk : 148 * 8));
   if (act_type == MOEB200_BF16)
-    finalize_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(acc, static_cast<__nv_bfloat16*>(out), n, add);
-  else if (act_type == MOEB200_F16)
-    finalize_kernel<__half><<<grid, threads, 0, s>>>(acc, static_cast<__half*>(out), n, add);
-  else
-    finalize_kernel<float><<<grid, threads, 0, s>>>(acc, static_cast<float*>(out), n, add);
-  return cudaGetLastError();
+    return launch_chained(finalize_kernel<__nv_bfloat16>, grid, dim3(threads), 0, s, acc,
+                          static_cast<__nv_bfloat16*>(out), n, add);
+  if (act_type == MOEB200_F16)
+    return launch_chained(finalize_kernel<__half>, grid, dim3(threads), 0, s, acc, static_cast<__half*>(out), n, add);
+  return launch_chained(finalize_kernel<float>, grid, dim3(threads), 0, s, acc, static_cast<float*>(out), n, add);
 }
 
 }  // namespace moeb200

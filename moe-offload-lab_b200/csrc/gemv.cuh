@@ -58,10 +58,13 @@ constexpr int kGemvCons = 8;                  // consumer warps of a GEMV CTA
 constexpr int kGemvJobRows = 32 * kGemvCons;  // weight rows of one job (up: 128 gate + 128 up)
 constexpr int kGemvThreads = 32 * (kGemvCons + 1);
 constexpr int kGemvStages = 2;
-constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline stage
+constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline stage (multiple of 128)
 constexpr int kSplitCols = 512;  // K splits are multiples of this many columns
 
-constexpr int kGemvWBytes = kGemvJobRows * kStepBytes;  // weight tile of a stage (two 128-byte halves)
+// weight tile of a stage: kStepBytes / 128 box columns, each 128 bytes of all kGemvJobRows rows
+constexpr int kGemvWBytes = kGemvJobRows * kStepBytes;
+constexpr int kGemvBoxCol = kGemvJobRows * 128;  // bytes between two box columns of a tile
+static_assert(kStepBytes % 128 == 0 && kGemvBoxCol == (1 << 15), "box columns are 32 KB apart");
 constexpr int kGemvMaxGrid = 160;                        // tensor-map slots are carved for this many CTAs
 constexpr int kTmapSlots = 16;  // 128-byte tensor-map slots per CTA in the tensor-map workspace
 

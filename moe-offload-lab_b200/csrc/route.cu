@@ -44,6 +44,8 @@ __device__ __forceinline__ float elem8<__half>(const uint4& v, int j) {
 template <typename AT, int RE, int RT, int EG>
 __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict__ h, const AT* __restrict__ wr,
                                                             int T, int H, int E, float* __restrict__ logits) {
+  chain_wait();
+  chain_release();
   constexpr int TG = 8 / EG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = (blockIdx.x * EG + warp % EG) * RE;
@@ -163,6 +165,8 @@ __device__ void token_levels(const float* w, int k, const PolicyDev& pol, uint8_
 
 __global__ void levels_kernel(const float* __restrict__ w, int T, int k, PolicyDev pol, uint8_t* __restrict__ level,
                               uint8_t* __restrict__ skip) {
+  chain_wait();
+  chain_release();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   token_levels(w + (int64_t)t * k, k, pol, level + (int64_t)t * k, skip ? skip + (int64_t)t * k : nullptr);
@@ -177,6 +181,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                                                           float* __restrict__ w, int64_t* __restrict__ idx,
                                                           PolicyDev pol, int with_levels,
                                                           uint8_t* __restrict__ level, uint8_t* __restrict__ skip) {
+  chain_wait();
+  chain_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
@@ -332,6 +338,8 @@ __device__ __forceinline__ void pair_key(const DispatchParams& p, int i, int& ke
 // D1: one warp per block of kDispBlock pairs, processed in order 32 at a time. Each pair gets its
 // rank among the earlier pairs of the block with the same key (expert, and expert*P + slot).
 __global__ void __launch_bounds__(kDispLoadThreads) dispatch_count_kernel(DispatchParams p) {
+  chain_wait();
+  chain_release();
   extern __shared__ int32_t sh[];
   int32_t* cnt_k = sh;               // [E*P]
   int32_t* cnt_e = sh + p.E * p.P;   // [E]
@@ -534,6 +542,8 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
 // D2: one block of 1024 threads over the per-block counts of D1.
 __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
   __shared__ int32_t sh_warp[32];
+  chain_wait();
+  chain_release();
   finish_keys(p, nullptr, nullptr, nullptr, nullptr, sh_warp);
 }
 
@@ -543,6 +553,8 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
 __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) {
   extern __shared__ int32_t sh[];
   __shared__ int32_t sh_warp[32];
+  chain_wait();
+  chain_release();
   const int keys = p.E * p.P;
   int32_t* cnt_k = sh;                 // [keys]
   int32_t* cnt_e = cnt_k + keys;       // [E]
@@ -572,6 +584,8 @@ __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) 
 
 // D3: scatter each kept pair to its sorted positions.
 __global__ void dispatch_scatter_kernel(DispatchParams p) {
+  chain_wait();
+  chain_release();
   const int n = p.T * p.k;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -600,40 +614,40 @@ cudaError_t launch_router(const void* h, const void* wr, const float* bias, int 
   const dim3 g16 = huge  ? dim3((E + 15) / 16, (T + 31) / 32)
                    : big ? dim3((E + 7) / 8, (T + 31) / 32)
                          : dim3((E + 7) / 8, (T + 3) / 4);
+  cudaError_t e = cudaSuccess;
   if (act_type == MOEB200_F16) {
     const __half* ha = static_cast<const __half*>(h);
     const __half* wa = static_cast<const __half*>(wr);
     if (huge)
-      router_logits_kernel<__half, 8, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+      e = launch_chained(router_logits_kernel<__half, 8, 8, 2>, g16, 256, 0, s, ha, wa, T, H, E, logits);
     else if (big)
-      router_logits_kernel<__half, 4, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+      e = launch_chained(router_logits_kernel<__half, 4, 8, 2>, g16, 256, 0, s, ha, wa, T, H, E, logits);
     else
-      router_logits_kernel<__half, 1, 4, 8><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+      e = launch_chained(router_logits_kernel<__half, 1, 4, 8>, g16, 256, 0, s, ha, wa, T, H, E, logits);
   } else if (act_type == MOEB200_BF16) {
     const __nv_bfloat16* ha = static_cast<const __nv_bfloat16*>(h);
     const __nv_bfloat16* wa = static_cast<const __nv_bfloat16*>(wr);
     if (huge)
-      router_logits_kernel<__nv_bfloat16, 8, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+      e = launch_chained(router_logits_kernel<__nv_bfloat16, 8, 8, 2>, g16, 256, 0, s, ha, wa, T, H, E, logits);
     else if (big)
-      router_logits_kernel<__nv_bfloat16, 4, 8, 2><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
+      e = launch_chained(router_logits_kernel<__nv_bfloat16, 4, 8, 2>, g16, 256, 0, s, ha, wa, T, H, E, logits);
     else
-      router_logits_kernel<__nv_bfloat16, 1, 4, 8><<<g16, 256, 0, s>>>(ha, wa, T, H, E, logits);
-  } else
+      e = launch_chained(router_logits_kernel<__nv_bfloat16, 1, 4, 8>, g16, 256, 0, s, ha, wa, T, H, E, logits);
+  } else {
     router_logits_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(h), static_cast<const float*>(wr), T, H,
                                                   E, tpb, logits);
-  cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   PolicyDev pd{};
   if (pol) pd = *pol;
-  router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, bias, T, E, k, renorm, probs, w, idx, pd, pol != nullptr,
-                                                 level, skip);
-  return cudaGetLastError();
+  return launch_chained(router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, logits, bias, T, E, k, renorm, probs, w,
+                        idx, pd, (int)(pol != nullptr), level, skip);
 }
 
 cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, uint8_t* level, uint8_t* skip,
                           cudaStream_t s) {
-  levels_kernel<<<(T + 127) / 128, 128, 0, s>>>(w, T, k, pol, level, skip);
-  return cudaGetLastError();
+  return launch_chained(levels_kernel, dim3((T + 127) / 128), dim3(128), 0, s, w, T, k, pol, level, skip);
 }
 
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
@@ -642,19 +656,15 @@ cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
     const size_t shf = (size_t)(2 * (keys + p.E) + 4 * kDispBlock) * sizeof(int32_t);
     cudaError_t e = cudaFuncSetAttribute(dispatch_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shf);
     if (e != cudaSuccess) return e;
-    dispatch_fused_kernel<<<1, 1024, shf, s>>>(p);
-    return cudaGetLastError();
+    return launch_chained(dispatch_fused_kernel, dim3(1), dim3(1024), shf, s, p);
   }
   const size_t sh = (size_t)(keys + p.E + 2 * kDispBlock) * sizeof(int32_t);
-  dispatch_count_kernel<<<p.nblk, kDispLoadThreads, sh, s>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_chained(dispatch_count_kernel, dim3(p.nblk), dim3(kDispLoadThreads), sh, s, p);
   if (e != cudaSuccess) return e;
-  dispatch_scan_kernel<<<1, 1024, 0, s>>>(p);
-  e = cudaGetLastError();
+  e = launch_chained(dispatch_scan_kernel, dim3(1), dim3(1024), 0, s, p);
   if (e != cudaSuccess) return e;
   const int n = p.T * p.k;
-  dispatch_scatter_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_chained(dispatch_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0, s, p);
 }
 
 }  // namespace moeb200
