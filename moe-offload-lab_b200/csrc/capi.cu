@@ -71,6 +71,8 @@ struct WsHeader {
   int32_t n_items;
   int32_t n_kept;
   int32_t miss;
+  int32_t job_next[2];  // GEMV job counters (up, down), zeroed by the kernel that writes the items
+  int32_t _pad[2];
 };
 
 int act_bytes(int act) { return act == MOEB200_F32 ? 4 : 2; }
@@ -206,7 +208,8 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
 }
 
 __global__ void table_items_kernel(const int64_t* __restrict__ tab, const float* __restrict__ w, int n,
-                                   Item* __restrict__ items, int32_t* __restrict__ n_items, int32_t* __restrict__ pos) {
+                                   Item* __restrict__ items, int32_t* __restrict__ n_items, int32_t* __restrict__ pos,
+                                   int32_t* __restrict__ job_next) {
   // one block: compact the rows whose weight is non-zero into one-token items
   __shared__ int32_t base;
   if (threadIdx.x == 0) base = 0;
@@ -235,7 +238,11 @@ __global__ void table_items_kernel(const int64_t* __restrict__ tab, const float*
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) *n_items = base;
+  if (threadIdx.x == 0) {
+    *n_items = base;
+    job_next[0] = 0;
+    job_next[1] = 0;
+  }
 }
 
 // Shared expert (Qwen3-Next): one warp per token computes the gate logit x[t] . wg (fp32 FMA chain
@@ -246,7 +253,8 @@ template <typename AT>
 __global__ void __launch_bounds__(256) shared_gate_kernel(const AT* __restrict__ x, const AT* __restrict__ wg, int T,
                                                           int H, int nt, int64_t rec, LayoutOffs lo,
                                                           float* __restrict__ w, int32_t* __restrict__ pos,
-                                                          Item* __restrict__ items, int32_t* __restrict__ n_items) {
+                                                          Item* __restrict__ items, int32_t* __restrict__ n_items,
+                                                          int32_t* __restrict__ job_next) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int ni = (T + nt - 1) / nt;
@@ -262,7 +270,11 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const AT* __restrict__
     it._pad = 0;
     items[gtid] = it;
   }
-  if (gtid == 0) *n_items = ni;
+  if (gtid == 0) {
+    *n_items = ni;
+    job_next[0] = 0;
+    job_next[1] = 0;
+  }
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
   const AT* xr = x + (int64_t)t * H;
@@ -513,7 +525,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (I / 16));
   uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)H);
-  table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos);
+  table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos, hdr->job_next);
   CUDA_TRY(cudaGetLastError());
   GemvParams gp{};
   gp.items = items;
@@ -531,6 +543,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;
+  gp.job_next = hdr->job_next;
   gp.lay[0] = to_dev(*layout);
   gp.zero_acc = 1;
   return run_expert_phases(gp, layout, 1, act_type, n, n, 8, s, out, /*add=*/1);
@@ -612,6 +625,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   }
   dp.miss = miss ? miss : &fw.hdr->miss;
   dp.status = &fw.hdr->status;
+  dp.job_next = fw.hdr->job_next;
   CUDA_TRY(launch_dispatch(dp, s));
   GemvParams gp{};
   gp.items = fw.items;
@@ -629,6 +643,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.tmap_ws = fw.tmaps;
   gp.acc = part ? part : fw.acc;
   gp.status = &fw.hdr->status;
+  gp.job_next = fw.hdr->job_next;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
   // upper bound on items: every key splits into ceil(c / nt) items
@@ -720,10 +735,10 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   if (act_type == MOEB200_BF16)
     shared_gate_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                            static_cast<const __nv_bfloat16*>(wg), T, H, nt, rec, lo, wt,
-                                                           pos, items, &hdr->n_items);
+                                                           pos, items, &hdr->n_items, hdr->job_next);
   else
     shared_gate_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(wg), T, H,
-                                                    nt, rec, lo, wt, pos, items, &hdr->n_items);
+                                                    nt, rec, lo, wt, pos, items, &hdr->n_items, hdr->job_next);
   CUDA_TRY(cudaGetLastError());
   GemvParams gp{};
   gp.items = items;
@@ -741,6 +756,7 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;
+  gp.job_next = hdr->job_next;
   gp.lay[0] = to_dev(*layout);
   gp.zero_acc = 1;
   return run_expert_phases(gp, layout, 1, act_type, (T + nt - 1) / nt, T, nt, s, out, add ? 1 : 0, gemm);

@@ -359,6 +359,15 @@ struct Job {
 
 __device__ __forceinline__ int job_item(int job, int rb_per_item, int ks_n) { return job / (rb_per_item * ks_n); }
 
+// A job as the producer announces it to the consumers, in the shared-memory slot of the job's first
+// stage (job < 0: no more jobs).
+struct alignas(16) JobSlot {
+  Item it;
+  int32_t job;
+  int32_t _pad[3];
+};
+static_assert(sizeof(JobSlot) == 64, "JobSlot layout");
+
 // Item of a job (a global load: callers fetch it one job ahead).
 __device__ __forceinline__ Item load_item(const GemvParams& p, int job, int n_jobs, int rb_per_item, int ks_n) {
   Item it{};
@@ -424,6 +433,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   uint64_t* sfull = bars + 2 * kGemvStages;   // [2] scale area landed
   uint64_t* sempty = sfull + 2;               // [2] scale area released
   int32_t* bcast = reinterpret_cast<int32_t*>(sempty + 2);
+  JobSlot* jslot = reinterpret_cast<JobSlot*>(sempty + 4);  // [stages], 16-byte aligned
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemvStages; ++s) {
@@ -457,13 +467,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // ---------------- producer warp ----------------
     uint32_t it = 0, sj = 0, jn = 0;
     bool ok = true;
-    Item nxt = load_item(p, blockIdx.x, n_jobs, rb_per_item, ks_n);
-    // describes the first non-empty job at index >= j (j advances to it); the item of the job after
-    // it is loaded meanwhile
-    auto next_job = [&](int& j, Job& out) -> bool {
-      for (; j < n_jobs; j += gridDim.x) {
-        describe_job<UP>(p, j, nxt, rb_per_item, ks_n, out);
-        nxt = load_item(p, j + gridDim.x, n_jobs, rb_per_item, ks_n);
+    // Job order: a CTA's first two jobs are blockIdx.x and blockIdx.x + gridDim.x (no draw on the
+    // path of small launches); every further job is drawn from the launch's job counter (jobs are
+    // numbered largest records first), so CTAs that draw short jobs take more of them and the CTAs
+    // finish together. The next job is drawn, and its item loaded, while the current one streams.
+    int32_t* ctr = p.job_next + (UP ? 0 : 1);
+    int jpre = blockIdx.x;  // next job index to describe
+    int taken = 0;          // jobs described so far
+    Item ipre = load_item(p, jpre, n_jobs, rb_per_item, ks_n);
+    auto draw = [&]() -> int {
+      if (++taken == 1) return (int)(blockIdx.x + gridDim.x);
+      int j = 0;
+      if (lane == 0) j = (int)(2 * gridDim.x) + atomicAdd(ctr, 1);
+      return __shfl_sync(0xffffffffu, j, 0);
+    };
+    // describes the next non-empty job (its index in j, its item in jit)
+    auto next_job = [&](int& j, Item& jit, Job& out) -> bool {
+      while (jpre < n_jobs) {
+        j = jpre;
+        jit = ipre;
+        describe_job<UP>(p, j, jit, rb_per_item, ks_n, out);
+        jpre = draw();
+        ipre = load_item(p, jpre, n_jobs, rb_per_item, ks_n);
         if (out.nsteps > 0) return true;
       }
       return false;
@@ -478,16 +503,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     auto map_slot = [&](uint32_t n) {
       return reinterpret_cast<uint64_t>(p.tmap_ws) + (uint64_t)(blockIdx.x * kTmapSlots + (n % kMapRing)) * 128;
     };
-    int job = blockIdx.x;
+    int job = 0;
+    Item jit{};
     Job d;
-    bool has = next_job(job, d);
+    bool has = next_job(job, jit, d);
     uint64_t gdesc = 0;
     if (has) {
       gdesc = map_slot(jn++);
       retarget_tmap(tm.m[d.slot], smem_u32(sdesc), gdesc, d.q, lane);
     }
     while (has && ok) {
-      int jnext = job + gridDim.x;
+      int jnext = 0;
+      Item jitn{};
       Job dn;
       bool hn = false;
       uint64_t gnext = 0;
@@ -523,6 +550,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         const uint32_t bseg = (uint32_t)(ncols * (int)sizeof(AT));
         const uint32_t wst = smem_u32(stages + sidx * p.stage_bytes);
         if (lane == 0) {
+          if (step == 0) {  // announce the job with its first stage (published by the arrive below)
+            jslot[sidx].it = jit;
+            jslot[sidx].job = job;
+          }
           // the weight tile: whole boxes land (rows or bytes past the tensor read as zeros)
           mbar_arrive_expect_tx(&full[sidx], kGemvWBytes + d.ntok * bseg);
           const int xb = col0 * d.wbits / 8;  // first byte of the step in each row (a multiple of 128)
@@ -541,7 +572,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         if (lane < d.ntok)
           bulk_g2s(stages + sidx * p.stage_bytes + kGemvWBytes + lane * p.b_stride, brow + col0, bseg, &full[sidx]);
         if (step == 0) {  // the next job's map, while this job's first stage lands
-          hn = next_job(jnext, dn);
+          hn = next_job(jnext, jitn, dn);
           if (hn) {
             gnext = map_slot(jn++);
             retarget_tmap(tm.m[dn.slot], smem_u32(sdesc), gnext, dn.q, lane);
@@ -549,6 +580,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         }
       }
       d = dn;
+      jit = jitn;
       job = jnext;
       gdesc = gnext;
       has = hn;
@@ -557,6 +589,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // already in the normal flow; after a failed wait they may still be landing)
     for (uint32_t q = it > kGemvStages ? it - kGemvStages : 0; q < it; ++q)
       mbar_wait(&full[q % kGemvStages], (q / kGemvStages) & 1, nullptr);
+    // then tell the consumers that no job follows: job -1 in the slot of the next stage, once that
+    // stage's previous use has been consumed (after a failed wait the consumers time out instead)
+    if (ok) {
+      const int sidx = it % kGemvStages;
+      if (it >= kGemvStages) ok = mbar_wait(&empty[sidx], ((it / kGemvStages) - 1) & 1, p.status);
+      if (ok && lane == 0) {
+        jslot[sidx].job = -1;
+        mbar_arrive(&full[sidx]);
+      }
+    }
     return;
   }
 
@@ -575,12 +617,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const int R = UP ? rt * 128 + 16 * warp + g + 8 * hh : 32 * warp + 16 * rt + g + 8 * hh;
       rowoff[rt][hh] = R * 128;
     }
-  Item nxt = load_item(p, blockIdx.x, n_jobs, rb_per_item, ks_n);
-  for (int job = blockIdx.x; job < n_jobs && !failed; job += gridDim.x) {
+  while (!failed) {
+    // the next job is announced in the slot of its first stage: wait for that stage, read the job
+    {
+      const int sidx = it % kGemvStages;
+      if (!mbar_wait(&full[sidx], (it / kGemvStages) & 1, p.status)) break;
+    }
+    const JobSlot& js = jslot[it % kGemvStages];
+    const int job = js.job;
+    if (job < 0) break;  // no more jobs
     Job d;
-    describe_job<UP>(p, job, nxt, rb_per_item, ks_n, d);
-    nxt = load_item(p, job + gridDim.x, n_jobs, rb_per_item, ks_n);  // in flight during this job
-    if (d.nsteps == 0) continue;
+    describe_job<UP>(p, job, js.it, rb_per_item, ks_n, d);
     // the down epilogue's token and weight of each of the lane's fragment tokens, loaded now
     int etok[NB][2];
     float ew[NB][2];
@@ -622,7 +669,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         for (int i = 0; i < 4; ++i) tot[rt][nb][i] = 0.f;
     for (int step = 0; step < d.nsteps && !failed; ++step, ++it) {
       const int sidx = it % kGemvStages;
-      if (!mbar_wait(&full[sidx], (it / kGemvStages) & 1, p.status)) {
+      if (step > 0 && !mbar_wait(&full[sidx], (it / kGemvStages) & 1, p.status)) {
         failed = true;  // finish this job's barriers with the other consumer warps, then stop
         break;
       }
@@ -785,8 +832,9 @@ int phase_smem(GemvParams& p, const moeb200_layout* lays, int nlay, int nb, int 
   p.b_rows = 8 * nb;
   p.stage_bytes = (kGemvWBytes + p.b_rows * bst + 1023) / 1024 * 1024;
   p.s_bytes = (kGemvJobRows * sst + 127) / 128 * 128;
-  // barriers: full/empty per stage, sfull/sempty (2 each), the broadcast word (8 bytes)
-  return kGemvStages * p.stage_bytes + 2 * p.s_bytes + 128 + (2 * kGemvStages + 5) * 8 + 1024;
+  // barriers: full/empty per stage, sfull/sempty (2 each), the broadcast word (16 bytes), a 64-byte
+  // job slot per stage
+  return kGemvStages * p.stage_bytes + 2 * p.s_bytes + 128 + (2 * kGemvStages + 6) * 8 + kGemvStages * 64 + 1024;
 }
 
 cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay, int act, int nb, int max_items,

@@ -51,6 +51,8 @@ struct GemvParams {
   int32_t stage_bytes;  // one stage: the weight tile (kGemvJobRows x 256 bytes), then b_rows token rows
   int32_t s_bytes;      // one job's scale area
   int32_t zero_acc;     // up phase: zero acc before use
+  int32_t* job_next;    // [2] job counters of the up and down launches, zeroed by the kernel that wrote
+                        // the items (dispatch, table items, shared gate)
 };
 
 // Geometry shared by host and device.

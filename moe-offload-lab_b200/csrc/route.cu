@@ -536,6 +536,10 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   if (tid == 0) {
     if (p.n_items) *p.n_items = n_items;
     if (p.n_kept) *p.n_kept = n_kept;
+    if (p.job_next) {
+      p.job_next[0] = 0;
+      p.job_next[1] = 0;
+    }
   }
 }
 

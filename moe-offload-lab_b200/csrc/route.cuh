@@ -49,6 +49,7 @@ struct DispatchParams {
   LayoutOffs offs[4];
   int32_t* miss;          // [1] pairs routed to a non-resident record, or null
   int32_t* status;
+  int32_t* job_next;      // [2] GEMV job counters to zero with the items, or null
 };
 
 cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,
