@@ -127,8 +127,15 @@ int check_shapes(int H, int I) {
 
 // Split-K planning of the GEMV phases: a split covers a multiple of kSplitCols input columns (a
 // multiple of every group size and pipeline step), and is only used for small pair counts (the
-// pre-activation buffer is sized for kMaxSplitPairs pairs).
-constexpr int kMaxSplitPairs = 2048;
+// pre-activation buffer holds kMaxKSplit slices of kMaxSplitPairs pairs). Splits only pay when the
+// jobs would not fill the SMs, i.e. for a few hundred pairs at most.
+constexpr int kMaxSplitPairs = 256;
+
+// Split-K scratch of a call over n pairs: pre-activation rows per split slice, and arrival counters
+// (zeroed by the kernel that writes the call's items).
+int split_rows(int64_t n) { return (int)std::min<int64_t>(n, kMaxSplitPairs); }
+size_t split_pre_floats(int64_t n, int I) { return (size_t)kMaxKSplit * split_rows(n) * 2 * I; }
+int split_cnt_ints(int64_t n, int I) { return split_rows(n) * (I / 16); }
 
 
 struct ForwardWs {
@@ -163,8 +170,8 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.rank_e = c.take<int32_t>(n);
   w.items = c.take<Item>(n);
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
-  w.pre = c.take<float>((size_t)std::min(n, kMaxSplitPairs) * 2 * I);
-  w.cnt = c.take<int32_t>((size_t)std::min(n, kMaxSplitPairs) * (I / 16));
+  w.pre = c.take<float>(split_pre_floats(n, I));
+  w.cnt = c.take<int32_t>(split_cnt_ints(n, I));
   w.tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
@@ -209,7 +216,8 @@ int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int 
 
 __global__ void table_items_kernel(const int64_t* __restrict__ tab, const float* __restrict__ w, int n,
                                    Item* __restrict__ items, int32_t* __restrict__ n_items, int32_t* __restrict__ pos,
-                                   int32_t* __restrict__ job_next) {
+                                   int32_t* __restrict__ job_next, int32_t* __restrict__ cnt, int cnt_n) {
+  for (int i = threadIdx.x; i < cnt_n; i += blockDim.x) cnt[i] = 0;  // split-K arrival counters
   // one block: compact the rows whose weight is non-zero into one-token items
   __shared__ int32_t base;
   if (threadIdx.x == 0) base = 0;
@@ -254,9 +262,11 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const AT* __restrict__
                                                           int H, int nt, int64_t rec, LayoutOffs lo,
                                                           float* __restrict__ w, int32_t* __restrict__ pos,
                                                           Item* __restrict__ items, int32_t* __restrict__ n_items,
-                                                          int32_t* __restrict__ job_next) {
+                                                          int32_t* __restrict__ job_next, int32_t* __restrict__ cnt,
+                                                          int cnt_n) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = gtid; i < cnt_n; i += gridDim.x * blockDim.x) cnt[i] = 0;  // split-K arrival counters
   const int ni = (T + nt - 1) / nt;
   if (gtid < ni) {
     Item it;
@@ -495,8 +505,8 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<Item>(n);
   c.take<int32_t>(n);
   c.take<uint8_t>((size_t)n * layout->inter * 2);
-  c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * layout->inter);
-  c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (layout->inter / 16));
+  c.take<float>(split_pre_floats(n, layout->inter));
+  c.take<int32_t>(split_cnt_ints(n, layout->inter));
   c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   c.take<float>((size_t)layout->hidden);
   return c.off;
@@ -521,11 +531,11 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   Item* items = c.take<Item>(n);
   int32_t* pos = c.take<int32_t>(n);
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
-  float* pre = c.take<float>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * 2 * I);
-  int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(n, kMaxSplitPairs) * (I / 16));
+  float* pre = c.take<float>(split_pre_floats(n, I));
+  int32_t* cnt = c.take<int32_t>(split_cnt_ints(n, I));
   uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)H);
-  table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos, hdr->job_next);
+  table_items_kernel<<<1, 256, 0, s>>>(tab, w, n, items, &hdr->n_items, pos, hdr->job_next, cnt, split_cnt_ints(n, I));
   CUDA_TRY(cudaGetLastError());
   GemvParams gp{};
   gp.items = items;
@@ -540,6 +550,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.h = hbuf;
   gp.pre = pre;
   gp.tile_cnt = cnt;
+  gp.pre_rows = split_rows(n);
   gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;
@@ -626,6 +637,8 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   dp.miss = miss ? miss : &fw.hdr->miss;
   dp.status = &fw.hdr->status;
   dp.job_next = fw.hdr->job_next;
+  dp.zero_cnt = fw.cnt;
+  dp.zero_n = split_cnt_ints(n, I);
   CUDA_TRY(launch_dispatch(dp, s));
   GemvParams gp{};
   gp.items = fw.items;
@@ -640,6 +653,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.h = fw.h;
   gp.pre = fw.pre;
   gp.tile_cnt = fw.cnt;
+  gp.pre_rows = split_rows(n);
   gp.tmap_ws = fw.tmaps;
   gp.acc = part ? part : fw.acc;
   gp.status = &fw.hdr->status;
@@ -688,8 +702,8 @@ size_t moeb200_shared_expert_workspace(const moeb200_layout* layout, int32_t T) 
   c.take<int32_t>(T);
   c.take<float>(T);
   c.take<uint8_t>((size_t)T * layout->inter * 2);
-  c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * layout->inter);
-  c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (layout->inter / 16));
+  c.take<float>(split_pre_floats(T, layout->inter));
+  c.take<int32_t>(split_cnt_ints(T, layout->inter));
   c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   c.take<float>((size_t)T * layout->hidden);
   return c.off;
@@ -724,8 +738,8 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   int32_t* pos = c.take<int32_t>(T);
   float* wt = c.take<float>(T);
   uint8_t* hbuf = c.take<uint8_t>((size_t)T * I * 2);
-  float* pre = c.take<float>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * 2 * I);
-  int32_t* cnt = c.take<int32_t>((size_t)std::min<int32_t>(T, kMaxSplitPairs) * (I / 16));
+  float* pre = c.take<float>(split_pre_floats(T, I));
+  int32_t* cnt = c.take<int32_t>(split_cnt_ints(T, I));
   uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)T * H);
   const LayoutOffs lo{layout->off_gu_q, is_int(layout->wtype) ? layout->off_gu_s : 0, layout->off_dn_q,
@@ -735,10 +749,12 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   if (act_type == MOEB200_BF16)
     shared_gate_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                            static_cast<const __nv_bfloat16*>(wg), T, H, nt, rec, lo, wt,
-                                                           pos, items, &hdr->n_items, hdr->job_next);
+                                                           pos, items, &hdr->n_items, hdr->job_next, cnt,
+                                                           split_cnt_ints(T, I));
   else
     shared_gate_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(wg), T, H,
-                                                    nt, rec, lo, wt, pos, items, &hdr->n_items, hdr->job_next);
+                                                    nt, rec, lo, wt, pos, items, &hdr->n_items, hdr->job_next, cnt,
+                                                    split_cnt_ints(T, I));
   CUDA_TRY(cudaGetLastError());
   GemvParams gp{};
   gp.items = items;
@@ -753,6 +769,7 @@ int moeb200_shared_expert(const moeb200_layout* layout, const void* record, cons
   gp.h = hbuf;
   gp.pre = pre;
   gp.tile_cnt = cnt;
+  gp.pre_rows = split_rows(T);
   gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;

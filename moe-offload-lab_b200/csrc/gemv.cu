@@ -348,7 +348,7 @@ __host__ __device__ __forceinline__ int split_cols(int K, int ks_n) {
 struct Job {
   const uint8_t* q;  // weight field of the record (gate_up or down)
   const uint8_t* s;  // scale field (integer records)
-  int32_t item, rb, start, ntok, slot;
+  int32_t item, rb, ks, start, ntok, slot;
   int32_t kind, gs, wbits;
   int32_t r0, nrow;          // up: first gate row and gate rows (up rows mirror them); down: rows
   int32_t k_lo, k_hi;        // input columns of this K split
@@ -388,6 +388,7 @@ __device__ __forceinline__ void describe_job(const GemvParams& p, int job, const
   const bool isint = L.wtype == MOEB200_I4 || L.wtype == MOEB200_I8;
   d.item = item;
   d.rb = rb;
+  d.ks = ks;
   d.slot = it.slot;
   d.start = it.start;
   d.ntok = it.ntok;
@@ -728,9 +729,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             if (16 * warp + rrow >= d.nrow) continue;
             const int r = d.r0 + 16 * warp + rrow;  // gate row; its up row is I + r
             if constexpr (SPLIT) {
-              float* prow = p.pre + (int64_t)j * 2 * p.I + r;
-              red_add_f32(prow, tot[0][nb][i]);
-              red_add_f32(prow + p.I, tot[1][nb][i]);
+              float* prow = p.pre + ((int64_t)d.ks * p.pre_rows + j) * 2 * p.I + r;  // this split's slice
+              prow[0] = tot[0][nb][i];
+              prow[p.I] = tot[1][nb][i];
             } else {
               const float hv = silu_mul(tot[0][nb][i], tot[1][nb][i]);
               static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
@@ -747,9 +748,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       // the last K split of this row block to arrive turns the block's pre-activations into h
       __threadfence();
       consumers_sync();
+      const int kc = split_cols(p.H, ks_n);
+      const int ksplits = (p.H + kc - 1) / kc;  // non-empty splits
       if (threadIdx.x == 0) {
-        const int kc = split_cols(p.H, ks_n);
-        const int ksplits = (p.H + kc - 1) / kc;  // non-empty splits
         int32_t* cnt = p.tile_cnt + (int64_t)d.item * rb_per_item + d.rb;
         *bcast = atomicAdd(cnt, 1) == ksplits - 1;
       }
@@ -760,8 +761,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         __threadfence();
         for (int q = threadIdx.x; q < d.nrow * d.ntok; q += kGemvCons * 32) {
           const int j = d.start + q / d.nrow, r = d.r0 + q % d.nrow;
-          const float* prow = p.pre + (int64_t)j * 2 * p.I;
-          const float hv = silu_mul(__ldcg(prow + r), __ldcg(prow + p.I + r));
+          // the splits' partial sums, added in split order (the same sum on every run)
+          float gv = 0.f, uv = 0.f;
+          for (int sp = 0; sp < ksplits; ++sp) {
+            const float* prow = p.pre + ((int64_t)sp * p.pre_rows + j) * 2 * p.I;
+            gv += __ldcg(prow + r);
+            uv += __ldcg(prow + p.I + r);
+          }
+          const float hv = silu_mul(gv, uv);
           static_cast<AT*>(p.h)[(int64_t)j * p.I + r] = from_f32<AT>(hv);
         }
       }
@@ -848,7 +855,7 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   // several-fold in bytes; more, smaller jobs balance the CTAs; up: only with room for pre)
   int ks = 1;
   const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
-  while (can_split && ks < 8 && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
+  while (can_split && ks < kMaxKSplit && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
   if (up)
     p.ksplit_up = ks;
   else
@@ -863,12 +870,6 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
     if (e != cudaSuccess) return e;
   }
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(sms, kGemvMaxGrid), jobs1 * ks));
-  if (up && ks > 1) {
-    cudaError_t e = cudaMemsetAsync(p.pre, 0, (size_t)n_pairs * 2 * p.I * sizeof(float), s);
-    if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(p.tile_cnt, 0, (size_t)max_items * ((p.I + rpj - 1) / rpj) * sizeof(int32_t), s);
-    if (e != cudaSuccess) return e;
-  }
   if (act == MOEB200_BF16)
     return up ? launch_phase<__nv_bfloat16, true>(p, tm, nb, grid, smem, s)
               : launch_phase<__nv_bfloat16, false>(p, tm, nb, grid, smem, s);

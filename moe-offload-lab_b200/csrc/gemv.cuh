@@ -37,8 +37,10 @@ struct GemvParams {
   int32_t T;
   const void* x;   // [T, H] activations
   void* h;         // [n_pairs, I] activations, row j = sorted pair j
-  float* pre;      // [n_pairs, 2I] fp32 gate|up pre-activations (split-K up phase), else null
-  int32_t* tile_cnt;  // [items, I/16] arrivals of the K splits of each up job (split-K), zeroed per call
+  float* pre;      // [kMaxKSplit][pre_rows][2I] fp32 gate|up pre-activations of each K split (split-K
+                   // up phase), else null
+  int32_t* tile_cnt;  // [items, I/16] arrivals of the K splits of each up job (split-K), zeroed by the
+                      // kernel that wrote the items
   float* acc;      // [T, H] fp32 combine buffer
   int32_t* status;
   LayoutDev lay[4];
@@ -51,6 +53,7 @@ struct GemvParams {
   int32_t stage_bytes;  // one stage: the weight tile (kGemvJobRows x 256 bytes), then b_rows token rows
   int32_t s_bytes;      // one job's scale area
   int32_t zero_acc;     // up phase: zero acc before use
+  int32_t pre_rows;     // rows of one split's pre-activation slice (>= pairs whenever K is split)
   int32_t* job_next;    // [2] job counters of the up and down launches, zeroed by the kernel that wrote
                         // the items (dispatch, table items, shared gate)
 };
@@ -62,6 +65,7 @@ constexpr int kGemvThreads = 32 * (kGemvCons + 1);
 constexpr int kGemvStages = 2;
 constexpr int kStepBytes = 256;  // bytes of one weight row per pipeline stage (multiple of 128)
 constexpr int kSplitCols = 512;  // K splits are multiples of this many columns
+constexpr int kMaxKSplit = 8;    // K splits of one GEMV launch at most
 
 // weight tile of a stage: kStepBytes / 128 box columns, each 128 bytes of all kGemvJobRows rows
 constexpr int kGemvWBytes = kGemvJobRows * kStepBytes;

@@ -415,6 +415,7 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   const int keys = p.E * p.P;
   const int tid = threadIdx.x;
   if (tid == 0 && p.miss) *p.miss = 0;
+  for (int i = tid; i < p.zero_n; i += blockDim.x) p.zero_cnt[i] = 0;
   __syncthreads();
   constexpr int PER = kMaxKeys / 1024;
   int32_t tot_k[PER], tot_e[PER], nit[PER];
@@ -552,8 +553,10 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
 }
 
 // D1+D2+D3 in one block of 1024 threads when all pairs fit one dispatch block (T*k <= kDispBlock):
-// keys, in-order ranks (one warp), totals/positions/items, scatter -- counts and ranks stay in
-// shared memory.
+// keys; per-key and per-expert totals by shared-memory atomics (any order); totals/positions/items;
+// each pair dropped into its key's and its expert's bucket at the slot its atomic returned; then
+// each pair's in-order rank is the number of smaller pair indices in its bucket (a bucket holds at
+// most T pairs: a token routes to k distinct experts), which fixes the stable sorted order.
 __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) {
   extern __shared__ int32_t sh[];
   __shared__ int32_t sh_warp[32];
@@ -564,25 +567,36 @@ __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) 
   int32_t* cnt_e = cnt_k + keys;       // [E]
   int32_t* offk = cnt_e + p.E;         // [keys]
   int32_t* offe = offk + keys;         // [E]
-  int32_t* key_s = offe + p.E;         // [kDispBlock]
-  int32_t* e_s = key_s + kDispBlock;   // [kDispBlock]
-  int32_t* rk_s = e_s + kDispBlock;    // [kDispBlock]
-  int32_t* re_s = rk_s + kDispBlock;   // [kDispBlock]
+  int32_t* bk_s = offe + p.E;          // [kDispBlock] pair indices bucketed by key (unordered in a bucket)
+  int32_t* be_s = bk_s + kDispBlock;   // [kDispBlock] pair indices bucketed by expert
   const int tid = threadIdx.x;
   const int n = p.T * p.k;
   for (int i = tid; i < keys + p.E; i += blockDim.x) sh[i] = 0;
-  if (tid < n) pair_key(p, tid, key_s[tid], e_s[tid]);
+  int key = -1, e = -1;
+  if (tid < n) pair_key(p, tid, key, e);
   __syncthreads();
-  if (tid < 32) rank_in_order(tid, n, key_s, e_s, cnt_k, cnt_e, rk_s, re_s);
+  int sk = 0, se = 0;
+  if (key >= 0) {
+    sk = atomicAdd(&cnt_k[key], 1);
+    se = atomicAdd(&cnt_e[e], 1);
+  }
   __syncthreads();
   finish_keys(p, cnt_k, cnt_e, offk, offe, sh_warp);
   __syncthreads();
-  if (tid < n) {
-    const int key = key_s[tid];
-    if (key >= 0) {
-      p.pos_k[offk[key] + rk_s[tid]] = tid;
-      p.pos_e[offe[e_s[tid]] + re_s[tid]] = tid;
-    }
+  if (key >= 0) {
+    bk_s[offk[key] + sk] = tid;
+    be_s[offe[e] + se] = tid;
+  }
+  __syncthreads();
+  if (key >= 0) {
+    const int k0 = offk[key], kn = cnt_k[key];
+    int rk = 0;
+    for (int q = 0; q < kn; ++q) rk += bk_s[k0 + q] < tid;
+    const int e0 = offe[e], en = cnt_e[e];
+    int re = 0;
+    for (int q = 0; q < en; ++q) re += be_s[e0 + q] < tid;
+    p.pos_k[k0 + rk] = tid;
+    p.pos_e[e0 + re] = tid;
   }
 }
 
@@ -657,7 +671,7 @@ cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, ui
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {
   const int keys = p.E * p.P;
   if (p.nblk == 1) {
-    const size_t shf = (size_t)(2 * (keys + p.E) + 4 * kDispBlock) * sizeof(int32_t);
+    const size_t shf = (size_t)(2 * (keys + p.E) + 2 * kDispBlock) * sizeof(int32_t);
     cudaError_t e = cudaFuncSetAttribute(dispatch_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shf);
     if (e != cudaSuccess) return e;
     return launch_chained(dispatch_fused_kernel, dim3(1), dim3(1024), shf, s, p);

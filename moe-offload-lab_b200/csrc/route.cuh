@@ -50,6 +50,8 @@ struct DispatchParams {
   int32_t* miss;          // [1] pairs routed to a non-resident record, or null
   int32_t* status;
   int32_t* job_next;      // [2] GEMV job counters to zero with the items, or null
+  int32_t* zero_cnt;      // [zero_n] split-K arrival counters to zero with the items, or null
+  int32_t zero_n;
 };
 
 cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,

@@ -149,7 +149,7 @@ def test_levels_known_answer(cuda_dev):
 
 
 # -- dispatch -----------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("T,k,E,P", [(1, 8, 64, 1), (37, 4, 16, 3), (64, 8, 64, 2), (2048, 8, 128, 1),
+@pytest.mark.parametrize("T,k,E,P", [(1, 8, 64, 1), (37, 4, 16, 3), (64, 8, 64, 2), (1024, 1, 4, 1), (2048, 8, 128, 1),
                                      (4096, 10, 512, 3), (3000, 10, 512, 2)])
 def test_dispatch_bit_exact(cuda_dev, T, k, E, P):
     g = torch.Generator(device=cuda_dev).manual_seed(T + E)
