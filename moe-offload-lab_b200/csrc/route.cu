@@ -419,6 +419,7 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   __syncthreads();
   constexpr int PER = kMaxKeys / 1024;
   int32_t tot_k[PER], tot_e[PER], nit[PER];
+  int64_t rec_i[PER];  // record address of each of the thread's slot-major keys (loaded once)
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int key = tid * PER + i;
@@ -470,16 +471,18 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   for (int i = 0; i < PER; ++i) {
     const int m = tid * PER + i;  // slot-major index sl * E + ex
     int32_t ni = 0;
+    int64_t rec = 0;
     if (p.items != nullptr && m < keys) {
       const int sl = m / p.E, ex = m % p.E;
       const int32_t run = tot_s[ex * p.P + sl];
       if (run > 0) {
-        const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 1;
-        if (rec != 0) ni = (run + p.nt - 1) / p.nt;
+        rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
+        if (rec != 0 || !p.table) ni = (run + p.nt - 1) / p.nt;
         else if (p.miss) atomicAdd(p.miss, run);
       }
     }
     nit[i] = ni;
+    rec_i[i] = rec;
   }
   int32_t off_k[PER], off_e[PER], off_i[PER];
 #pragma unroll
@@ -508,7 +511,7 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
     if (nit[i] > 0) {
       const int sl = m / p.E, ex = m % p.E;
       const int key = ex * p.P + sl;
-      const int64_t rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
+      const int64_t rec = rec_i[i];
       const LayoutOffs lo = p.offs[sl];
       const int32_t run = tot_s[key];
       for (int q = 0; q < nit[i]; ++q) {
