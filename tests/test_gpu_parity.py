@@ -222,6 +222,38 @@ def test_experts_forward_matches_oracle(cuda_dev, case):
     assert int(rt.miss.item()) == 0
 
 
+def test_calls_in_a_row_reuse_the_workspace(cuda_dev):
+    # The GEMV job counters and the split-K arrival counters live in the workspace and are zeroed by
+    # the kernel that writes each call's items: T = 1 (K split), T = 64 (jobs drawn from the counter),
+    # then T = 3 and T = 1 again on the same workspace must each match the oracle.
+    H, I, E, k = 2048, 1024, 64, 8
+    precs = ["fp16", "int4"]
+    lays, recs = layer_records(precs, H, I, E, seed=77, device=cuda_dev, std=0.02)
+    rt = B200Runtime(precs, lays, E, cuda_dev, ops.PolicySpec("threshold", thr=0.1), layers=[0])
+    for p in precs:
+        for e in range(E):
+            rt.add_record(0, e, p, recs[p][e])
+    recs_np = [[b.cpu().numpy() for b in recs[p]] for p in precs]
+    g = torch.Generator(device=cuda_dev).manual_seed(11)
+    ops.set_path("gemv")
+    try:
+        for T in (1, 64, 3, 1):
+            x = torch.randn(T, H, generator=g, device=cuda_dev).half()
+            logits = torch.randn(T, E, generator=g, device=cuda_dev)
+            wv, idx = torch.topk(logits.softmax(-1), k, dim=-1)
+            out = rt.run_layer(0, x, idx, wv, torch.nn.SiLU())
+            lvl, skip = rt.levels(0, wv)
+            lv = np.zeros((T, k), np.int64) if lvl is None else lvl.cpu().numpy().astype(np.int64)
+            sk = None if skip is None else skip.cpu().numpy().astype(bool)
+            slot = np.vectorize(lambda v: O.level_to_slot(int(v), 2))(lv)
+            ref = O.moe_layer(act_np(x), idx.cpu().numpy(), wv.cpu().numpy(), slot, sk, recs_np,
+                              [lays[p] for p in precs], E)
+            err = O.max_rel_err(act_np(out), ref)
+            assert err < TOL, (T, err)
+    finally:
+        ops.set_path("auto")
+
+
 def test_missing_expert_counted_and_skipped(cuda_dev):
     H, I, E, k, T = 256, 128, 16, 4, 6
     lays, recs = layer_records(["int4"], H, I, E, seed=9, device=cuda_dev, std=0.05)
