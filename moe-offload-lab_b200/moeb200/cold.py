@@ -113,11 +113,24 @@ class ColdExperts:
             self._codes[layer] = c
         return c
 
+    def _write_table(self, writes: dict[int, list[tuple[int, int]]]) -> None:
+        """Write (flat index p * E + e, record address) entries into each layer's device table with
+        one indexed store per layer on the current stream; the index/value pairs go up from pinned
+        memory without blocking the host."""
+        for layer, ent in writes.items():
+            if not ent:
+                continue
+            iv = torch.tensor(ent, dtype=torch.int64).pin_memory().to(self.dev, non_blocking=True)
+            self.rt._table(layer).view(-1).index_put_((iv[:, 0],), iv[:, 1])
+
     def reset(self) -> None:
         """Drop every uploaded record (their table entries go back to not resident)."""
+        E = self.rt.num_experts
+        writes: dict[int, list[tuple[int, int]]] = {}
         for p, plan in self.plans.items():
             for (layer, e, prec) in plan.clear():
-                self.rt._table(layer)[self.rt.precisions.index(prec), e] = 0
+                writes.setdefault(layer, []).append((self.rt.precisions.index(prec) * E + e, 0))
+        self._write_table(writes)
 
     @torch.no_grad()
     def run_layer(self, layer: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, level: torch.Tensor | None,
@@ -125,9 +138,16 @@ class ColdExperts:
         rt = self.rt
         T, k = idx.shape
         P = rt.n_prec
-        idx_h = idx.cpu().numpy()
-        lv_h = level.cpu().numpy().astype(np.int64) if level is not None else np.zeros((T, k), np.int64)
-        sk_h = skip.cpu().numpy().astype(bool) if skip is not None else np.zeros((T, k), bool)
+        # one read-back of the routing (indices, levels, skips)
+        rows = [idx.to(torch.int64)]
+        if level is not None:
+            rows.append(level.to(torch.int64))
+        if skip is not None:
+            rows.append(skip.to(torch.int64))
+        back = torch.stack(rows).cpu().numpy()
+        idx_h = back[0]
+        lv_h = back[1] if level is not None else np.zeros((T, k), np.int64)
+        sk_h = back[-1].astype(bool) if skip is not None else np.zeros((T, k), bool)
         # precision slot of every pair (moelab/policy.py:188-192) and its (expert, slot) code
         slot = np.minimum(lv_h, P - 1) if P >= 3 else np.where(lv_h == 0, 0, P - 1)
         code = idx_h.astype(np.int64) * P + slot
@@ -140,7 +160,8 @@ class ColdExperts:
         cold_pair = torch.from_numpy(cold_pair)
         if not cold_pair.any():
             return rt.run_layer(layer, x, idx, w, level=level, skip=skip, out=out)
-        table = rt._table(layer)
+        E = rt.num_experts
+        writes: dict[int, list[tuple[int, int]]] = {}
         cur = torch.cuda.current_stream(self.dev)
         self.copy_stream.wait_stream(cur)  # the routing and any earlier table writes come first
         used = []
@@ -159,9 +180,12 @@ class ColdExperts:
                     self.uploads += 1
                     if old is not None:
                         ol, oe, op = old
-                        rt._table(ol)[rt.precisions.index(op), oe] = 0
+                        writes.setdefault(ol, []).append((rt.precisions.index(op) * E + oe, 0))
                 for (l_, e, p_), s in slot_of.items():
-                    table[rt.precisions.index(p_), e] = self.buf[p_][s].data_ptr()
+                    writes.setdefault(layer, []).append((rt.precisions.index(p_) * E + e, self.buf[p_][s].data_ptr()))
+            # one indexed store per table; its entries are distinct (an evicted key is never one that
+            # this layer needs, and each slot holds one key)
+            self._write_table(writes)
             done = torch.cuda.Event()
             done.record(self.copy_stream)
         mask = cold_pair.to(self.dev, non_blocking=True).to(torch.uint8)
