@@ -137,6 +137,17 @@ int split_rows(int64_t n) { return (int)std::min<int64_t>(n, kMaxSplitPairs); }
 size_t split_pre_floats(int64_t n, int I) { return (size_t)kMaxKSplit * split_rows(n) * 2 * I; }
 int split_cnt_ints(int64_t n, int I) { return split_rows(n) * (I / 16); }
 
+// K splits the GEMV planner can choose for n one-token items (the pointer-table entry points): it
+// doubles the splits while the up jobs (n items x ceil(I/128) row blocks) would not give every SM one.
+// Sizing their pre-activation slices by it keeps small calls' scratch small.
+int table_split_slices(int64_t n, int I) {
+  const int64_t jobs1 = std::max<int64_t>(1, n) * ((I + 127) / 128);
+  const int sms = num_sms_cached();
+  int ks = 1;
+  while (ks < kMaxKSplit && jobs1 * ks < sms) ks *= 2;
+  return ks;
+}
+
 
 struct ForwardWs {
   WsHeader* hdr;
@@ -505,7 +516,7 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n) {
   c.take<Item>(n);
   c.take<int32_t>(n);
   c.take<uint8_t>((size_t)n * layout->inter * 2);
-  c.take<float>(split_pre_floats(n, layout->inter));
+  c.take<float>((size_t)table_split_slices(n, layout->inter) * split_rows(n) * 2 * layout->inter);
   c.take<int32_t>(split_cnt_ints(n, layout->inter));
   c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   c.take<float>((size_t)layout->hidden);
@@ -531,7 +542,8 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   Item* items = c.take<Item>(n);
   int32_t* pos = c.take<int32_t>(n);
   uint8_t* hbuf = c.take<uint8_t>((size_t)n * I * 2);
-  float* pre = c.take<float>(split_pre_floats(n, I));
+  const int slices = table_split_slices(n, I);
+  float* pre = c.take<float>((size_t)slices * split_rows(n) * 2 * I);
   int32_t* cnt = c.take<int32_t>(split_cnt_ints(n, I));
   uint8_t* tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   float* acc = c.take<float>((size_t)H);
@@ -551,6 +563,7 @@ int moeb200_grouped_ffn(const moeb200_layout* layout, const int64_t* tab, const 
   gp.pre = pre;
   gp.tile_cnt = cnt;
   gp.pre_rows = split_rows(n);
+  gp.pre_slices = slices;
   gp.tmap_ws = tmaps;
   gp.acc = acc;
   gp.status = &hdr->status;

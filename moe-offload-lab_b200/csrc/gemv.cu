@@ -855,7 +855,8 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   // several-fold in bytes; more, smaller jobs balance the CTAs; up: only with room for pre)
   int ks = 1;
   const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
-  while (can_split && ks < kMaxKSplit && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
+  const int ks_cap = up && p.pre_slices > 0 ? p.pre_slices : kMaxKSplit;  // up: one pre slice per split
+  while (can_split && ks < ks_cap && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
   if (up)
     p.ksplit_up = ks;
   else

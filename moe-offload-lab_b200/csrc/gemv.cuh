@@ -54,6 +54,7 @@ struct GemvParams {
   int32_t s_bytes;      // one job's scale area
   int32_t zero_acc;     // up phase: zero acc before use
   int32_t pre_rows;     // rows of one split's pre-activation slice (>= pairs whenever K is split)
+  int32_t pre_slices;   // split slices in pre (the up phase splits K at most this many ways; 0 = kMaxKSplit)
   int32_t* job_next;    // [2] job counters of the up and down launches, zeroed by the kernel that wrote
                         // the items (dispatch, table items, shared gate)
 };
