@@ -96,7 +96,7 @@ def dist_setup(n_gpus: int):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    else:
+    elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
 
@@ -556,30 +556,65 @@ def cpu_layer_sample(stack: Stack, T: int, layer: int = 0):
     return dt, f"layer {layer} of the step at T={T} (all its routed pairs), scaled x{cfg['layers']} layers"
 
 
+def headline_config(T: int, world: int, exchange: str) -> dict:
+    """The `config` object of the headline line, shared by both arms (same workload, same keys)."""
+    return {"workload": f"c1 OLMoE-1B-7B 16-layer MoE stack decode, T={T}/GPU, "
+                        "fp16/int4 by router prob >= 0.1, all experts resident",
+            "global_batch": T * world, "layers": CFG1["layers"], "experts": CFG1["E"], "top_k": CFG1["k"],
+            "hidden": CFG1["H"], "inter": CFG1["I"],
+            "parallelism": (f"ep{world} (experts in contiguous blocks; dispatch/combine " + (
+                "through peer memory over NVLink: CUDA IPC buffers, flag handshakes)"
+                if exchange == "p2p" else "by NCCL all_gather + all_to_all)")) if world > 1 else "1gpu",
+            "l2": "no flush: each step streams the routed records of 16 layers, GBs (> 126 MB L2)",
+            "dense_part": "attention stood in by a residual add between layers (out of scope)",
+            "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks"}
+
+
+def _encode_oracle(args):
+    """Worker of the reference arm's record pool: one record with the oracle's numpy quantiser."""
+    from oracle import moe_oracle as O
+
+    lay, gu, dn = args
+    return O.encode_record(lay, gu, dn)
+
+
 def reference_arm(args, world, rank):
-    """--impl reference: the oracle port of the reference's CPU expert path on the host cores,
-    rank 0 only. Nothing of this build's CUDA library runs here: the records are built with torch
-    ops (the moelab quantiser restated in moeb200.format), routing and masks by the oracle."""
+    """--impl reference: the reference's CPU expert path (moelab/runtime.py:681-702: materialise each
+    routed record to fp32, expert_ffn, weighted index_add) on the host cores, rank 0 only.
+
+    The reference (moelab) is a Python project without packaging metadata, so it cannot be installed
+    on the GPU box; its CPU path runs here as the oracle's numpy restatement (kind "port"), pinned
+    to the reference's own outputs by the golden tests. Nothing of this build's CUDA library runs:
+    the weights are drawn with the same seeded torch generator as the headline's layer 0, records
+    are quantised by the oracle (a process pool on the host cores), routing and masks by the oracle.
+    Each timed step is ONE MoE layer of the workload (all T*k routed pairs of layer 0): ms_per_step is
+    that measured layer, and value = T / (16 x ms_per_step), the metric of the 16 identical layers."""
     if rank != 0:
         return
-    from moeb200 import format as F
+    import multiprocessing as mp
+
     from oracle import moe_oracle as O
 
     cfg = CFG1
     H, I, E, k, T = cfg["H"], cfg["I"], cfg["E"], cfg["k"], args.batch
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
     g = torch.Generator(device=dev).manual_seed(0)
-    lays = [F.record_layout(p, H, I) for p in cfg["precs"]]
-    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).half()
-    recs = [[] for _ in cfg["precs"]]
+    lays = [O.record_layout(p, H, I) for p in cfg["precs"]]
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).half().float().cpu().numpy()
+    jobs = []
     for e in range(E):
-        gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
-        dn = torch.randn(H, I, generator=g, device=dev) * 0.02
-        for s_, lay in enumerate(lays):
-            recs[s_].append(F.encode_record(lay, gu, dn).cpu().numpy())
+        gu = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).cpu().numpy()
+        dn = (torch.randn(H, I, generator=g, device=dev) * 0.02).cpu().numpy()
+        jobs += [(lay, gu, dn) for lay in lays]
+    cores = os.cpu_count() or 1
+    t_build = time.perf_counter()
+    with mp.get_context("spawn").Pool(min(cores, 32)) as pool:
+        blobs = pool.map(_encode_oracle, jobs, chunksize=1)
+    t_build = time.perf_counter() - t_build
+    recs = [[blobs[e * len(lays) + s_] for e in range(E)] for s_ in range(len(lays))]
     torch.manual_seed(1234)
-    x = torch.randn(T, H).half().float().numpy()
-    probs, w, idx, _ = O.router(x, wr.float().cpu().numpy(), k, cfg["renorm"], "float16")
+    x = torch.randn(T, H, device=dev).half().float().cpu().numpy()
+    probs, w, idx, _ = O.router(x, wr, k, cfg["renorm"], "float16")
     lvl, skip = O.threshold_levels(w, cfg["policy"]["thr"])
     slot = np.vectorize(lambda v: O.level_to_slot(int(v), len(lays)))(lvl.astype(np.int64))
     times = []
@@ -588,19 +623,18 @@ def reference_arm(args, world, rank):
         O.moe_layer(x, idx, w, slot, skip, recs, lays, E)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
-    step_s = float(np.mean(times)) * cfg["layers"]
-    v = T / step_s
-    cores = os.cpu_count()
+    step_s = float(np.mean(times))
+    v = T / (cfg["layers"] * step_s)
+    sample = (f"each step: layer 0 of the workload (all {T * k} routed pairs of T={T}, records materialised "
+              f"to fp32 per call, numpy on the host cores); value = T / ({cfg['layers']} x measured step)")
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"c1 OLMoE 16-layer MoE stack decode T={T}, fp16/int4 threshold 0.1",
-                       "global_batch": T, "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": "each step: one MoE layer of the workload (all T*k routed pairs, "
-                                       "records materialised to fp32 per call) on the host cores with numpy, "
-                                       "scaled to 16 layers"},
-            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "layers_per_step": 1, "ms_per_layer": step_s * 1e3,
+            "config": headline_config(T, world, args.exchange),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "setup_s": {"record_quantisation": t_build}}
     print(json.dumps(line), flush=True)
 
 
@@ -740,15 +774,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 activations, fp16+int4 gs64 records, f32 accumulation",
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) random-init experts and routers)",
-            "config": {"workload": f"c1 OLMoE-1B-7B 16-layer MoE stack decode, T={T}/GPU, "
-                                   "fp16/int4 by router prob >= 0.1, all experts resident",
-                       "global_batch": T * world, "layers": L, "experts": CFG1["E"], "top_k": CFG1["k"],
-                       "hidden": H, "inter": CFG1["I"], "parallelism": (f"ep{world} (experts in contiguous blocks; dispatch/combine " + (
-                           "through peer memory over NVLink: CUDA IPC buffers, flag handshakes)"
-                           if args.exchange == "p2p" else "by NCCL all_gather + all_to_all)")) if world > 1 else "1gpu",
-                       "l2": "no flush: each step streams ~%.1f GB of records (> 126 MB L2)" % (
-                           (rb["up"] + rb["down"]) / 1e9),
-                       "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks"},
+            "config": headline_config(T, world, args.exchange),
             "int4_fp16_record_gbs": (rb["up"] + rb["down"]) / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "gemv up (gate/up dequant GEMV + SwiGLU)",
                          "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": up_gbs / hbm_peak,

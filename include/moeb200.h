@@ -163,6 +163,13 @@ size_t moeb200_grouped_ffn_workspace(const moeb200_layout* layout, int32_t n);
 #define MOEB200_NOALLOC_SCRATCH_BYTES (1u << 20)
 int moeb200_grouped_ffn_noalloc(const moeb200_layout* layout, const int64_t* tab, const float* w, int32_t n,
                                 const void* x, int32_t act_type, void* out, void* stream);
+/* Companion of moeb200_grouped_ffn_noalloc (no counterpart in the reference). The static scratch
+ * array of the current device starts with the same device status word as every workspace (see
+ * moeb200_check_workspace); the workspace-free calls never clear it, so a bounded wait that gave up
+ * or a bad index in any of them since the last check is kept. This call copies the word to *status
+ * and clears it, synchronising the stream. The array's address is cached per device ordinal, which
+ * assumes one context per device (the runtime's primary context). */
+int moeb200_noalloc_check_status(int32_t* status, void* stream);
 
 /* ---- the experts module ------------------------------------------------------------------------
  * Replaces OffloadedExperts.forward -> MoERuntime.run_layer for experts resident on this GPU

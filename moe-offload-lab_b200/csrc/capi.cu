@@ -137,11 +137,14 @@ int split_rows(int64_t n) { return (int)std::min<int64_t>(n, kMaxSplitPairs); }
 size_t split_pre_floats(int64_t n, int I) { return (size_t)kMaxKSplit * split_rows(n) * 2 * I; }
 int split_cnt_ints(int64_t n, int I) { return split_rows(n) * (I / 16); }
 
-// K splits the GEMV planner can choose for n one-token items (the pointer-table entry points): it
-// doubles the splits while the up jobs (n items x ceil(I/128) row blocks) would not give every SM one.
-// Sizing their pre-activation slices by it keeps small calls' scratch small.
+// Upper bound on the K splits the GEMV planner (gemv.cu plan_and_launch) can choose for n one-token
+// items (the pointer-table entry points). The planner doubles the splits while the up jobs (n items x
+// ceil(I / (kGemvJobRows/2)) row blocks) would not give every SM one, capped by the slices sized here;
+// it may stop earlier (split_ok), never later, so the slices always suffice. Sizing them by this rule
+// keeps small calls' scratch small. Keep the two rules in step.
 int table_split_slices(int64_t n, int I) {
-  const int64_t jobs1 = std::max<int64_t>(1, n) * ((I + 127) / 128);
+  constexpr int kUpRows = kGemvJobRows / 2;
+  const int64_t jobs1 = std::max<int64_t>(1, n) * ((I + kUpRows - 1) / kUpRows);
   const int sms = num_sms_cached();
   int ks = 1;
   while (ks < kMaxKSplit && jobs1 * ks < sms) ks *= 2;

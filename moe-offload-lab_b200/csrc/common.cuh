@@ -19,7 +19,8 @@
 namespace moeb200 {
 
 // Device-side status word: kernels that wait on anything record why they gave up here instead of
-// hanging; the host reads it back through moeb200_read_status.
+// hanging; the host reads it back through moeb200_check_workspace (moeb200_noalloc_check_status for
+// the static scratch of the workspace-free entry point).
 enum DevStatus : int32_t {
   kDevOk = 0,
   kDevTimeout = 1,       // an mbarrier wait ran past its iteration budget

@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue warps 8..11 ----------------
+    // ---------------- epilogue warps (kEpiWarp0 .. kEpiWarp0 + 3) ----------------
     const int q = warp - kEpiWarp0;  // TMEM lane quarter
     const int r_local = q * 32 + lane;
     if (UP && p.zero_acc) {  // the down phase reduces into acc: clear it while the first tile runs

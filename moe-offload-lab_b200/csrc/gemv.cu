@@ -855,7 +855,9 @@ cudaError_t plan_and_launch(GemvParams& p, const moeb200_layout* lays, int nlay,
   // several-fold in bytes; more, smaller jobs balance the CTAs; up: only with room for pre)
   int ks = 1;
   const bool can_split = !up || (max_items <= max_split_pairs && n_pairs <= max_split_pairs && p.pre != nullptr);
-  const int ks_cap = up && p.pre_slices > 0 ? p.pre_slices : kMaxKSplit;  // up: one pre slice per split
+  // up: one pre slice per split (the pointer-table entry points size their slices with capi.cu
+  // table_split_slices, which mirrors this loop without split_ok)
+  const int ks_cap = up && p.pre_slices > 0 ? p.pre_slices : kMaxKSplit;
   while (can_split && ks < ks_cap && jobs1 * ks < (int64_t)sms && split_ok(lays, nlay, K, up, ks * 2)) ks *= 2;
   if (up)
     p.ksplit_up = ks;

@@ -13,6 +13,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libmoeb200.so"
 
 F32, F16, BF16, I8, I4 = 0, 1, 2, 3, 4
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3, 4
+# MOEB200_NOALLOC_SCRATCH_BYTES of include/moeb200.h: the static scratch of the workspace-free entry point
+NOALLOC_SCRATCH_BYTES = 1 << 20
 
 
 class MoeB200Error(RuntimeError):
@@ -65,6 +67,7 @@ _SIGS = {
                                       _P]),
     "moeb200_grouped_ffn_workspace": (C.c_size_t, [C.POINTER(Layout), C.c_int32]),
     "moeb200_grouped_ffn_noalloc": (C.c_int, [C.POINTER(Layout), _P, _P, C.c_int32, _P, C.c_int32, _P, _P]),
+    "moeb200_noalloc_check_status": (C.c_int, [C.POINTER(C.c_int32), _P]),
     "moeb200_experts_forward": (C.c_int, [C.POINTER(ExpertTable), _P, C.c_int32, C.c_int32, _P, _P, C.c_int32,
                                           _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "moeb200_experts_workspace": (C.c_size_t, [C.POINTER(ExpertTable), C.c_int32, C.c_int32]),

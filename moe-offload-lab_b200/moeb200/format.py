@@ -8,8 +8,8 @@ field table, the packing and the scale choice follow it step for step:
   - int4 packs two values per byte, stored +8 in [0, 15], low nibble = even column;
   - the scale of a group is max|w|/qmax ("absmax") or the best of 32 candidates ("mse", the
     store's default for int4), rounded to fp16 before quantising and never zero.
-Building records runs on the device of the weights (torch ops), like the reference's quantiser;
-it is offline work, not part of the MoE-layer hot path.
+Integer records are quantised on the GPU by the library's own quantiser kernel (csrc/quant.cu); it
+is offline work, not part of the MoE-layer hot path.
 """
 
 from __future__ import annotations
@@ -20,9 +20,6 @@ from . import _lib
 
 ALIGN = 4096
 FIELD_ALIGN = 64
-QMAX = {8: 127, 4: 7}
-QMIN = {8: -127, 4: -8}
-_GRID = [1.0 - 0.02 * i for i in range(16)]
 
 PRECISIONS = {
     "fp32": {"kind": "float", "dtype": "float32"},
@@ -119,63 +116,6 @@ def field_offsets(layout: dict) -> list[int]:
     return [offs["gate_up.q"], offs["gate_up.s"], offs["down.q"], offs["down.s"]]
 
 
-# ---- quantiser (moelab/quant.py:57-127) ---------------------------------------------------------------
-def _safe(s: torch.Tensor) -> torch.Tensor:
-    s16 = s.to(torch.float16)
-    tiny = torch.tensor(1e-7, dtype=torch.float16, device=s.device)
-    return torch.where(s16 == 0, tiny, s16)
-
-
-def choose_scales(wf: torch.Tensor, bits: int, method: str = "absmax") -> torch.Tensor:
-    qmin, qmax = QMIN[bits], QMAX[bits]
-    absmax = wf.abs().amax(dim=-1, keepdim=True)
-    if method == "absmax":
-        return _safe((absmax / qmax).clamp(min=1e-7))
-    if method != "mse":
-        raise ValueError(f"unknown scale method {method}")
-    bases = [absmax / qmax]
-    if qmin == -qmax - 1:
-        mx = wf.gather(-1, wf.abs().argmax(dim=-1, keepdim=True))
-        bases.append(mx / qmin)
-    best_s = best_e = None
-    for b in bases:
-        for f in _GRID:
-            s = _safe(b * f)
-            sf = s.float()
-            err = ((torch.round(wf / sf).clamp(qmin, qmax) * sf - wf) ** 2).sum(dim=-1, keepdim=True)
-            if best_s is None:
-                best_s, best_e = s, err
-            else:
-                better = err < best_e
-                best_s = torch.where(better, s, best_s)
-                best_e = torch.where(better, err, best_e)
-    return best_s
-
-
-def pack(q: torch.Tensor, bits: int) -> torch.Tensor:
-    if bits == 8:
-        return q.to(torch.int8).contiguous()
-    u = (q + 8).to(torch.uint8)
-    return (u[:, 0::2] | (u[:, 1::2] << 4)).contiguous()
-
-
-def quantize(w: torch.Tensor, bits: int, group_size: int, method: str = "absmax", chunk_rows: int = 4096):
-    """(out, in) float -> (packed q, fp16 scales (out, in/gs)), computed on w's device."""
-    out_f, in_f = w.shape
-    if in_f % group_size:
-        raise ValueError(f"in_features={in_f} not divisible by group_size={group_size}")
-    qs, ss = [], []
-    for r0 in range(0, out_f, chunk_rows):
-        wf = w[r0:r0 + chunk_rows].float().reshape(-1, in_f // group_size, group_size)
-        s = choose_scales(wf, bits, method)
-        q = torch.round(wf / s.float()).clamp(QMIN[bits], QMAX[bits]).to(torch.int16)
-        qs.append(q.reshape(-1, in_f))
-        ss.append(s.reshape(-1, in_f // group_size))
-    q = torch.cat(qs) if len(qs) > 1 else qs[0]
-    s = torch.cat(ss) if len(ss) > 1 else ss[0]
-    return pack(q, bits), s.contiguous()
-
-
 def views(layout: dict, blob: torch.Tensor) -> dict[str, torch.Tensor]:
     """Typed zero-copy views into a record (moelab/store.py:153-161)."""
     out = {}
@@ -190,32 +130,17 @@ def views(layout: dict, blob: torch.Tensor) -> dict[str, torch.Tensor]:
     return out
 
 
-def encode_record_device(layout: dict, gate_up: torch.Tensor, down: torch.Tensor,
-                         out: torch.Tensor | None = None) -> torch.Tensor:
-    """encode_record with the integer records quantised by the B200 quantiser (moeb200_quantize):
-    one kernel per matrix instead of the scale search's tensor passes; CUDA tensors only."""
-    from . import ops
-
-    spec = PRECISIONS[layout["precision"]]
-    if spec["kind"] == "float":
-        return encode_record(layout, gate_up, down, out)
-    buf = out if out is not None else torch.empty(layout["record_bytes"], dtype=torch.uint8, device=gate_up.device)
-    buf.zero_()
-    v = views(layout, buf)
-    method = layout.get("scale") or "absmax"
-    method = "absmax" if method == "gptq" else method
-    for name, w in (("gate_up", gate_up), ("down", down)):
-        q, s = ops.quantize(w.contiguous(), spec["bits"], layout["group_sizes"][name], method)
-        v[f"{name}.q"].copy_(q.view(v[f"{name}.q"].dtype))
-        v[f"{name}.s"].copy_(s)
-    return buf
-
-
 def encode_record(layout: dict, gate_up: torch.Tensor, down: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Record bytes from float weights, on the weights' device (moelab/store.py:122-150).
-    `out` (uint8, record_bytes) is filled in place when given."""
+    """Record bytes from float weights (moelab/store.py:122-150), on the weights' device.
+
+    Integer precisions are quantised by the B200 quantiser (``moeb200_quantize``: moelab's absmax /
+    mse scale search, byte-identical integers and scales), so they need CUDA tensors; float
+    precisions are a plain cast into the record's fields. ``out`` (uint8, record_bytes) is filled in
+    place when given."""
     spec = PRECISIONS[layout["precision"]]
     dev = gate_up.device
+    if spec["kind"] == "int" and dev.type != "cuda":
+        raise ValueError("integer records are quantised on the GPU: pass CUDA tensors")
     buf = out if out is not None else torch.empty(layout["record_bytes"], dtype=torch.uint8, device=dev)
     buf.zero_()
     v = views(layout, buf)
@@ -223,11 +148,13 @@ def encode_record(layout: dict, gate_up: torch.Tensor, down: torch.Tensor, out: 
         dt = TORCH_DTYPES[spec["dtype"]]
         v["gate_up"].copy_(gate_up.to(dt))
         v["down"].copy_(down.to(dt))
-    else:
-        method = layout.get("scale") or "absmax"
-        method = "absmax" if method == "gptq" else method
-        for name, w in (("gate_up", gate_up), ("down", down)):
-            q, s = quantize(w, spec["bits"], layout["group_sizes"][name], method)
-            v[f"{name}.q"].copy_(q)
-            v[f"{name}.s"].copy_(s)
+        return buf
+    from . import ops
+
+    method = layout.get("scale") or "absmax"
+    method = "absmax" if method == "gptq" else method
+    for name, w in (("gate_up", gate_up), ("down", down)):
+        q, s = ops.quantize(w.contiguous(), spec["bits"], layout["group_sizes"][name], method)
+        v[f"{name}.q"].copy_(q.view(v[f"{name}.q"].dtype))
+        v[f"{name}.s"].copy_(s)
     return buf

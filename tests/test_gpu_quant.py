@@ -52,6 +52,14 @@ def test_device_records_equal_host_records(cuda_dev, prec):
     g = torch.Generator(device=cuda_dev).manual_seed(9)
     gu = torch.randn(512, 512, generator=g, device=cuda_dev) * 0.02
     dn = torch.randn(512, 256, generator=g, device=cuda_dev) * 0.02
-    dev_rec = Fmt.encode_record_device(lay, gu, dn)
+    dev_rec = Fmt.encode_record(lay, gu, dn)
     host = O.encode_record(lay, gu.cpu().numpy(), dn.cpu().numpy())
     assert np.array_equal(dev_rec.cpu().numpy(), host)
+
+
+@pytest.mark.parametrize("prec", ["int8", "int4"])
+def test_device_records_match_reference_goldens(cuda_dev, golden, golden_meta, prec):
+    lay = golden_meta["layouts"][f"{prec}_128_64"]
+    blob = Fmt.encode_record(lay, torch.from_numpy(golden["rec/gu"]).to(cuda_dev),
+                             torch.from_numpy(golden["rec/dn"]).to(cuda_dev))
+    assert np.array_equal(blob.cpu().numpy(), golden[f"rec/{prec}"])

@@ -5,6 +5,8 @@ The workspace-free call exists for callers that cannot allocate device scratch (
 C ABI with no device allocator, or code that must not call cudaMalloc); it keeps its scratch in one
 static 1 MiB device array per GPU. This file is collected last so a failure here never hides the
 other tests' results; it passes alone in a fresh process and after the rest of the suite.
+Also checked: the largest call the array admits (and the next size refused), that a call allocates
+no device memory, and the companion status call.
 """
 
 from __future__ import annotations
@@ -67,3 +69,71 @@ def test_noalloc_refuses_sizes_beyond_the_array(cuda_dev):
                                                 _lib.F16, C.c_void_p(dummy.data_ptr()), None)
     assert rc == _lib.ERR_UNSUPPORTED
     assert "scratch" in _lib.last_error()[1]
+
+
+def _largest_n(lay_c) -> int:
+    L = _lib.lib()
+    cap = _lib.NOALLOC_SCRATCH_BYTES
+    n = 1
+    while n < 4096 and L.moeb200_grouped_ffn_workspace(C.byref(lay_c), n + 1) <= cap:
+        n += 1
+    return n
+
+
+def _status() -> int:
+    st = C.c_int32(-1)
+    _lib.check(_lib.lib().moeb200_noalloc_check_status(C.byref(st), C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    return st.value
+
+
+def test_noalloc_largest_call_and_next_refused(cuda_dev):
+    # one-token items at the OLMoE shape: the largest n whose scratch fits the array runs and matches
+    # the workspace entry point; n + 1 is refused before anything launches
+    H, I = 2048, 1024
+    lay = F.record_layout("int4", H, I)
+    lay_c = F.to_c(lay)
+    n = _largest_n(lay_c)
+    assert n >= 8
+    m = 6  # distinct records, repeated through the table (the kernels read records in place)
+    lay, blobs, nps = make_records("int4", H, I, m, 21, cuda_dev)
+    lay_c = F.to_c(lay)
+    lay_c.off_gu_q = lay_c.off_gu_s = lay_c.off_dn_q = lay_c.off_dn_s = 0
+    g = torch.Generator(device=cuda_dev).manual_seed(22)
+    weights = (torch.rand(n, generator=g, device=cuda_dev) / n).tolist()
+    tab, w = _table(lay, [blobs[i % m] for i in range(n)], weights, cuda_dev)
+    x = torch.randn(H, generator=g, device=cuda_dev).half()
+    ref_out = torch.zeros(H, dtype=torch.float16, device=cuda_dev)
+    ops.grouped_ffn_table(lay_c, tab, w, x, ref_out)
+    out = torch.zeros(H, dtype=torch.float16, device=cuda_dev)
+    _noalloc(lay_c, tab, w, x, out)
+    torch.cuda.synchronize()
+    assert O.max_rel_err(act_np(out), act_np(ref_out)) < TOL, n
+    assert _status() == 0
+    big = torch.zeros(4 * (n + 1), dtype=torch.int64, device=cuda_dev)
+    wb = torch.zeros(n + 1, dtype=torch.float32, device=cuda_dev)
+    rc = _lib.lib().moeb200_grouped_ffn_noalloc(C.byref(lay_c), C.c_void_p(big.data_ptr()), C.c_void_p(wb.data_ptr()),
+                                                n + 1, C.c_void_p(x.data_ptr()), _lib.F16,
+                                                C.c_void_p(out.data_ptr()), None)
+    assert rc == _lib.ERR_UNSUPPORTED, n + 1
+    assert "scratch" in _lib.last_error()[1]
+
+
+def test_noalloc_call_allocates_nothing(cuda_dev):
+    H, I = 2048, 512
+    lay, blobs, nps = make_records("int8", H, I, 4, 31, cuda_dev)
+    lay_c = F.to_c(lay)
+    lay_c.off_gu_q = lay_c.off_gu_s = lay_c.off_dn_q = lay_c.off_dn_s = 0
+    tab, w = _table(lay, blobs, [0.4, 0.3, 0.2, 0.1], cuda_dev)
+    x = torch.randn(H, generator=torch.Generator(device=cuda_dev).manual_seed(32), device=cuda_dev).half()
+    out = torch.zeros(H, dtype=torch.float16, device=cuda_dev)
+    _noalloc(lay_c, tab, w, x, out)  # warm: module load, address lookup, kernel attributes
+    torch.cuda.synchronize()
+    torch_before = torch.cuda.memory_allocated(cuda_dev)
+    free_before, _ = torch.cuda.mem_get_info(cuda_dev)
+    for _ in range(3):
+        _noalloc(lay_c, tab, w, x, out)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(cuda_dev)
+    assert torch.cuda.memory_allocated(cuda_dev) == torch_before
+    assert free_after == free_before
+    assert _status() == 0
