@@ -456,13 +456,12 @@ def h2d_peak_gbs(dev, nbytes: int = 256 << 20) -> float:
 def measure_dense(dev, steps: int, warmup: int, peaks: dict) -> dict:
     """The dense int8 GEMV (B200QLinear decode path) on the OLMoE output head shape: 50304 x 2048
     int8 gs64, one token, fp16 -- the largest dense layer read per decoded token (103 MB)."""
-    from moeb200 import format as Fmt
     from moeb200 import ops
 
     O, K, gs = 50304, 2048, 64
     g = torch.Generator(device=dev).manual_seed(3)
     w = torch.randn(O, K, generator=g, device=dev) * 0.02
-    q, s = Fmt.quantize(w, 8, gs)
+    q, s = ops.quantize(w, 8, gs, "absmax")
     del w
     x = torch.randn(1, K, generator=g, device=dev).half()
     y = torch.empty(1, O, dtype=torch.float16, device=dev)

@@ -39,7 +39,7 @@ class B200QLinear(nn.Module):
         """Quantise an nn.Linear like moelab's QLinear.from_linear (absmax scales, gs64 by default)."""
         w = lin.weight.data
         gs = Fmt.pick_group_size(w.shape[1], group_size)
-        q, s = Fmt.quantize(w.to(device), 8, gs)
+        q, s = ops.quantize(w.to(device).contiguous(), 8, gs, "absmax")
         bias = None if lin.bias is None else lin.bias.data.to(device)
         return cls(q, s, gs, bias, w.dtype)
 

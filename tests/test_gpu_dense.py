@@ -10,7 +10,6 @@ import torch
 import torch.nn as nn
 
 from moeb200 import _lib, ops
-from moeb200 import format as Fmt
 from moeb200.dense import B200QLinear
 from oracle import moe_oracle as O
 
@@ -24,7 +23,7 @@ DT = {"fp16": (torch.float16, "float16"), "bf16": (torch.bfloat16, "bfloat16")}
 def _qs(Oo, K, gs, dev, seed):
     g = torch.Generator(device=dev).manual_seed(seed)
     w = torch.randn(Oo, K, generator=g, device=dev) * 0.02
-    q, s = Fmt.quantize(w, 8, gs)
+    q, s = ops.quantize(w, 8, gs, "absmax")
     return q, s
 
 
