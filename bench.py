@@ -73,7 +73,7 @@ def parse():
                     help="workload of --ncu mode")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
-    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm", "decode"])
     ap.add_argument("--exchange", default="nccl", choices=["p2p", "nccl"],
                     help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
@@ -353,7 +353,20 @@ class Stack:
         return out
 
 
-def time_graph(step, K: int, W: int, world: int):
+_L2_FLUSH: dict = {}
+
+
+def l2_flush(dev) -> None:
+    """Evict the 126 MB L2: write a 256 MB buffer (outside any timed interval)."""
+    buf = _L2_FLUSH.get(str(dev))
+    if buf is None:
+        buf = _L2_FLUSH[str(dev)] = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    buf.zero_()
+
+
+def time_graph(step, K: int, W: int, world: int, flush_l2: bool = False):
+    """Captures step in a CUDA graph and returns (graph, ms per replay). flush_l2: evict L2 before
+    every timed replay and time each replay on its own (workloads smaller than L2)."""
     for _ in range(W):
         step()
     torch.cuda.synchronize()
@@ -371,6 +384,19 @@ def time_graph(step, K: int, W: int, world: int):
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    if flush_l2:
+        dev = torch.device("cuda", torch.cuda.current_device())
+        evs = []
+        for _ in range(K):
+            l2_flush(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        barrier(world)
+        return g, sum(a.elapsed_time(b) for a, b in evs) / K
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(K):
@@ -382,9 +408,17 @@ def time_graph(step, K: int, W: int, world: int):
     return g, ms
 
 
-def phase_times(step, reps: int = 5):
+def path_used() -> int:
+    """Expert path of this thread's last experts_forward call: 1 GEMV, 2 GEMM, 3 fused decode."""
+    from moeb200 import _lib
+
+    return int(_lib.lib().moeb200_path_used())
+
+
+def phase_times(step, reps: int = 5, flush_l2: bool = False):
     """Summed duration (ms) per step of the gate/up and of the down expert kernels, from CUDA events
-    that libmoeb200 records on the launching stream around its phases (eager replay of the step)."""
+    that libmoeb200 records on the launching stream around its phases (eager replay of the step;
+    flush_l2: L2 evicted before every step)."""
     import ctypes as C
 
     from moeb200 import _lib
@@ -392,8 +426,11 @@ def phase_times(step, reps: int = 5):
     lib = _lib.lib()
     step()
     torch.cuda.synchronize()
+    dev = torch.device("cuda", torch.cuda.current_device())
     _lib.check(lib.moeb200_trace_begin())
     for _ in range(reps):
+        if flush_l2:
+            l2_flush(dev)
         step()
     up, dn, n = C.c_float(), C.c_float(), C.c_int32()
     _lib.check(lib.moeb200_trace_end(C.byref(up), C.byref(dn), C.byref(n)))
@@ -408,16 +445,18 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
     L = cfg["layers"]
     step = stack.make_device_step(T)
     stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
-    g, ms = time_graph(step, steps, warmup, world)
+    # one layer's records may fit the 126 MB L2: evict it before every timed replay
+    g, ms = time_graph(step, steps, warmup, world, flush_l2=True)
     del g
     ms = max_over_ranks(ms, world)
     rb = stack.routing_bytes()
-    up_ms, dn_ms = phase_times(step)
+    up_ms, dn_ms = phase_times(step, flush_l2=True)
     pairs = rb["pairs"] + rb.get("shared_pairs", 0)
     out = {"workload": cfg["name"], "T": T, "layers": L, "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": ms,
            "ms_per_layer": ms / L, "experts_ms": up_ms + dn_ms, "records": rb["records"], "pairs": pairs,
            "layer_precisions": [lp[0] for lp in cfg["layer_precs"]] if cfg.get("layer_precs") else cfg["precs"],
-           "shared_expert": bool(cfg.get("shared"))}
+           "shared_expert": bool(cfg.get("shared")),
+           "l2": "evicted (256 MB write) before every timed replay and every traced call"}
     prefill = T * cfg["k"] >= 16 * cfg["E"]
     if prefill:
         flops = 6.0 * cfg["H"] * cfg["I"] * pairs
@@ -430,7 +469,8 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
         byts = rb["up_total"] + rb["down_total"]
         gbs = byts / ((up_ms + dn_ms) / 1e3) / 1e9
         peak = peaks.get("hbm_gbs", 6650.0)
-        out["roofline"] = {"bound": "hbm", "kernel": "grouped GEMV (up + down)", "achieved": gbs, "peak": peak,
+        kname = "fused decode kernel (one launch)" if path_used() == 3 else "grouped GEMV (up + down)"
+        out["roofline"] = {"bound": "hbm", "kernel": kname, "achieved": gbs, "peak": peak,
                            "unit": "GB/s", "frac": gbs / peak, "bytes_per_step": byts, "up_ms": up_ms,
                            "down_ms": dn_ms}
     del stack
@@ -698,17 +738,24 @@ def main():
         print(f"phase timing unavailable: {exc}", file=sys.stderr)
         up_ms = dn_ms = float("nan")
     L = cfg["layers"]
-    up_bytes_launch = rb["up_total"] / L
-    dn_bytes_launch = rb["down_total"] / L
+    fused = path_used() == 3
+    if fused:
+        # one launch per layer does gate/up, down, the combine and the cast: its bytes are both phases'
+        up_bytes_launch = (rb["up_total"] + rb["down_total"]) / L
+        dn_bytes_launch = 0.0
+        up_ms, dn_ms = up_ms + dn_ms, 0.0
+    else:
+        up_bytes_launch = rb["up_total"] / L
+        dn_bytes_launch = rb["down_total"] / L
     up_gbs = up_bytes_launch / (up_ms / 1e3) / 1e9
-    dn_gbs = dn_bytes_launch / (dn_ms / 1e3) / 1e9
-    # DRAM bytes (read + write) of one gate/up launch: the committed ncu capture of this workload's
-    # layer 0 (a 2-layer stack), scaled from that launch's algorithmic bytes to this run's average
-    # launch (DRAM traffic follows the records a layer routes to)
+    dn_gbs = dn_bytes_launch / (dn_ms / 1e3) / 1e9 if dn_ms > 0 else None
+    # DRAM bytes (read + write) of one launch of the dominant kernel: the committed ncu capture of
+    # this workload's layer 0 (a 2-layer stack), scaled from that launch's algorithmic bytes to this
+    # run's average launch (DRAM traffic follows the records a layer routes to)
     traffic, traffic_src = None, None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists() and world == 1 and T == CFG1["T"]:
-        rec = json.loads(tf.read_text()).get("gemv_up_c1_T64")
+        rec = json.loads(tf.read_text()).get("decode_c1_T64" if fused else "gemv_up_c1_T64")
         if rec:
             traffic = rec["dram_bytes"] * up_bytes_launch / rec["alg_bytes"]
             traffic_src = (rec["source"] + f"; captured launch: {rec['dram_bytes']} DRAM bytes for {rec['alg_bytes']} "
@@ -775,7 +822,9 @@ def main():
             "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) random-init experts and routers)",
             "config": headline_config(T, world, args.exchange),
             "int4_fp16_record_gbs": (rb["up"] + rb["down"]) / (ms / 1e3) / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "gemv up (gate/up dequant GEMV + SwiGLU)",
+            "roofline": {"bound": "hbm", "kernel": ("fused decode kernel (gate/up + SwiGLU + down + combine + cast, "
+                                                    "one launch per layer)") if fused else
+                         "gemv up (gate/up dequant GEMV + SwiGLU)",
                          "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": up_gbs / hbm_peak,
                          "peak_kind": peak_kind, "traffic": traffic, "traffic_source": traffic_src,
                          "bytes_per_launch": up_bytes_launch,

@@ -69,12 +69,16 @@ typedef struct {
 
 /* Device table of resident expert records for one layer (mirror of moelab/fullgraph.py:43-98
  * DeviceTable): table[p * E + e] = device address of expert e's record at precision slot p
- * (0 = not resident). Precision slots are ordered most precise first, as moelab's store lists. */
+ * (0 = not resident). Precision slots are ordered most precise first, as moelab's store lists.
+ * tma_base (no reference counterpart): a device address at or below every record the table can
+ * hold, with every record address a multiple of 4096 above it; the fused decode kernel reads
+ * records through tensor maps based there (0 = not given: that kernel is not used). */
 typedef struct {
   int32_t n_prec;
   int32_t num_experts;
   moeb200_layout layout[4];
   const int64_t* table;
+  int64_t tma_base;
 } moeb200_expert_table;
 
 const char* moeb200_version(void);
@@ -87,12 +91,16 @@ int moeb200_last_error(char* buf, size_t n);
 int moeb200_num_sms(void);
 
 /* Expert-product path of the following moeb200_experts_forward calls on the calling thread
- * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 16*E, grouped GEMV
- * otherwise), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128). */
+ * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 16*E, else the two-launch
+ * grouped GEMV), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128), 3 = the fused
+ * one-launch decode kernel (int4/int8 records with group size 64 or float records of the activation
+ * type, H and I multiples of 64 up to 2048, a table with tma_base; refused with
+ * MOEB200_ERR_UNSUPPORTED where it does not apply). */
 int moeb200_set_path(int32_t path);
 /* Pairs per grouped-GEMV work item for the following moeb200_experts_forward calls on the calling
  * thread (no reference counterpart): 0 = automatic (16 when T >= 64, else 8), 8 or 16. A larger
- * item streams an expert's record once for more tokens at the cost of more multiplies per byte. */
+ * item streams an expert's record once for more tokens at the cost of more multiplies per byte.
+ * The fused decode kernel always works on items of 8; 16 makes the automatic path skip it. */
 int moeb200_set_item_tokens(int32_t nt);
 
 /* Measurement hooks (no reference counterpart). Between trace_begin and trace_end, every
@@ -102,6 +110,10 @@ int moeb200_set_item_tokens(int32_t nt);
  * it is for benchmarks, not for captured graphs. */
 int moeb200_trace_begin(void);
 int moeb200_trace_end(float* up_ms, float* down_ms, int32_t* calls);
+/* Measurement hook (no reference counterpart): the expert-product path the calling thread's last
+ * moeb200_experts_forward(_part) call took -- 1 grouped GEMV, 2 tcgen05 GEMM, 3 fused decode kernel
+ * (its whole launch is traced as the gate/up phase) -- or 0 before the first call. */
+int moeb200_path_used(void);
 
 /* ---- router --------------------------------------------------------------------------------
  * Replaces transformers OlmoeTopKRouter / Qwen3MoeTopKRouter / Qwen3NextTopKRouter.forward

@@ -28,9 +28,11 @@ thread_local bool g_tracing = false;
 thread_local std::vector<TraceRec> g_trace_pool;
 thread_local size_t g_trace_used = 0;
 
-// Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM.
+// Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM,
+// 3 fused decode kernel.
 thread_local int g_path = 0;
 thread_local int g_item_tokens = 0;  // GEMV work-item size: 0 = automatic, else 8 or 16
+thread_local int g_last_path = 0;    // path of the thread's last experts_forward call (moeb200_path_used)
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -185,7 +187,7 @@ ForwardWs carve_forward(void* base, int T, int k, int E, int P, int H, int I, in
   w.items = c.take<Item>(n);
   w.h = c.take<uint8_t>((size_t)n * I * act_bytes(act));
   w.pre = c.take<float>(split_pre_floats(n, I));
-  w.cnt = c.take<int32_t>(split_cnt_ints(n, I));
+  w.cnt = c.take<int32_t>((size_t)std::max<int64_t>(split_cnt_ints(n, I), decode_cnt_ints(n, H)));
   w.tmaps = c.take<uint8_t>((size_t)kTmapSlots * kGemvMaxGrid * 128);
   w.acc = c.take<float>((size_t)T * H);
   w.bytes = c.off;
@@ -383,7 +385,8 @@ int moeb200_last_error(char* buf, size_t n) {
 int moeb200_num_sms(void) { return num_sms_cached(); }
 
 int moeb200_set_path(int32_t path) {
-  if (path < 0 || path > 2) return fail(MOEB200_ERR_INVALID, "set_path: path must be 0 (auto), 1 (GEMV) or 2 (GEMM)");
+  if (path < 0 || path > 3)
+    return fail(MOEB200_ERR_INVALID, "set_path: path must be 0 (auto), 1 (GEMV), 2 (GEMM) or 3 (fused decode)");
   g_path = path;
   return MOEB200_OK;
 }
@@ -393,6 +396,8 @@ int moeb200_set_item_tokens(int32_t nt) {
   g_item_tokens = nt;
   return MOEB200_OK;
 }
+
+int moeb200_path_used(void) { return g_last_path; }
 
 int moeb200_trace_begin(void) {
   g_tracing = true;
@@ -612,14 +617,25 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   fw = carve_forward(ws, T, k, E, P, H, I, act_type);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n = T * k;
-  // tcgen05 GEMM when experts see many tokens (prefill), warp GEMV otherwise (decode)
+  // tcgen05 GEMM when experts see many tokens (prefill); otherwise the fused decode kernel when the
+  // layouts allow it (items of <= 8 pairs), else the two-launch grouped GEMV
   const bool gemm_ok = (H % 128 == 0) && (I % 128 == 0);
   bool gemm = g_path == 2 || (g_path == 0 && (int64_t)n >= 16ll * E);
   if (gemm && !gemm_ok) {
     if (g_path == 2) return fail(MOEB200_ERR_UNSUPPORTED, "GEMM path needs H and I multiples of 128 (H=%d, I=%d)", H, I);
     gemm = false;
   }
-  const int nt = gemm ? 128 : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
+  const bool dec_ok = ex->tma_base != 0 && ex->tma_base % 4096 == 0 && decode_supported(ex->layout, P, act_type, H, I);
+  if (g_path == 3 && !dec_ok)
+    return fail(MOEB200_ERR_UNSUPPORTED, "decode path: these record layouts or shapes are not supported by the fused "
+                                         "decode kernel");
+  // the fused decode kernel is taken only when asked for (path 3): measured slower than the
+  // two-launch grouped GEMV on every decode workload of the build's configs so far
+  const bool decode = !gemm && g_path == 3;
+  const int nt = gemm ? 128 : decode ? 8 : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
+  g_last_path = gemm ? 2 : decode ? 3 : 1;
+  // upper bound on items: every key splits into ceil(c / nt) items
+  const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)(e_hi - e_lo) * P);
   DispatchParams dp{};
   dp.idx = idx;
   dp.level = level;
@@ -654,8 +670,40 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   dp.status = &fw.hdr->status;
   dp.job_next = fw.hdr->job_next;
   dp.zero_cnt = fw.cnt;
-  dp.zero_n = split_cnt_ints(n, I);
+  dp.zero_n = decode ? (int)decode_cnt_ints(max_items, H) : split_cnt_ints(n, I);
+  dp.slot_items = decode ? fw.cnt + kDecSlotItems : nullptr;
   CUDA_TRY(launch_dispatch(dp, s));
+  if (decode) {
+    DecodeParams q{};
+    q.items = fw.items;
+    q.n_items = &fw.hdr->n_items;
+    q.pos = fw.pos_k;
+    q.wflat = w;
+    q.k = k;
+    q.H = H;
+    q.I = I;
+    q.T = T;
+    q.x = x;
+    q.h = fw.h;
+    q.acc = part ? part : fw.acc;
+    q.out = part ? nullptr : out;
+    q.add = 0;
+    q.max_items = (int)max_items;
+    q.status = &fw.hdr->status;
+    q.ctr = fw.cnt;
+    q.updone = fw.cnt + kDecUpdone;
+    q.slot_items = fw.cnt + kDecSlotItems;
+    q.nprec = P;
+    q.tma_base = ex->tma_base;
+    for (int p = 0; p < P; ++p) q.lay[p] = to_dev(ex->layout[p]);
+    const int64_t units = max_items * (I / 8 + H / 16);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms_cached(), units));
+    CUDA_TRY(trace_mark(0, s));
+    CUDA_TRY(launch_decode(q, ex->layout, P, act_type, grid, s));
+    CUDA_TRY(trace_mark(1, s));
+    CUDA_TRY(trace_mark(2, s));
+    return MOEB200_OK;
+  }
   GemvParams gp{};
   gp.items = fw.items;
   gp.n_items = &fw.hdr->n_items;
@@ -676,8 +724,6 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.job_next = fw.hdr->job_next;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
-  // upper bound on items: every key splits into ceil(c / nt) items
-  const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)(e_hi - e_lo) * P);
   return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, part ? nullptr : out, /*add=*/0,
                            gemm);
 }

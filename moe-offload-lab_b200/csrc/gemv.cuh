@@ -85,6 +85,45 @@ __host__ __device__ inline int gemv_b_stride(int wtype) {
   return kStepBytes * 8 / gemv_wbits(wtype) * 2 + 16;
 }
 
+// Fused decode kernel (decode.cu): gate/up + SwiGLU + down + combine + cast in one launch, for work
+// items of at most 8 pairs numbered slot-major. Counters (zeroed by the kernel that writes the
+// items): ctr[1] CTAs that cleared acc, ctr[2] CTAs done; updone[max_items] gate/up units finished
+// per item. slot_items[P + 1]: first item of each precision slot, then the item count.
+struct DecodeParams {
+  const Item* items;
+  const int32_t* n_items;
+  const int32_t* pos;      // sorted pair list: flat positions t*k + j
+  const float* wflat;      // [T*k] router weights
+  int32_t k;
+  int32_t H;
+  int32_t I;
+  int32_t T;               // rows of acc (and out)
+  const void* x;           // [tokens, H] activations
+  void* h;                 // [n_pairs, I] activations, row j = sorted pair j
+  float* acc;              // [T, H] fp32 combine buffer (the result itself when out is null)
+  void* out;               // [T, H] activation type, or null
+  int32_t add;             // out += instead of out =
+  int32_t max_items;
+  int32_t* status;
+  int32_t* ctr;
+  int32_t* updone;
+  const int32_t* slot_items;
+  int32_t nprec;
+  int64_t tma_base;        // base of the weight tensor maps (moeb200_expert_table.tma_base)
+  LayoutDev lay[4];
+};
+// Words of the decode kernel's counter region, zeroed with the items: ctr[4], slot_items[5] (padded
+// to 12), then updone[max_items].
+constexpr int kDecSlotItems = 4;
+constexpr int kDecUpdone = 16;
+inline int64_t decode_cnt_ints(int64_t max_items, int H) {
+  (void)H;
+  return kDecUpdone + max_items;
+}
+bool decode_supported(const moeb200_layout* lays, int nlay, int act_type, int H, int I);
+cudaError_t launch_decode(const DecodeParams& p, const moeb200_layout* lays, int nlay, int act_type, int grid,
+                          cudaStream_t s);
+
 // host launchers (gemv.cu)
 // Plans split-K and the shared-memory geometry of the two GEMV phases, then launches gate/up and
 // down (with trace marks around them). nb: token blocks of 8 per item (1 or 2).

@@ -494,6 +494,14 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   const int32_t n_kept = block_exclusive_scan<PER>(off_k, sh_warp);
   block_exclusive_scan<PER>(off_e, sh_warp);
   const int32_t n_items = block_exclusive_scan<PER>(off_i, sh_warp);
+  if (p.slot_items) {  // slot s's items start at key s*E (slot-major numbering)
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int m = tid * PER + i;
+      if (m < keys && m % p.E == 0) p.slot_items[m / p.E] = off_i[i];
+    }
+    if (tid == 0) p.slot_items[p.P] = n_items;
+  }
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int key = tid * PER + i;

@@ -52,6 +52,8 @@ struct DispatchParams {
   int32_t* job_next;      // [2] GEMV job counters to zero with the items, or null
   int32_t* zero_cnt;      // [zero_n] split-K arrival counters to zero with the items, or null
   int32_t zero_n;
+  int32_t* slot_items;    // [P + 1] first item of each precision slot (items are numbered slot-major)
+                          // and the item count, or null
 };
 
 cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,

@@ -52,6 +52,35 @@ cudaError_t tma_weight_template(CUtensorMap* out, int row_bytes, int rows, int b
   return cudaSuccess;
 }
 
+cudaError_t tma_rows3d_map(CUtensorMap* out, uint64_t base, int row_bytes, int box_rows) {
+  static std::mutex mu;
+  static std::map<std::tuple<uint64_t, int, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(base, row_bytes, box_rows);
+  auto f = cache.find(key);
+  if (f != cache.end()) {
+    *out = f->second;
+    return cudaSuccess;
+  }
+  auto encode = encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  // [segment][row][128 bytes]: dim 0 the bytes of a 128-byte segment, dim 1 rows (pitch row_bytes),
+  // dim 2 the row's segments (pitch 128); a box is box_rows rows x every segment, segment-major
+  const cuuint64_t dims[3] = {128u, 0x7fffffffull, (cuuint64_t)(row_bytes / 128)};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, 128u};
+  const cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, (cuuint32_t)(row_bytes / 128)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUtensorMap m;
+  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, reinterpret_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (cache.size() > 256) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return cudaSuccess;
+}
+
 cudaError_t tma_rows16_map(CUtensorMap* out, const void* base, int cols, int rows, int box_rows, int act_type) {
   auto encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;

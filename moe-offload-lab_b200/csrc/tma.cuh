@@ -44,6 +44,11 @@ __device__ __forceinline__ void retarget_tmap(const CUtensorMap& tmpl, uint32_t 
 // kernels swap in each record's address. Cached per shape.
 cudaError_t tma_weight_template(CUtensorMap* out, int row_bytes, int rows, int box_rows, void* placeholder);
 
+// Host: 3-D uint8 tensor map [segment][row][128 bytes] of all memory from `base` on: rows of
+// row_bytes (a multiple of 128), boxes of box_rows rows x every 128-byte segment of a row, laid out
+// segment-major in shared memory with 128-byte swizzle. Cached per (base, row_bytes, box_rows).
+cudaError_t tma_rows3d_map(CUtensorMap* out, uint64_t base, int row_bytes, int box_rows);
+
 // Host: tensor map of a row-major 16-bit matrix [rows][cols] at `base`, boxes of 64 columns x
 // box_rows with 128-byte swizzle (the K-major operand layout of the tensor cores).
 cudaError_t tma_rows16_map(CUtensorMap* out, const void* base, int cols, int rows, int box_rows, int act_type);

@@ -36,7 +36,7 @@ class Policy(C.Structure):
 
 class ExpertTable(C.Structure):
     _fields_ = [("n_prec", C.c_int32), ("num_experts", C.c_int32), ("layout", Layout * 4),
-                ("table", C.c_void_p)]
+                ("table", C.c_void_p), ("tma_base", C.c_int64)]
 
 
 class PeerGroup(C.Structure):
@@ -53,6 +53,7 @@ _SIGS = {
     "moeb200_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
     "moeb200_num_sms": (C.c_int, []),
     "moeb200_trace_begin": (C.c_int, []),
+    "moeb200_path_used": (C.c_int, []),
     "moeb200_trace_end": (C.c_int, [C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "moeb200_router": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                  _P, _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),

@@ -24,6 +24,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .runtime import aligned_empty
 
 
 class SlotPlan:
@@ -86,7 +87,8 @@ class ColdExperts:
         self.buf = {}
         for p, n in slots.items():
             rb = runtime.layouts[p]["record_bytes"]  # a multiple of 4096: every slot stays aligned
-            self.buf[p] = torch.empty(n, rb, dtype=torch.uint8, device=self.dev)
+            self.buf[p] = aligned_empty((n, rb), self.dev)
+            runtime.note_region(self.buf[p].data_ptr())
         self.last_use: dict[tuple[str, int], torch.cuda.Event] = {}
         self.uploaded_bytes = 0
         self.uploads = 0

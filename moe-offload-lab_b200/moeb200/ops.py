@@ -15,21 +15,35 @@ from . import _lib
 from .format import ACT_TYPE
 
 _WS: dict[tuple[int, int], torch.Tensor] = {}
+# Buffers replaced by a larger one. A CUDA graph captured while one of them was current keeps its
+# address, so they stay allocated: replaying such a graph after a larger call grew the workspace
+# must not touch freed memory. Growth at least doubles, so the retired buffers of a (device, slot)
+# together are smaller than its current one.
+_RETIRED: list[torch.Tensor] = []
 
 
 def workspace(nbytes: int, device: torch.device, slot: int = 0) -> torch.Tensor:
     """A cached uint8 device buffer of at least nbytes (one per device and slot).
 
-    Slots let callers that run concurrently (or that are captured in different graphs) keep
-    separate scratch. The buffer only grows; growing outside graph capture keeps captures valid.
+    Slots let callers that run concurrently keep separate scratch. The buffer only grows, and a
+    buffer that was replaced stays allocated (see release_workspaces), so graphs captured with it
+    stay valid; replays of graphs that share a slot must not overlap on the GPU.
     """
     dev = torch.device(device)
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), slot)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
+        if buf is not None:
+            _RETIRED.append(buf)
+        grow = 2 * buf.numel() if buf is not None else 0
+        buf = torch.empty(max(nbytes, grow, 1 << 16), dtype=torch.uint8, device=dev)
         _WS[key] = buf
     return buf
+
+
+def release_workspaces() -> None:
+    """Free the replaced workspaces. Only safe once no captured graph that used them is replayed."""
+    _RETIRED.clear()
 
 
 def _stream(device=None) -> C.c_void_p:
@@ -270,8 +284,9 @@ def shared_expert(layout_c: _lib.Layout, record: torch.Tensor, wg: torch.Tensor,
 
 
 def set_path(path: str) -> None:
-    """Expert-product path for this thread's next experts_forward calls: "auto", "gemv" or "gemm"."""
-    _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2}[path]))
+    """Expert-product path for this thread's next experts_forward calls: "auto", "gemv", "gemm" or "decode"
+    (the fused one-launch decode kernel)."""
+    _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2, "decode": 3}[path]))
 
 
 def set_item_tokens(nt: int) -> None:

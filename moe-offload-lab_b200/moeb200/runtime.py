@@ -41,6 +41,29 @@ def level_to_slot(level: int, n_prec: int) -> int:
     return 0 if level == 0 else n_prec - 1
 
 
+def aligned_copy(blob: torch.Tensor, align: int = 4096) -> torch.Tensor:
+    """blob itself when its address is a multiple of align, else a copy at such an address (a view
+    into a slightly larger buffer, which the view keeps alive)."""
+    if blob.data_ptr() % align == 0:
+        return blob
+    n = blob.numel()
+    buf = torch.empty(n + align, dtype=torch.uint8, device=blob.device)
+    off = (-buf.data_ptr()) % align
+    out = buf[off:off + n]
+    out.copy_(blob.reshape(-1))
+    return out
+
+
+def aligned_empty(shape, device, align: int = 4096) -> torch.Tensor:
+    """An uninitialised uint8 device tensor whose data starts at a multiple of align."""
+    n = 1
+    for d in shape:
+        n *= d
+    buf = torch.empty(n + align, dtype=torch.uint8, device=device)
+    off = (-buf.data_ptr()) % align
+    return buf[off:off + n].view(shape)
+
+
 class B200Runtime:
     """Resident expert records of every MoE layer plus the policy, for the B200 kernels.
 
@@ -62,6 +85,9 @@ class B200Runtime:
         self._ctables: dict[int, _lib.ExpertTable] = {}
         self._records: dict[tuple[int, int, str], torch.Tensor] = {}
         self._lays_c = [to_c(self.layouts[p]) for p in self.precisions]
+        # lowest device address a record of this runtime can have (records and slots are 4096-byte
+        # aligned): the base of the fused decode kernel's tensor maps
+        self._tma_base = 0
         for layer in layers:
             self._table(layer)
         self.miss = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -81,15 +107,26 @@ class B200Runtime:
             for i, L in enumerate(self._lays_c):
                 ct.layout[i] = L
             ct.table = t.data_ptr()
+            ct.tma_base = self._tma_base
             self._ctables[layer] = ct
         return t
 
+    def note_region(self, addr: int) -> None:
+        """Register device memory that records may occupy (4096-byte aligned), e.g. upload slots."""
+        if addr % 4096:
+            raise ValueError("record regions must be 4096-byte aligned")
+        if self._tma_base == 0 or addr < self._tma_base:
+            self._tma_base = addr
+            for ct in self._ctables.values():
+                ct.tma_base = addr
+
     def add_record(self, layer: int, expert: int, prec: str, blob: torch.Tensor) -> None:
-        """Make a resident record visible to the kernels (blob: uint8 CUDA tensor, kept alive)."""
+        """Make a resident record visible to the kernels (blob: uint8 CUDA tensor, kept alive). A
+        record that is not 4096-byte aligned is copied into an aligned buffer first."""
         if blob.device != self.device or blob.dtype != torch.uint8:
             raise ValueError("records must be uint8 tensors on the runtime's device")
-        if blob.data_ptr() % 256:
-            raise ValueError("records must be 256-byte aligned")
+        blob = aligned_copy(blob)
+        self.note_region(blob.data_ptr())
         p = self.precisions.index(prec)
         self._records[(layer, expert, prec)] = blob
         self._table(layer)[p, expert] = blob.data_ptr()

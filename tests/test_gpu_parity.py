@@ -9,6 +9,7 @@ import pytest
 import torch
 
 import moeb200
+from moeb200 import _lib
 from moeb200 import format as F
 from moeb200 import ops
 from moeb200.runtime import B200Runtime
@@ -192,8 +193,23 @@ LAYER_CASES = [
 ]
 
 
+def _run_on_path(path, fn):
+    """fn() with the expert-product path forced; a shape the fused decode kernel does not take is
+    skipped (the automatic path would use the grouped GEMV there)."""
+    ops.set_path(path)
+    try:
+        return fn()
+    except _lib.MoeB200Error as exc:
+        if path == "decode" and exc.code == _lib.ERR_UNSUPPORTED:
+            pytest.skip("layout not taken by the fused decode kernel")
+        raise
+    finally:
+        ops.set_path("auto")
+
+
+@pytest.mark.parametrize("path", ["gemv", "decode"])
 @pytest.mark.parametrize("case", LAYER_CASES, ids=[c[0] for c in LAYER_CASES])
-def test_experts_forward_matches_oracle(cuda_dev, case):
+def test_experts_forward_matches_oracle(cuda_dev, case, path):
     name, H, I, E, k, T, precs, pol, act = case
     dt = ACTS[act]
     lays, recs = layer_records(precs, H, I, E, seed=zlib.crc32(name.encode()) % 1000, device=cuda_dev, std=0.02 if H > 64 else 0.05)
@@ -205,11 +221,7 @@ def test_experts_forward_matches_oracle(cuda_dev, case):
     x = torch.randn(T, H, generator=g, device=cuda_dev).to(dt)
     logits = torch.randn(T, E, generator=g, device=cuda_dev)
     wv, idx = torch.topk(logits.softmax(-1), k, dim=-1)
-    ops.set_path("gemv")
-    try:
-        out = rt.run_layer(0, x, idx, wv, torch.nn.SiLU())
-    finally:
-        ops.set_path("auto")
+    out = _run_on_path(path, lambda: rt.run_layer(0, x, idx, wv, torch.nn.SiLU()))
     lvl, skip = rt.levels(0, wv)
     P = len(precs)
     lv = np.zeros((T, k), np.int64) if lvl is None else lvl.cpu().numpy().astype(np.int64)
@@ -222,10 +234,12 @@ def test_experts_forward_matches_oracle(cuda_dev, case):
     assert int(rt.miss.item()) == 0
 
 
-def test_calls_in_a_row_reuse_the_workspace(cuda_dev):
-    # The GEMV job counters and the split-K arrival counters live in the workspace and are zeroed by
-    # the kernel that writes each call's items: T = 1 (K split), T = 64 (jobs drawn from the counter),
-    # then T = 3 and T = 1 again on the same workspace must each match the oracle.
+@pytest.mark.parametrize("path", ["gemv", "decode"])
+def test_calls_in_a_row_reuse_the_workspace(cuda_dev, path):
+    # The GEMV job counters and the split-K arrival counters (decode kernel: unit claims, per-item
+    # and per-row-block counters) live in the workspace and are zeroed by the kernel that writes each
+    # call's items: T = 1 (K split), T = 64 (jobs drawn from the counter), then T = 3 and T = 1 again
+    # on the same workspace must each match the oracle.
     H, I, E, k = 2048, 1024, 64, 8
     precs = ["fp16", "int4"]
     lays, recs = layer_records(precs, H, I, E, seed=77, device=cuda_dev, std=0.02)
@@ -235,7 +249,7 @@ def test_calls_in_a_row_reuse_the_workspace(cuda_dev):
             rt.add_record(0, e, p, recs[p][e])
     recs_np = [[b.cpu().numpy() for b in recs[p]] for p in precs]
     g = torch.Generator(device=cuda_dev).manual_seed(11)
-    ops.set_path("gemv")
+    ops.set_path(path)
     try:
         for T in (1, 64, 3, 1):
             x = torch.randn(T, H, generator=g, device=cuda_dev).half()
@@ -270,3 +284,21 @@ def test_missing_expert_counted_and_skipped(cuda_dev):
     ref = O.moe_layer(act_np(x), idx.cpu().numpy(), wv.cpu().numpy(), None, skip,
                       [[b.cpu().numpy() for b in recs["int4"]]], [lays["int4"]], E)
     assert O.max_rel_err(act_np(out), ref) < TOL
+
+
+@pytest.mark.parametrize("path", ["gemv", "decode"])
+def test_every_pair_skipped_gives_zero_output(cuda_dev, path):
+    # no work item at all: the output must still be written (zeros), on every path
+    H, I, E, k, T = 2048, 512, 16, 4, 3
+    lays, recs = layer_records(["int4"], H, I, E, seed=4, device=cuda_dev, std=0.02)
+    rt = B200Runtime(["int4"], lays, E, cuda_dev, ops.PolicySpec("lo"), layers=[0])
+    for e in range(E):
+        rt.add_record(0, e, "int4", recs["int4"][e])
+    x = torch.randn(T, H, device=cuda_dev).half()
+    idx = torch.arange(k, device=cuda_dev).repeat(T, 1)
+    wv = torch.full((T, k), 0.25, device=cuda_dev)
+    skip = torch.ones(T, k, dtype=torch.uint8, device=cuda_dev)
+    out = torch.full((T, H), 7.0, dtype=torch.float16, device=cuda_dev)
+    _run_on_path(path, lambda: rt.run_layer(0, x, idx, wv, out=out, level=torch.zeros_like(skip), skip=skip))
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
