@@ -228,9 +228,12 @@ int moeb200_ep_unpack(const void* rows, int32_t n, int32_t H, int32_t k, int32_t
  * moeb200_experts_forward_part into the own partial sums, moeb200_ep_signal(1),
  * moeb200_ep_combine_peers (waits for every rank's partial sums, adds this rank's tokens' rows in
  * rank order, casts once). Waits are bounded: on timeout the status word is set. Every rank must run
- * the same sequence of calls with the same T. */
+ * the same sequence of calls with the same T. spin is the number of polls a wait makes before it
+ * gives up (0 = 2^22, several seconds; each poll sleeps about 64 ns); a smaller budget makes a
+ * missing peer show up in the status word sooner. */
 typedef struct {
-  int32_t G, rank, T, H, k, _pad;
+  int32_t G, rank, T, H, k;
+  uint32_t spin;         /* polls per wait, 0 = default */
   const int64_t* rows;   /* [G] device array */
   const int64_t* parts;  /* [G] device array */
   const int64_t* flags;  /* [G] device array */

@@ -158,9 +158,9 @@ __device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait (bounded) until *flag >= epoch; false and status set on timeout.
-__device__ bool wait_flag(const int32_t* flag, int epoch, int32_t* status) {
-  for (uint32_t i = 0; i < kPeerSpin; ++i) {
+// Wait (bounded: `spin` polls) until *flag >= epoch; false and status set on timeout.
+__device__ bool wait_flag(const int32_t* flag, int epoch, uint32_t spin, int32_t* status) {
+  for (uint32_t i = 0; i < spin; ++i) {
     if (ld_acquire_sys(flag) >= epoch) return true;
     __nanosleep(64);
   }
@@ -175,6 +175,7 @@ struct PeerArgs {
   int32_t* epoch;        // this rank's call counter
   int32_t* status;       // this rank's status word
   int32_t G, rank, T, H, k;
+  uint32_t spin;         // polls per wait
 };
 
 // which == 0: epoch += 1 first. Then flag[which][rank] = epoch on every rank.
@@ -200,7 +201,7 @@ __global__ void ep_gather_kernel(PeerArgs a, int xbytes, int rb, int rpb, uint8_
   __shared__ int ok;
   if (threadIdx.x == 0) {
     const int32_t* f = reinterpret_cast<const int32_t*>(a.flags[a.rank]) + s;
-    ok = wait_flag(f, *a.epoch, a.status);
+    ok = wait_flag(f, *a.epoch, a.spin, a.status);
   }
   __syncthreads();
   const uint8_t* src = reinterpret_cast<const uint8_t*>(a.rows[s]);
@@ -233,7 +234,7 @@ __global__ void ep_combine_peers_kernel(PeerArgs a, AT* __restrict__ out, int ad
   if (threadIdx.x == 0) {
     ok = 1;
     const int32_t* f = reinterpret_cast<const int32_t*>(a.flags[a.rank]) + a.G;
-    for (int s = 0; s < a.G; ++s) ok &= wait_flag(f + s, *a.epoch, a.status);
+    for (int s = 0; s < a.G; ++s) ok &= wait_flag(f + s, *a.epoch, a.spin, a.status);
   }
   __syncthreads();
   const int64_t n = (int64_t)a.T * a.H;
@@ -258,6 +259,7 @@ PeerArgs peer_args(const moeb200_peer_group* g) {
   a.T = g->T;
   a.H = g->H;
   a.k = g->k;
+  a.spin = g->spin ? g->spin : kPeerSpin;
   return a;
 }
 

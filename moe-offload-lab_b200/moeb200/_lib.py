@@ -43,7 +43,7 @@ class PeerGroup(C.Structure):
     """moeb200_peer_group: device tables of every rank's mapped exchange buffers."""
 
     _fields_ = [("G", C.c_int32), ("rank", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("k", C.c_int32),
-                ("_pad", C.c_int32), ("rows", C.c_void_p), ("parts", C.c_void_p), ("flags", C.c_void_p),
+                ("spin", C.c_uint32), ("rows", C.c_void_p), ("parts", C.c_void_p), ("flags", C.c_void_p),
                 ("epoch", C.c_void_p), ("status", C.c_void_p)]
 
 

@@ -39,6 +39,12 @@ import torch.distributed as dist
 import torch.nn as nn
 
 
+class PeerFailure(RuntimeError):
+    """A collective of the expert-parallel exchange did not complete: a peer raised and left, exited,
+    or stalled past the process group's timeout. The group is unusable afterwards: every later call
+    on the same ExpertParallel raises this at once instead of entering another collective."""
+
+
 def partition(num_experts: int, world: int, rank: int) -> tuple[int, int]:
     """Contiguous expert block [lo, hi) owned by `rank` of `world` ranks."""
     if world <= 0 or not 0 <= rank < world:
@@ -186,6 +192,16 @@ class ExpertParallel:
         self.exchange = exchange
         self._bufs: dict[tuple, _Bufs] = {}
         self._peers: dict[tuple, PeerExchange] = {}
+        self.failed: str | None = None  # the first failed collective, once one failed
+
+    def _collective(self, phase: str, fn, *args) -> None:
+        """Run one collective of the exchange; a failure (peer error, exit or timeout) marks the group
+        failed and raises PeerFailure naming the phase."""
+        try:
+            fn(*args, group=self.group)
+        except Exception as exc:
+            self.failed = f"{phase} on rank {self.rank}: {exc}"
+            raise PeerFailure(self.failed) from exc
 
     def close(self) -> None:
         for px in self._peers.values():
@@ -229,6 +245,8 @@ class ExpertParallel:
         w = top_k_weights.reshape(T, k).float().contiguous()
         if level is None and skip is None:
             level, skip = self.runtime.levels(layer, w)
+        if self.failed is not None:
+            raise PeerFailure(f"the exchange group failed earlier ({self.failed})")
         b = self._buffers(T, H, k, x2.dtype, x2.device)
         if out is None:
             out = torch.empty_like(x2)
@@ -236,11 +254,11 @@ class ExpertParallel:
             self._run_p2p(layer, x2, idx, w, level, skip, b, out.view(T, H))
             return out.view_as(x)
         self.ops.pack(x2, idx, w, level, skip, b.rows)
-        dist.all_gather_into_tensor(b.rows_all, b.rows, group=self.group)
+        self._collective("dispatch all_gather", dist.all_gather_into_tensor, b.rows_all, b.rows)
         self.ops.unpack(b.rows_all, H, k, x2.dtype, b.x_all, b.idx_all, b.w_all, b.level_all, b.skip_all)
         self.ops.local(self.runtime, layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all,
                        b.skip_all, b.part)
-        dist.all_to_all_single(b.recv, b.part, group=self.group)
+        self._collective("combine all_to_all", dist.all_to_all_single, b.recv, b.part)
         self.ops.combine(b.recv.view(self.world, T, H), out.view(T, H))
         return out.view_as(x)
 

@@ -36,7 +36,7 @@ def workspace(nbytes: int, device: torch.device, slot: int = 0) -> torch.Tensor:
         if buf is not None:
             _RETIRED.append(buf)
         grow = 2 * buf.numel() if buf is not None else 0
-        buf = torch.empty(max(nbytes, grow, 1 << 16), dtype=torch.uint8, device=dev)
+        buf = torch.zeros(max(nbytes, grow, 1 << 16), dtype=torch.uint8, device=dev)  # status word 0
         _WS[key] = buf
     return buf
 

@@ -1,0 +1,158 @@
+"""Failure detection on the GPU without a GPU fault: the device status word.
+
+* An expert index outside [0, E) reaches the dispatch: the pair is dropped, the status word reads 2
+  (bad index) and the call still returns with every other pair summed.
+* A bounded device wait runs out: the peer-memory exchange on ONE GPU, with a peer group of two
+  ranks whose second rank never raises its flags (both table entries point at this GPU's own
+  buffers, so nothing leaves the device). The gather and the combine give up after the group's
+  spin budget, set the status word to 1, write the missing rank's rows as dropped and return; the
+  context stays usable and a later call with the flag raised completes with status 0.
+
+The reference has no device-side wait to time out (its expert-parallel path is not built) and
+switches to its torch path on a kernel exception (moelab runtime.py:346-348); here every device
+wait is bounded and reports through the status word instead."""
+
+from __future__ import annotations
+
+import ctypes as C
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from moeb200 import _lib, ops
+from moeb200.runtime import B200Runtime
+from oracle import moe_oracle as O
+
+from gpu_util import TOL, act_np, layer_records
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("path", ["gemv", "gemm", "decode"])
+def test_out_of_range_expert_sets_status_and_is_dropped(cuda_dev, path):
+    H, I, E, k, T = 2048, 512, 16, 4, 6
+    lays, recs = layer_records(["int4"], H, I, E, seed=12, device=cuda_dev, std=0.02)
+    rt = B200Runtime(["int4"], lays, E, cuda_dev, ops.PolicySpec("lo"), layers=[0])
+    for e in range(E):
+        rt.add_record(0, e, "int4", recs["int4"][e])
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    x = torch.randn(T, H, generator=g, device=cuda_dev).half()
+    idx = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(t))[:k] for t in range(T)]).to(cuda_dev)
+    idx[2, 1] = E  # one past the last expert
+    idx[4, 3] = -1
+    wv = torch.full((T, k), 0.25, device=cuda_dev)
+    level = torch.zeros(T, k, dtype=torch.uint8, device=cuda_dev)
+    skip = torch.zeros(T, k, dtype=torch.uint8, device=cuda_dev)
+    table = rt._ctables[0]
+    ws = torch.zeros(_lib.lib().moeb200_experts_workspace(C.byref(table), T, k), dtype=torch.uint8, device=cuda_dev)
+    ops.set_path(path)
+    try:
+        out = ops.experts_forward(table, x, idx, wv, level, skip, miss=rt.miss, ws=ws)
+    except _lib.MoeB200Error as exc:
+        if path == "decode" and exc.code == _lib.ERR_UNSUPPORTED:
+            pytest.skip("layout not taken by the fused decode kernel")
+        raise
+    finally:
+        ops.set_path("auto")
+    assert ops.check_workspace(ws) == 2
+    assert ops.check_workspace(ws) == 0  # reading the word clears it
+    bad = ((idx < 0) | (idx >= E)).cpu().numpy()
+    ref = O.moe_layer(act_np(x), np.where(bad, 0, idx.cpu().numpy()), wv.cpu().numpy(), None, bad,
+                      [[b.cpu().numpy() for b in recs["int4"]]], [lays["int4"]], E)
+    assert O.max_rel_err(act_np(out), ref) < TOL
+    assert int(rt.miss.item()) == 0
+
+
+class _OneGpuPair:
+    """A peer group of G=2 ranks on one GPU, rank 0 being this process: both entries of the rows,
+    partial-sum and flag tables point at this GPU's own buffers, so rank 1's flags (entries
+    [0][1] and [1][1] of the flag array) are raised by nobody unless the test writes them."""
+
+    def __init__(self, dev, T, H, k, spin):
+        self.T, self.H, self.k = T, H, k
+        self.rb = ops.ep_row_bytes(H, k, torch.float16)
+        self.rows = torch.zeros(T, self.rb, dtype=torch.uint8, device=dev)
+        self.parts = torch.zeros(2 * T, H, dtype=torch.float32, device=dev)
+        self.flags = torch.zeros(2, 2, dtype=torch.int32, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.tabs = [torch.tensor([t.data_ptr()] * 2, dtype=torch.int64, device=dev)
+                     for t in (self.rows, self.parts, self.flags)]
+        g = _lib.PeerGroup()
+        g.G, g.rank, g.T, g.H, g.k, g.spin = 2, 0, T, H, k, spin
+        g.rows, g.parts, g.flags = (t.data_ptr() for t in self.tabs)
+        g.epoch, g.status = self.epoch.data_ptr(), self.status.data_ptr()
+        self.g = g
+
+    def signal(self, which):
+        _lib.check(_lib.lib().moeb200_ep_signal(C.byref(self.g), which, ops._stream()))
+
+    def gather(self, x_all, idx_all, w_all, lvl_all, skip_all):
+        _lib.check(_lib.lib().moeb200_ep_gather(C.byref(self.g), _lib.F16, x_all.data_ptr(), idx_all.data_ptr(),
+                                                w_all.data_ptr(), lvl_all.data_ptr(), skip_all.data_ptr(),
+                                                ops._stream()))
+
+    def combine(self, out):
+        _lib.check(_lib.lib().moeb200_ep_combine_peers(C.byref(self.g), _lib.F16, out.data_ptr(), 0, ops._stream()))
+
+
+def test_peer_wait_runs_out_and_sets_status(cuda_dev):
+    T, H, k = 8, 256, 4
+    pair = _OneGpuPair(cuda_dev, T, H, k, spin=4096)
+    gen = torch.Generator(device=cuda_dev).manual_seed(1)
+    x = torch.randn(T, H, generator=gen, device=cuda_dev).half()
+    idx = torch.randint(0, 16, (T, k), generator=gen, device=cuda_dev)
+    w = torch.rand(T, k, generator=gen, device=cuda_dev)
+    lvl = torch.ones(T, k, dtype=torch.uint8, device=cuda_dev)
+    sk = torch.zeros(T, k, dtype=torch.uint8, device=cuda_dev)
+    ops.ep_pack(x, idx, w, lvl, sk, rows=pair.rows)
+    x_all = torch.full((2 * T, H), 5.0, dtype=torch.float16, device=cuda_dev)
+    idx_all = torch.full((2 * T, k), 99, dtype=torch.int64, device=cuda_dev)
+    w_all = torch.full((2 * T, k), 5.0, device=cuda_dev)
+    lvl_all = torch.full((2 * T, k), 7, dtype=torch.uint8, device=cuda_dev)
+    skip_all = torch.zeros(2 * T, k, dtype=torch.uint8, device=cuda_dev)
+
+    # rows phase: this rank raises its own flag (epoch 1); rank 1's flag stays 0
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pair.signal(0)
+    pair.gather(x_all, idx_all, w_all, lvl_all, skip_all)
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert waited < 2.0, waited  # the small budget, not the default several-second one
+    assert int(pair.epoch.item()) == 1
+    assert int(pair.status.item()) == 1
+    assert torch.equal(x_all[:T], x) and torch.equal(idx_all[:T], idx) and torch.equal(w_all[:T], w)
+    assert torch.equal(lvl_all[:T], lvl) and torch.equal(skip_all[:T], sk)
+    # the rows that never arrived are written as dropped pairs of zero tokens
+    assert torch.count_nonzero(x_all[T:]).item() == 0 and torch.count_nonzero(w_all[T:]).item() == 0
+    assert bool((skip_all[T:] == 1).all()) and torch.count_nonzero(idx_all[T:]).item() == 0
+
+    # combine phase: partial sums of rank 1 never flagged -> zeros, status still 1
+    pair.status.zero_()
+    pair.parts.normal_()
+    out = torch.full((T, H), 3.0, dtype=torch.float16, device=cuda_dev)
+    pair.signal(1)
+    pair.combine(out)
+    torch.cuda.synchronize()
+    assert int(pair.status.item()) == 1
+    assert torch.count_nonzero(out).item() == 0
+
+    # the context is still usable, and with rank 1's flags raised the same calls complete cleanly
+    y = (torch.randn(64, 64, device=cuda_dev) @ torch.randn(64, 64, device=cuda_dev)).sum()
+    assert torch.isfinite(y)
+    pair.status.zero_()
+    pair.signal(0)  # epoch 2
+    pair.flags[0, 1] = 2
+    pair.gather(x_all, idx_all, w_all, lvl_all, skip_all)
+    pair.signal(1)
+    pair.flags[1, 1] = 2
+    pair.combine(out)
+    torch.cuda.synchronize()
+    assert int(pair.status.item()) == 0
+    assert torch.equal(x_all[T:], x) and torch.equal(skip_all[T:], sk)
+    # out[t] = parts[0*T + t] + parts[0*T + t]: rank 0's rows of both (identical) partial-sum tables
+    ref = (pair.parts[:T] + pair.parts[:T]).half()
+    assert torch.equal(out, ref)
