@@ -73,7 +73,7 @@ def parse():
                     help="workload of --ncu mode")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: one warm-up step, then one device step inside cudaProfilerStart/Stop")
-    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm", "decode"])
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm", "decode", "ws"])
     ap.add_argument("--exchange", default="nccl", choices=["p2p", "nccl"],
                     help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
@@ -171,7 +171,8 @@ class Clocks:
 class Stack:
     """The 16-layer MoE stack of config 1 with every record resident on the device."""
 
-    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0, ep: bool = False, exchange: str = "p2p"):
+    def __init__(self, cfg: dict, dev: torch.device, seed: int = 0, ep: bool = False, exchange: str = "p2p",
+                 shared_mode: str = "fused"):
         import moeb200
         from moeb200 import format as F
         from moeb200 import ops
@@ -182,7 +183,11 @@ class Stack:
         self.act = {"fp16": torch.float16, "bf16": torch.bfloat16}[cfg["act"]]
         self.lays = {p: F.record_layout(p, H, I) for p in cfg["precs"]}
         self.policy = ops.PolicySpec(**cfg["policy"])
-        self.rt = moeb200.B200Runtime(cfg["precs"], self.lays, E, dev, self.policy, layers=range(L))
+        # Qwen3-Next shared expert folded into the routed launches as expert E (one more pair per
+        # token from the router), or run beside them (its own gate / gate-up / down / finalize)
+        self.shared_fused = bool(cfg.get("shared")) and not ep and shared_mode == "fused"
+        self.rt = moeb200.B200Runtime(cfg["precs"], self.lays, E + (1 if self.shared_fused else 0), dev, self.policy,
+                                      layers=range(L))
         # expert parallelism when launched on several ranks: this rank holds only its expert block
         self.ep = None
         self.world = 1
@@ -194,6 +199,11 @@ class Stack:
             self.world = dist.get_world_size()
             self.ep = ExpertParallel(self.rt, exchange=exchange)
         self.e_lo, self.e_hi = (self.ep.e_lo, self.ep.e_hi) if self.ep else (0, E)
+        # expert-parallel runs: rank 0 also keeps layer 0 with ALL experts on one GPU, the reference
+        # the EP layer output is checked against (built from the same seeded draws)
+        self.rt_full0 = None
+        if self.ep is not None and self.ep.rank == 0:
+            self.rt_full0 = moeb200.B200Runtime(cfg["precs"], self.lays, E, dev, self.policy, layers=[0])
         g = torch.Generator(device=dev).manual_seed(seed)
         self.wr = []
         if cfg.get("bias") == "zipf":  # log(rank^-1.1) over a seeded permutation of the experts
@@ -203,12 +213,16 @@ class Stack:
         else:
             self.bias = (torch.randn(E, generator=g, device=dev) if cfg.get("bias") else None)
         self.shared = []  # per layer (record, layout, wg) of the shared expert, if the config has one
+        self.wr_ext, self.shared_level = [], []  # fused shared expert: router rows + gate row, its level
         for li in range(L):
             self.wr.append((torch.randn(E, H, generator=g, device=dev) * 0.02).to(self.act))
             lprecs = cfg["layer_precs"][li] if cfg.get("layer_precs") else cfg["precs"]
             for e in range(E):
                 gu = torch.randn(2 * I, H, generator=g, device=dev) * 0.02
                 dn = torch.randn(H, I, generator=g, device=dev) * 0.02
+                if li == 0 and self.rt_full0 is not None:
+                    for p in lprecs:
+                        self.rt_full0.add_record(0, e, p, F.encode_record(self.lays[p], gu, dn))
                 if not self.e_lo <= e < self.e_hi:
                     continue
                 for p in lprecs:
@@ -218,7 +232,15 @@ class Stack:
                 dn = torch.randn(H, I, generator=g, device=dev) * 0.02
                 wg = (torch.randn(H, generator=g, device=dev) * 0.02).to(self.act)
                 lay = self.lays[lprecs[0]]
-                self.shared.append((F.encode_record(lay, gu, dn), lay, F.to_c(lay), wg))
+                rec = F.encode_record(lay, gu, dn)
+                self.shared.append((rec, lay, F.to_c(lay), wg))
+                if self.shared_fused:
+                    slot = cfg["precs"].index(lprecs[0])
+                    self.rt.add_record(li, E, lprecs[0], rec)
+                    self.wr_ext.append(torch.cat([self.wr[li], wg[None, :]]).contiguous())
+                    # the level whose precision slot holds the shared record (moelab/policy.py:188-192)
+                    P = len(cfg["precs"])
+                    self.shared_level.append(slot if P >= 3 else (0 if slot == 0 else 2))
         self.routers = [moeb200.B200Router(w, cfg["k"], cfg["renorm"], self.bias) for w in self.wr]
         if self.ep:
             from moeb200.ep import B200EPExperts
@@ -234,9 +256,10 @@ class Stack:
 
         cfg, dev = self.cfg, self.dev
         L, k, H = cfg["layers"], cfg["k"], cfg["H"]
-        self.bufs = [dict(w=torch.empty(T, k, device=dev), idx=torch.empty(T, k, dtype=torch.int64, device=dev),
-                          level=torch.empty(T, k, dtype=torch.uint8, device=dev),
-                          skip=torch.empty(T, k, dtype=torch.uint8, device=dev)) for _ in range(L)]
+        kk = k + (1 if self.shared_fused else 0)  # the fused shared expert is one more pair per token
+        self.bufs = [dict(w=torch.empty(T, kk, device=dev), idx=torch.empty(T, kk, dtype=torch.int64, device=dev),
+                          level=torch.empty(T, kk, dtype=torch.uint8, device=dev),
+                          skip=torch.empty(T, kk, dtype=torch.uint8, device=dev)) for _ in range(L)]
         self.xs = [torch.empty(T, H, dtype=self.act, device=dev) for _ in range(L + 1)]
         self.outs = [torch.empty(T, H, dtype=self.act, device=dev) for _ in range(L)]
         pols = [self.policy.to_c(li) for li in range(L)]
@@ -244,13 +267,18 @@ class Stack:
         miss = self.rt.miss
 
         ep = self.ep
-        shared = self.shared
+        fused = self.shared_fused
+        shared = [] if fused else self.shared
 
         def step():
             for li in range(L):
                 b = self.bufs[li]
                 x = self.xs[li]
-                ops.router(x, self.wr[li], k, cfg["renorm"], self.bias, pols[li], want_probs=False, out=b)
+                if fused:
+                    ops.router(x, self.wr_ext[li], k, cfg["renorm"], self.bias, pols[li], want_probs=False, out=b,
+                               shared_level=self.shared_level[li])
+                else:
+                    ops.router(x, self.wr[li], k, cfg["renorm"], self.bias, pols[li], want_probs=False, out=b)
                 if ep is not None:
                     ep.run_layer(li, x, b["idx"], b["w"], b["level"], b["skip"], out=self.outs[li])
                 else:
@@ -265,12 +293,13 @@ class Stack:
     def launches_per_step(self) -> int:
         # per layer: router logits, router top-k (+ levels), dispatch (one fused kernel when the
         # layer's pairs fit one 1024-pair block, else count, scan, scatter), gate/up GEMV, down GEMV,
-        # finalize; expert parallel: + pack, unpack, combine, no finalize; shared expert: gate
-        # kernel, gate/up, down, finalize
+        # finalize; expert parallel: + pack, unpack, combine, no finalize; shared expert run beside
+        # the routed ones: gate kernel, gate/up, down, finalize (folded in: no launch of its own)
         T = self.xs[0].shape[0] * self.world
-        disp = 1 if T * self.cfg["k"] <= 1024 else 3
+        kk = self.cfg["k"] + (1 if self.shared_fused else 0)
+        disp = 1 if T * kk <= 1024 else 3
         base = 2 + disp + 2 + (3 if self.ep else 1)
-        return self.cfg["layers"] * (base + (4 if self.shared else 0))
+        return self.cfg["layers"] * (base + (4 if self.shared and not self.shared_fused else 0))
 
     def gathered_routing(self, li: int):
         """idx, level, skip of every rank's tokens for layer li (numpy), outside any timed region."""
@@ -286,6 +315,34 @@ class Stack:
             dist.all_gather_into_tensor(full, t.contiguous())
             outs.append(full.cpu().numpy())
         return outs[0], outs[1], outs[2].astype(bool)
+
+    def ep_layer0_error(self) -> float | None:
+        """Expert-parallel parity of the last device step's layer 0: every rank's input rows, routing
+        and EP output are gathered; rank 0 runs the same tokens and routing through the single-GPU
+        layer over all experts and returns max |EP - single| / max |single| (None on other ranks).
+        The two differ only in the fp32 summation order of the expert contributions."""
+        import torch.distributed as dist
+
+        from moeb200 import ops
+
+        b = self.bufs[0]
+        got = {}
+        for name, t in (("x", self.xs[0]), ("out", self.outs[0]), ("idx", b["idx"]), ("w", b["w"]),
+                        ("level", b["level"]), ("skip", b["skip"])):
+            full = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(full, t.contiguous())
+            got[name] = full
+        err = None
+        if self.rt_full0 is not None:
+            rt = self.rt_full0
+            ref = ops.experts_forward(rt._ctables[0], got["x"], got["idx"], got["w"], got["level"], got["skip"],
+                                      miss=rt.miss)
+            if self.shared:
+                rec, _, lay_c, wg = self.shared[0]
+                ops.shared_expert(lay_c, rec, wg, got["x"], out=ref, add=True)
+            err = float((got["out"].float() - ref.float()).abs().max() / ref.float().abs().max().clamp_min(1e-30))
+        dist.barrier()
+        return err
 
     def e2e_step(self, x_host: torch.Tensor, x_dev: torch.Tensor, y_host: torch.Tensor):
         x_dev.copy_(x_host, non_blocking=True)
@@ -409,7 +466,7 @@ def time_graph(step, K: int, W: int, world: int, flush_l2: bool = False):
 
 
 def path_used() -> int:
-    """Expert path of this thread's last experts_forward call: 1 GEMV, 2 GEMM, 3 fused decode."""
+    """Expert path of this thread's last experts_forward call: 1 GEMV, 2 GEMM, 3 fused decode, 4 warp-streamed GEMV."""
     from moeb200 import _lib
 
     return int(_lib.lib().moeb200_path_used())
@@ -455,7 +512,8 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
     out = {"workload": cfg["name"], "T": T, "layers": L, "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": ms,
            "ms_per_layer": ms / L, "experts_ms": up_ms + dn_ms, "records": rb["records"], "pairs": pairs,
            "layer_precisions": [lp[0] for lp in cfg["layer_precs"]] if cfg.get("layer_precs") else cfg["precs"],
-           "shared_expert": bool(cfg.get("shared")),
+           "shared_expert": ("folded into the routed launches (expert E, one more pair per token)"
+                             if stack.shared_fused else bool(cfg.get("shared"))),
            "l2": "evicted (256 MB write) before every timed replay and every traced call"}
     prefill = T * cfg["k"] >= 16 * cfg["E"]
     if prefill:
@@ -729,6 +787,8 @@ def main():
     rb = stack.routing_bytes()
     miss = int(stack.rt.miss.item())
     del graph
+    # expert-parallel runs: the last replay's layer 0 against the single-GPU layer (outside timing)
+    ep_err = stack.ep_layer0_error() if world > 1 else None
 
     # roofline of the dominant kernel (gate/up GEMV) from CUDA events on its stream
     try:
@@ -836,6 +896,7 @@ def main():
             "clocks": clk,
             "sweep": sweep,
             "missing_pairs": miss,
+            "ep_max_rel_err": ep_err,
             "extra_configs": extra,
             "records_per_step": rb["records"], "pairs_per_step": rb["pairs"],
         }

@@ -95,7 +95,9 @@ int moeb200_num_sms(void);
  * grouped GEMV), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128), 3 = the fused
  * one-launch decode kernel (int4/int8 records with group size 64 or float records of the activation
  * type, H and I multiples of 64 up to 2048, a table with tma_base; refused with
- * MOEB200_ERR_UNSUPPORTED where it does not apply). */
+ * MOEB200_ERR_UNSUPPORTED where it does not apply), 4 = the warp-streamed grouped GEMV (items of at
+ * most 8 pairs; int4/int8 records with group size 64 or float records of the activation type;
+ * H and I multiples of 512; x 16-byte aligned; refused with MOEB200_ERR_UNSUPPORTED otherwise). */
 int moeb200_set_path(int32_t path);
 /* Pairs per grouped-GEMV work item for the following moeb200_experts_forward calls on the calling
  * thread (no reference counterpart): 0 = automatic (16 when T >= 64, else 8), 8 or 16. A larger
@@ -112,7 +114,8 @@ int moeb200_trace_begin(void);
 int moeb200_trace_end(float* up_ms, float* down_ms, int32_t* calls);
 /* Measurement hook (no reference counterpart): the expert-product path the calling thread's last
  * moeb200_experts_forward(_part) call took -- 1 grouped GEMV, 2 tcgen05 GEMM, 3 fused decode kernel
- * (its whole launch is traced as the gate/up phase) -- or 0 before the first call. */
+ * (its whole launch is traced as the gate/up phase), 4 warp-streamed grouped GEMV -- or 0 before
+ * the first call. */
 int moeb200_path_used(void);
 
 /* ---- router --------------------------------------------------------------------------------
@@ -130,6 +133,20 @@ int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act
                    const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
                    void* stream);
 size_t moeb200_router_workspace(int32_t T, int32_t E);
+/* Router with a Qwen3-Next shared expert folded in as one more routed pair per token (no reference
+ * counterpart: transformers runs the shared expert beside the routed ones,
+ * qwen3_next/modeling_qwen3_next.py:789-801, and moelab leaves it there). wr holds E + 1 rows:
+ * the E router rows, then the shared expert's gate row (shared_expert_gate.weight). w, idx and
+ * level / skip are [T, k + 1]: the k routed pairs as moeb200_router gives them, then the pair
+ * (expert E, sigmoid(x . wg) with the logit rounded to the activation dtype, level shared_level,
+ * not skipped). probs stays [T, E]; logits, when given, is [T, E + 1]; size the workspace with
+ * moeb200_router_workspace(T, E + 1). An expert table with E + 1 experts whose expert E holds the
+ * shared MLP's record (at the precision slot shared_level selects) then computes the routed and
+ * shared experts in the same launches. */
+int moeb200_router_shared(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H,
+                          int32_t E, int32_t k, int32_t renorm, int32_t shared_level, float* probs, float* w,
+                          int64_t* idx, float* logits, const moeb200_policy* policy, uint8_t* level, uint8_t* skip,
+                          void* ws, size_t ws_bytes, void* stream);
 
 /* ---- precision levels ----------------------------------------------------------------------
  * Replaces PrecisionPolicy.levels / levels_one (moelab/policy.py:110-137) and the device version
@@ -137,6 +154,14 @@ size_t moeb200_router_workspace(int32_t T, int32_t E);
  * skip [T,k] uint8 (may be NULL). */
 int moeb200_levels(const float* w, int32_t T, int32_t k, const moeb200_policy* policy, uint8_t* level,
                    uint8_t* skip, void* stream);
+
+/* Per-expert precision vote of the reference's multi-token path (PrecisionPolicy.expert_level,
+ * moelab/policy.py:148-154, applied per expert by MoERuntime._decide_general,
+ * moelab/runtime.py:476-488): over the kept pairs of each expert, the expert's level is the most
+ * precise L in {0, 1} asked for by at least hi_vote of them, else 2; level [T,k] is rewritten in
+ * place so that every kept pair carries its expert's level. skip may be NULL. E <= 16384. */
+int moeb200_levels_vote(const int64_t* idx, uint8_t* level, const uint8_t* skip, int32_t T, int32_t k, int32_t E,
+                        double hi_vote, void* stream);
 
 /* ---- dispatch --------------------------------------------------------------------------------
  * Replaces the routing part of MoERuntime._decide_general (moelab/runtime.py:459-492): pairs

@@ -29,7 +29,7 @@ thread_local std::vector<TraceRec> g_trace_pool;
 thread_local size_t g_trace_used = 0;
 
 // Expert-product path of the next calls on this thread: 0 auto, 1 grouped GEMV, 2 tcgen05 GEMM,
-// 3 fused decode kernel.
+// 3 fused decode kernel, 4 warp-streamed grouped GEMV.
 thread_local int g_path = 0;
 thread_local int g_item_tokens = 0;  // GEMV work-item size: 0 = automatic, else 8 or 16
 thread_local int g_last_path = 0;    // path of the thread's last experts_forward call (moeb200_path_used)
@@ -203,7 +203,12 @@ LayoutDev to_dev(const moeb200_layout& L) {
 }
 
 int run_expert_phases(GemvParams& gp, const moeb200_layout* lays, int nlay, int act, int max_items, int n_pairs,
-                      int nt, cudaStream_t s, void* out, int add, bool gemm = false) {
+                      int nt, cudaStream_t s, void* out, int add, bool gemm = false, bool streamed = false) {
+  if (streamed) {
+    CUDA_TRY(launch_ws_phases(gp, lays, nlay, act, max_items, s));
+    if (out) CUDA_TRY(launch_finalize(gp.acc, out, act, (int64_t)gp.T * gp.H, add, s));
+    return MOEB200_OK;
+  }
   if (gemm) {
     const int sms = num_sms_cached();
     const int64_t tiles = (int64_t)max_items * (gp.I / 128);
@@ -385,8 +390,9 @@ int moeb200_last_error(char* buf, size_t n) {
 int moeb200_num_sms(void) { return num_sms_cached(); }
 
 int moeb200_set_path(int32_t path) {
-  if (path < 0 || path > 3)
-    return fail(MOEB200_ERR_INVALID, "set_path: path must be 0 (auto), 1 (GEMV), 2 (GEMM) or 3 (fused decode)");
+  if (path < 0 || path > 4)
+    return fail(MOEB200_ERR_INVALID,
+                "set_path: path must be 0 (auto), 1 (GEMV), 2 (GEMM), 3 (fused decode) or 4 (warp-streamed GEMV)");
   g_path = path;
   return MOEB200_OK;
 }
@@ -431,10 +437,11 @@ size_t moeb200_router_workspace(int32_t T, int32_t E) {
   return c.off;
 }
 
-int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H, int32_t E,
-                   int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, float* logits_out,
-                   const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
-                   void* stream) {
+namespace {
+int router_impl(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H, int32_t E,
+                int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, float* logits_out,
+                const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes, void* stream,
+                int shared_level) {
   if (!h || !wr || !w || !idx) return fail(MOEB200_ERR_INVALID, "router: null pointer");
   if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > 32 || k > E || E > 1024)
     return fail(MOEB200_ERR_INVALID, "router: bad sizes T=%d H=%d E=%d k=%d (k <= 32, E <= 1024)", T, H, E, k);
@@ -442,17 +449,38 @@ int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act
     return fail(MOEB200_ERR_INVALID, "router: activation type must be F16, BF16 or F32");
   if (H % (act_type == MOEB200_F32 ? 4 : 8)) return fail(MOEB200_ERR_UNSUPPORTED, "router: H must be a multiple of 8");
   if (policy && !level) return fail(MOEB200_ERR_INVALID, "router: policy given without a level output");
-  if (ws_bytes < moeb200_router_workspace(T, E)) return fail(MOEB200_ERR_WORKSPACE, "router: workspace too small");
+  const int cols = shared_level >= 0 ? E + 1 : E;  // logit columns
+  if (ws_bytes < moeb200_router_workspace(T, cols)) return fail(MOEB200_ERR_WORKSPACE, "router: workspace too small");
   Carve c(ws);
   WsHeader* hdr = c.take<WsHeader>(1);
   (void)hdr;
-  float* logits = c.take<float>((size_t)T * E);
+  float* logits = c.take<float>((size_t)T * cols);
   if (logits_out) logits = logits_out;
   PolicyDev pd{};
   if (policy) pd = {policy->mode, policy->t1, policy->t_mid, policy->t2, policy->thr};
   CUDA_TRY(launch_router(h, wr, bias, act_type, T, H, E, k, renorm, logits, probs, w, idx, policy ? &pd : nullptr,
-                         level, skip, static_cast<cudaStream_t>(stream)));
+                         level, skip, static_cast<cudaStream_t>(stream), shared_level));
   return MOEB200_OK;
+}
+}  // namespace
+
+int moeb200_router(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H, int32_t E,
+                   int32_t k, int32_t renorm, float* probs, float* w, int64_t* idx, float* logits_out,
+                   const moeb200_policy* policy, uint8_t* level, uint8_t* skip, void* ws, size_t ws_bytes,
+                   void* stream) {
+  return router_impl(h, wr, bias, act_type, T, H, E, k, renorm, probs, w, idx, logits_out, policy, level, skip, ws,
+                     ws_bytes, stream, -1);
+}
+
+int moeb200_router_shared(const void* h, const void* wr, const float* bias, int32_t act_type, int32_t T, int32_t H,
+                          int32_t E, int32_t k, int32_t renorm, int32_t shared_level, float* probs, float* w,
+                          int64_t* idx, float* logits_out, const moeb200_policy* policy, uint8_t* level,
+                          uint8_t* skip, void* ws, size_t ws_bytes, void* stream) {
+  if (shared_level < 0 || shared_level > 2) return fail(MOEB200_ERR_INVALID, "router_shared: shared_level must be 0, 1 or 2");
+  if (k + 1 > 32) return fail(MOEB200_ERR_INVALID, "router_shared: k + 1 must be at most 32");
+  if (E + 1 > 1024) return fail(MOEB200_ERR_INVALID, "router_shared: E + 1 must be at most 1024");
+  return router_impl(h, wr, bias, act_type, T, H, E, k, renorm, probs, w, idx, logits_out, policy, level, skip, ws,
+                     ws_bytes, stream, shared_level);
 }
 
 int moeb200_levels(const float* w, int32_t T, int32_t k, const moeb200_policy* policy, uint8_t* level, uint8_t* skip,
@@ -462,6 +490,17 @@ int moeb200_levels(const float* w, int32_t T, int32_t k, const moeb200_policy* p
   if (policy->mode < 0 || policy->mode > 3) return fail(MOEB200_ERR_INVALID, "levels: unknown mode %d", policy->mode);
   PolicyDev pd{policy->mode, policy->t1, policy->t_mid, policy->t2, policy->thr};
   CUDA_TRY(launch_levels(w, T, k, pd, level, skip, static_cast<cudaStream_t>(stream)));
+  return MOEB200_OK;
+}
+
+int moeb200_levels_vote(const int64_t* idx, uint8_t* level, const uint8_t* skip, int32_t T, int32_t k, int32_t E,
+                        double hi_vote, void* stream) {
+  if (!idx || !level) return fail(MOEB200_ERR_INVALID, "levels_vote: null pointer");
+  if (T <= 0 || k <= 0 || k > 32 || (int64_t)T * k >= (1ll << 30))
+    return fail(MOEB200_ERR_INVALID, "levels_vote: bad sizes T=%d k=%d", T, k);
+  if (E <= 0 || E > 16384) return fail(MOEB200_ERR_INVALID, "levels_vote: E=%d outside [1, 16384]", E);
+  if (!(hi_vote >= 0.0 && hi_vote <= 1.0)) return fail(MOEB200_ERR_INVALID, "levels_vote: hi_vote outside [0, 1]");
+  CUDA_TRY(launch_levels_vote(idx, level, skip, T * k, E, hi_vote, static_cast<cudaStream_t>(stream)));
   return MOEB200_OK;
 }
 
@@ -632,8 +671,15 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   // the fused decode kernel is taken only when asked for (path 3): measured slower than the
   // two-launch grouped GEMV on every decode workload of the build's configs so far
   const bool decode = !gemm && g_path == 3;
-  const int nt = gemm ? 128 : decode ? 8 : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
-  g_last_path = gemm ? 2 : decode ? 3 : 1;
+  // warp-streamed GEMV: items of <= 8 pairs; x rows are staged with 16-byte bulk copies
+  const bool ws_ok = ws_supported(ex->layout, P, act_type, H, I, 8) && reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  if (g_path == 4 && !ws_ok)
+    return fail(MOEB200_ERR_UNSUPPORTED, "warp-streamed GEMV: these record layouts, shapes or the x alignment are "
+                                         "not supported");
+  const bool streamed = !gemm && !decode && g_path == 4;
+  // (the warp-streamed GEMV stages at most min(8, T) activation rows per item)
+  const int nt = gemm ? 128 : decode ? 8 : streamed ? std::min(8, T) : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
+  g_last_path = gemm ? 2 : decode ? 3 : streamed ? 4 : 1;
   // upper bound on items: every key splits into ceil(c / nt) items
   const int64_t max_items = std::min<int64_t>(n, (int64_t)(n + nt - 1) / nt + (int64_t)(e_hi - e_lo) * P);
   DispatchParams dp{};
@@ -725,7 +771,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
   return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, part ? nullptr : out, /*add=*/0,
-                           gemm);
+                           gemm, streamed);
 }
 }  // namespace
 

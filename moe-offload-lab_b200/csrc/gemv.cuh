@@ -124,6 +124,12 @@ bool decode_supported(const moeb200_layout* lays, int nlay, int act_type, int H,
 cudaError_t launch_decode(const DecodeParams& p, const moeb200_layout* lays, int nlay, int act_type, int grid,
                           cudaStream_t s);
 
+// Warp-streamed grouped GEMV (gemv_ws.cu): items of at most 8 pairs; int4 / int8 records with
+// 64-column groups, or float records of the activation type; H and I multiples of 512.
+bool ws_supported(const moeb200_layout* lays, int nlay, int act_type, int H, int I, int max_item_pairs);
+cudaError_t launch_ws_phases(GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int max_items,
+                             cudaStream_t s);
+
 // host launchers (gemv.cu)
 // Plans split-K and the shared-memory geometry of the two GEMV phases, then launches gate/up and
 // down (with trace marks around them). nb: token blocks of 8 per item (1 or 2).

@@ -172,21 +172,64 @@ __global__ void levels_kernel(const float* __restrict__ w, int T, int k, PolicyD
   token_levels(w + (int64_t)t * k, k, pol, level + (int64_t)t * k, skip ? skip + (int64_t)t * k : nullptr);
 }
 
+// ---- per-expert precision vote (moelab/policy.py:148-154, applied per expert by
+// moelab/runtime.py:476-488): over the kept pairs of expert e (n of them), the expert's level is the
+// most precise L in (0, 1) with #(levels <= L) >= (hi_vote - 1e-9) * n (double arithmetic, as the
+// reference's Python), else 2; every kept pair of e then takes that level. One CTA: the three
+// counters of every expert live in shared memory. Pairs with an expert index outside [0, E) keep
+// their level (the dispatch drops them and sets the status word).
+__global__ void __launch_bounds__(1024) levels_vote_kernel(const int64_t* __restrict__ idx, uint8_t* __restrict__ level,
+                                                           const uint8_t* __restrict__ skip, int n, int E,
+                                                           double hi_vote) {
+  extern __shared__ int32_t vc[];  // [E] kept pairs (then the vote), [E] levels <= 0, [E] levels <= 1
+  chain_wait();
+  chain_release();
+  for (int i = threadIdx.x; i < 3 * E; i += blockDim.x) vc[i] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < n; p += blockDim.x) {
+    if (skip && skip[p]) continue;
+    const int64_t e = idx[p];
+    if (e < 0 || e >= E) continue;
+    const int l = level[p];
+    atomicAdd(&vc[e], 1);
+    if (l <= 0) atomicAdd(&vc[E + e], 1);
+    if (l <= 1) atomicAdd(&vc[2 * E + e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const double need = (hi_vote - 1e-9) * (double)vc[e];
+    vc[e] = (double)vc[E + e] >= need ? 0 : (double)vc[2 * E + e] >= need ? 1 : 2;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < n; p += blockDim.x) {
+    if (skip && skip[p]) continue;
+    const int64_t e = idx[p];
+    if (e < 0 || e >= E) continue;
+    level[p] = (uint8_t)vc[e];
+  }
+}
+
 // ---- softmax + top-k: one warp per token ------------------------------------------------------------
 constexpr int kMaxEPerLane = 32;  // E <= 1024
 
+// shared_level >= 0: logits rows hold E + 1 columns, the last one the shared expert's gate logit;
+// every token gets one more pair after its k routed ones: (expert E, sigmoid(gate logit), level
+// shared_level, not skipped), so outputs are [T, k + 1].
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
                                                           const float* __restrict__ bias, int T, int E, int k,
                                                           int renorm, float* __restrict__ probs,
                                                           float* __restrict__ w, int64_t* __restrict__ idx,
                                                           PolicyDev pol, int with_levels,
-                                                          uint8_t* __restrict__ level, uint8_t* __restrict__ skip) {
+                                                          uint8_t* __restrict__ level, uint8_t* __restrict__ skip,
+                                                          int shared_level) {
   chain_wait();
   chain_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
   const int per = (E + 31) / 32;
+  const int ls = shared_level >= 0 ? E + 1 : E;  // logits row stride
+  const int kk = shared_level >= 0 ? k + 1 : k;  // output row stride
   float v[kMaxEPerLane];
   float m = -INFINITY;
 #pragma unroll
@@ -195,7 +238,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     const int e = lane + 32 * i;
     float l = -INFINITY;
     if (e < E) {
-      l = logits[(int64_t)t * E + e];
+      l = logits[(int64_t)t * ls + e];
       if (bias) l = __fadd_rn(l, bias[e]);
     }
     v[i] = l;
@@ -269,15 +312,25 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     wsel = __fdiv_rn(wsel, tot);
   }
   if (lane < k) {
-    w[(int64_t)t * k + lane] = wsel;
-    idx[(int64_t)t * k + lane] = isel;
+    w[(int64_t)t * kk + lane] = wsel;
+    idx[(int64_t)t * kk + lane] = isel;
+  }
+  if (shared_level >= 0 && lane == 0) {
+    // the gate logit is already rounded to the activation dtype (as F.linear returns it)
+    const float gl = logits[(int64_t)t * ls + E];
+    w[(int64_t)t * kk + k] = 1.0f / (1.0f + expf(-gl));
+    idx[(int64_t)t * kk + k] = E;
   }
   if (with_levels) {
     __syncwarp();
     if (lane == 0) {
       float wl[32];
-      for (int j = 0; j < k; ++j) wl[j] = w[(int64_t)t * k + j];
-      token_levels(wl, k, pol, level + (int64_t)t * k, skip ? skip + (int64_t)t * k : nullptr);
+      for (int j = 0; j < k; ++j) wl[j] = w[(int64_t)t * kk + j];
+      token_levels(wl, k, pol, level + (int64_t)t * kk, skip ? skip + (int64_t)t * kk : nullptr);
+      if (shared_level >= 0) {
+        level[(int64_t)t * kk + k] = (uint8_t)shared_level;
+        if (skip) skip[(int64_t)t * kk + k] = 0;
+      }
     }
   }
 }
@@ -630,9 +683,10 @@ __global__ void dispatch_scatter_kernel(DispatchParams p) {
 
 }  // namespace
 
-cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,
-                          int renorm, float* logits, float* probs, float* w, int64_t* idx, const PolicyDev* pol,
-                          uint8_t* level, uint8_t* skip, cudaStream_t s) {
+cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E_route,
+                          int k, int renorm, float* logits, float* probs, float* w, int64_t* idx, const PolicyDev* pol,
+                          uint8_t* level, uint8_t* skip, cudaStream_t s, int shared_level) {
+  const int E = shared_level >= 0 ? E_route + 1 : E_route;  // logit columns (router rows of wr)
   const int tpb = T <= 8 ? T : 8;
   dim3 grid((E + 7) / 8, (T + tpb - 1) / tpb);
   // few (token, expert) logits: one expert x 4 tokens per warp (8 experts per block) keeps every SM
@@ -670,13 +724,21 @@ cudaError_t launch_router(const void* h, const void* wr, const float* bias, int 
   if (e != cudaSuccess) return e;
   PolicyDev pd{};
   if (pol) pd = *pol;
-  return launch_chained(router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, logits, bias, T, E, k, renorm, probs, w,
-                        idx, pd, (int)(pol != nullptr), level, skip);
+  return launch_chained(router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, logits, bias, T, E_route, k, renorm,
+                        probs, w, idx, pd, (int)(pol != nullptr), level, skip, shared_level);
 }
 
 cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, uint8_t* level, uint8_t* skip,
                           cudaStream_t s) {
   return launch_chained(levels_kernel, dim3((T + 127) / 128), dim3(128), 0, s, w, T, k, pol, level, skip);
+}
+
+cudaError_t launch_levels_vote(const int64_t* idx, uint8_t* level, const uint8_t* skip, int n, int E, double hi_vote,
+                               cudaStream_t s) {
+  const size_t sh = (size_t)3 * E * sizeof(int32_t);
+  cudaError_t e = cudaFuncSetAttribute(levels_vote_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh);
+  if (e != cudaSuccess) return e;
+  return launch_chained(levels_vote_kernel, dim3(1), dim3(1024), sh, s, idx, level, skip, n, E, hi_vote);
 }
 
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s) {

@@ -56,11 +56,15 @@ struct DispatchParams {
                           // and the item count, or null
 };
 
+// shared_level >= 0: wr has E + 1 rows (the last one a shared expert's gate) and every token gets a
+// (k + 1)-th pair (expert E, sigmoid of the gate logit, that level); outputs are [T, k + 1].
 cudaError_t launch_router(const void* h, const void* wr, const float* bias, int act_type, int T, int H, int E, int k,
                           int renorm, float* logits, float* probs, float* w, int64_t* idx, const PolicyDev* pol,
-                          uint8_t* level, uint8_t* skip, cudaStream_t s);
+                          uint8_t* level, uint8_t* skip, cudaStream_t s, int shared_level = -1);
 cudaError_t launch_levels(const float* w, int T, int k, const PolicyDev& pol, uint8_t* level, uint8_t* skip,
                           cudaStream_t s);
+cudaError_t launch_levels_vote(const int64_t* idx, uint8_t* level, const uint8_t* skip, int n, int E, double hi_vote,
+                               cudaStream_t s);
 cudaError_t launch_dispatch(const DispatchParams& p, cudaStream_t s);
 
 }  // namespace moeb200

@@ -58,6 +58,9 @@ _SIGS = {
     "moeb200_router": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                  _P, _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
     "moeb200_set_path": (C.c_int, [C.c_int32]),
+    "moeb200_router_shared": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                        C.c_int32, _P, _P, _P, _P, C.POINTER(Policy), _P, _P, _P, C.c_size_t, _P]),
+    "moeb200_levels_vote": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_double, _P]),
     "moeb200_set_item_tokens": (C.c_int, [C.c_int32]),
     "moeb200_router_workspace": (C.c_size_t, [C.c_int32, C.c_int32]),
     "moeb200_levels": (C.c_int, [_P, C.c_int32, C.c_int32, C.POINTER(Policy), _P, _P, _P]),

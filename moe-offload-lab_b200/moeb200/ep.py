@@ -96,6 +96,11 @@ class CudaOps:
 
         return ops.combine_parts(parts, out, add)
 
+    def vote(self, idx, level, skip, num_experts, hi_vote):
+        from . import ops
+
+        return ops.levels_vote(idx, level, skip, num_experts, hi_vote)
+
 
 @dataclass
 class _Bufs:
@@ -243,26 +248,32 @@ class ExpertParallel:
         idx = idx.contiguous()
         k = idx.shape[1]
         w = top_k_weights.reshape(T, k).float().contiguous()
+        votes = hasattr(self.runtime, "votes") and self.runtime.votes(layer)
         if level is None and skip is None:
-            level, skip = self.runtime.levels(layer, w)
+            # per-pair levels here; a per-expert vote is taken over every rank's tokens after the gather
+            level, skip = self.runtime.levels(layer, w, vote=False) if votes else self.runtime.levels(layer, w)
+        elif votes and level is None:
+            votes = False  # no levels to vote on
         if self.failed is not None:
             raise PeerFailure(f"the exchange group failed earlier ({self.failed})")
         b = self._buffers(T, H, k, x2.dtype, x2.device)
         if out is None:
             out = torch.empty_like(x2)
         if self.exchange == "p2p":
-            self._run_p2p(layer, x2, idx, w, level, skip, b, out.view(T, H))
+            self._run_p2p(layer, x2, idx, w, level, skip, b, out.view(T, H), votes)
             return out.view_as(x)
         self.ops.pack(x2, idx, w, level, skip, b.rows)
         self._collective("dispatch all_gather", dist.all_gather_into_tensor, b.rows_all, b.rows)
         self.ops.unpack(b.rows_all, H, k, x2.dtype, b.x_all, b.idx_all, b.w_all, b.level_all, b.skip_all)
+        if votes and self.world * T > 1:
+            self.ops.vote(b.idx_all, b.level_all, b.skip_all, self.runtime.num_experts, self.runtime.policy.hi_vote)
         self.ops.local(self.runtime, layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all,
                        b.skip_all, b.part)
         self._collective("combine all_to_all", dist.all_to_all_single, b.recv, b.part)
         self.ops.combine(b.recv.view(self.world, T, H), out.view(T, H))
         return out.view_as(x)
 
-    def _run_p2p(self, layer, x2, idx, w, level, skip, b: _Bufs, out) -> None:
+    def _run_p2p(self, layer, x2, idx, w, level, skip, b: _Bufs, out, votes: bool = False) -> None:
         from . import _lib
         from . import ops as O
 
@@ -282,6 +293,8 @@ class ExpertParallel:
         _lib.check(L.moeb200_ep_signal(g, 0, st))
         _lib.check(L.moeb200_ep_gather(g, act, O._ptr(b.x_all), O._ptr(b.idx_all), O._ptr(b.w_all),
                                        O._ptr(b.level_all), O._ptr(b.skip_all), st))
+        if votes and self.world * T > 1:
+            O.levels_vote(b.idx_all, b.level_all, b.skip_all, self.runtime.num_experts, self.runtime.policy.hi_vote)
         rt = self.runtime
         rt._table(layer)
         n = self.world * T

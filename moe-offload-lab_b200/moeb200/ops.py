@@ -77,6 +77,9 @@ class PolicySpec:
     t2: float | None = None
     thr: float = 0.1
     protect_layers: frozenset = frozenset()
+    # per-expert vote of the reference's multi-token path (moelab/policy.py:148-154; its default
+    # hi_vote is 0.5): None = every pair keeps its own level
+    hi_vote: float | None = None
 
     def to_c(self, layer: int | None = None) -> _lib.Policy:
         mode = self.mode
@@ -93,12 +96,18 @@ class PolicySpec:
 
 def router(h: torch.Tensor, wr: torch.Tensor, k: int, renorm: bool, bias: torch.Tensor | None = None,
            policy: _lib.Policy | None = None, want_probs: bool = True, out: dict | None = None,
-           logits: torch.Tensor | None = None):
+           logits: torch.Tensor | None = None, shared_level: int | None = None):
     """Fused router: (probs [T,E] f32 | None, w [T,k] f32, idx [T,k] i64, level [T,k] u8 | None,
-    skip [T,k] u8 | None)."""
+    skip [T,k] u8 | None).
+
+    shared_level (Qwen3-Next shared expert folded in): wr holds E + 1 rows, the last one the shared
+    expert's gate; w / idx / level / skip gain a (k+1)-th column per token = (expert E,
+    sigmoid(x . wg), shared_level, not skipped)."""
     _need_cuda(h, wr, bias)
     T, H = h.shape
-    E = wr.shape[0]
+    sh = shared_level is not None
+    E = wr.shape[0] - (1 if sh else 0)
+    kk = k + (1 if sh else 0)
     dev = h.device
     o = out or {}
     probs = o.get("probs") if want_probs else None
@@ -106,25 +115,34 @@ def router(h: torch.Tensor, wr: torch.Tensor, k: int, renorm: bool, bias: torch.
         probs = torch.empty(T, E, dtype=torch.float32, device=dev)
     w = o.get("w")
     if w is None:
-        w = torch.empty(T, k, dtype=torch.float32, device=dev)
+        w = torch.empty(T, kk, dtype=torch.float32, device=dev)
     idx = o.get("idx")
     if idx is None:
-        idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+        idx = torch.empty(T, kk, dtype=torch.int64, device=dev)
     level = skip = None
     if policy is not None:
         level = o.get("level")
         if level is None:
-            level = torch.empty(T, k, dtype=torch.uint8, device=dev)
+            level = torch.empty(T, kk, dtype=torch.uint8, device=dev)
         skip = o.get("skip")
         if skip is None:
-            skip = torch.empty(T, k, dtype=torch.uint8, device=dev)
+            skip = torch.empty(T, kk, dtype=torch.uint8, device=dev)
+    for name, t in (("w", w), ("idx", idx), ("level", level), ("skip", skip)):
+        if t is not None and (tuple(t.shape) != (T, kk) or not t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous [{T}, {kk}] tensor")
     L = _lib.lib()
-    nbytes = L.moeb200_router_workspace(T, E)
+    nbytes = L.moeb200_router_workspace(T, E + (1 if sh else 0))
     ws = workspace(nbytes, dev, slot=1)
-    _lib.check(L.moeb200_router(_ptr(h), _ptr(wr), _ptr(bias), _act(h.dtype), T, H, E, k, int(bool(renorm)),
-                                _ptr(probs), _ptr(w), _ptr(idx), _ptr(logits),
-                                C.byref(policy) if policy is not None else None,
-                                _ptr(level), _ptr(skip), _ptr(ws), ws.numel(), _stream(dev)))
+    pol = C.byref(policy) if policy is not None else None
+    if sh:
+        _lib.check(L.moeb200_router_shared(_ptr(h), _ptr(wr), _ptr(bias), _act(h.dtype), T, H, E, k,
+                                           int(bool(renorm)), int(shared_level), _ptr(probs), _ptr(w), _ptr(idx),
+                                           _ptr(logits), pol, _ptr(level), _ptr(skip), _ptr(ws), ws.numel(),
+                                           _stream(dev)))
+    else:
+        _lib.check(L.moeb200_router(_ptr(h), _ptr(wr), _ptr(bias), _act(h.dtype), T, H, E, k, int(bool(renorm)),
+                                    _ptr(probs), _ptr(w), _ptr(idx), _ptr(logits), pol,
+                                    _ptr(level), _ptr(skip), _ptr(ws), ws.numel(), _stream(dev)))
     return probs, w, idx, level, skip
 
 
@@ -139,6 +157,17 @@ def levels(w: torch.Tensor, policy: _lib.Policy, level: torch.Tensor | None = No
     _lib.check(_lib.lib().moeb200_levels(_ptr(w), T, k, C.byref(policy), _ptr(level), _ptr(skip),
                                          _stream(w.device)))
     return level, skip
+
+
+def levels_vote(idx: torch.Tensor, level: torch.Tensor, skip: torch.Tensor | None, E: int, hi_vote: float) -> torch.Tensor:
+    """Rewrite level [T,k] in place with each expert's vote over its kept pairs (moelab/policy.py:148-154)."""
+    _need_cuda(idx, level, skip)
+    T, k = idx.shape
+    if idx.dtype != torch.int64 or level.dtype != torch.uint8 or not (idx.is_contiguous() and level.is_contiguous()):
+        raise ValueError("idx must be contiguous int64 and level contiguous uint8")
+    _lib.check(_lib.lib().moeb200_levels_vote(_ptr(idx), _ptr(level), _ptr(skip), T, k, E, float(hi_vote),
+                                              _stream(idx.device)))
+    return level
 
 
 def dispatch(idx: torch.Tensor, level: torch.Tensor | None, skip: torch.Tensor | None, E: int, P: int):
@@ -284,9 +313,9 @@ def shared_expert(layout_c: _lib.Layout, record: torch.Tensor, wg: torch.Tensor,
 
 
 def set_path(path: str) -> None:
-    """Expert-product path for this thread's next experts_forward calls: "auto", "gemv", "gemm" or "decode"
-    (the fused one-launch decode kernel)."""
-    _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2, "decode": 3}[path]))
+    """Expert-product path for this thread's next experts_forward calls: "auto", "gemv", "gemm", "decode"
+    (the fused one-launch decode kernel) or "ws" (the warp-streamed grouped GEMV)."""
+    _lib.check(_lib.lib().moeb200_set_path({"auto": 0, "gemv": 1, "gemm": 2, "decode": 3, "ws": 4}[path]))
 
 
 def set_item_tokens(nt: int) -> None:

@@ -131,16 +131,35 @@ class B200Runtime:
         self._records[(layer, expert, prec)] = blob
         self._table(layer)[p, expert] = blob.data_ptr()
 
+    def record(self, layer: int, expert: int, prec: str) -> torch.Tensor:
+        """The resident record blob of (layer, expert, precision)."""
+        return self._records[(layer, expert, prec)]
+
     def remove_record(self, layer: int, expert: int, prec: str) -> None:
         p = self.precisions.index(prec)
         self._records.pop((layer, expert, prec), None)
         self._table(layer)[p, expert] = 0
 
-    def levels(self, layer: int, top_k_weights: torch.Tensor):
+    def votes(self, layer: int) -> bool:
+        """Whether this layer's levels go through the per-expert vote (policy.hi_vote set, a rule that
+        depends on the router weights, layer not protected)."""
+        pol = self.policy
+        return pol.hi_vote is not None and pol.mode not in ("hi", "lo") and layer not in pol.protect_layers
+
+    def levels(self, layer: int, top_k_weights: torch.Tensor, top_k_index: torch.Tensor | None = None,
+               vote: bool = True):
+        """(level, skip) [T,k] of the policy; with ``policy.hi_vote`` set and more than one token, every
+        kept pair takes its expert's vote (moelab/runtime.py:476-488), which needs top_k_index
+        (vote=False: per-pair levels only, for callers that vote over more tokens themselves)."""
         pol = self.policy
         if pol.mode == "hi" and not pol.protect_layers:
             return None, None
-        return ops.levels(top_k_weights.float().contiguous(), pol.to_c(layer))
+        level, skip = ops.levels(top_k_weights.float().contiguous(), pol.to_c(layer))
+        if vote and self.votes(layer) and top_k_weights.shape[0] > 1:
+            if top_k_index is None:
+                raise ValueError("the per-expert vote needs the routed expert indices")
+            ops.levels_vote(top_k_index.long().contiguous(), level, skip, self.num_experts, pol.hi_vote)
+        return level, skip
 
     @torch.no_grad()
     def run_layer(self, layer: int, x: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
@@ -151,7 +170,8 @@ class B200Runtime:
         if act_fn is not None:
             require_silu(act_fn)
         if level is None and skip is None:
-            level, skip = self.levels(layer, top_k_weights)
+            level, skip = self.levels(layer, top_k_weights.reshape(-1, top_k_index.shape[-1]),
+                                      top_k_index.reshape(-1, top_k_index.shape[-1]))
         self._table(layer)
         x2 = x.reshape(-1, x.shape[-1])
         idx = top_k_index.reshape(x2.shape[0], -1)
@@ -212,6 +232,51 @@ class B200Router(nn.Module):
         return probs, w, idx
 
 
+class B200MoeBlock(nn.Module):
+    """A whole Qwen3-Next sparse MoE block (transformers qwen3_next/modeling_qwen3_next.py:783-801:
+    router, routed experts, sigmoid-gated shared expert) on the B200 kernels, with the shared expert
+    folded into the routed launches: the router gives every token one more pair (expert E,
+    sigmoid(x . shared_expert_gate)), and expert E of the runtime's table holds the shared MLP's
+    record. No moelab counterpart: moelab leaves the shared expert to transformers."""
+
+    def __init__(self, runtime: "B200Runtime", layer: int, router_weight: torch.Tensor, shared_gate: torch.Tensor,
+                 top_k: int, norm_topk_prob: bool, shared_level: int = 0):
+        super().__init__()
+        self.runtime = runtime
+        self.layer = layer
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.num_experts, self.hidden_dim = router_weight.shape
+        self.shared_level = shared_level
+        w = torch.cat([router_weight.detach(), shared_gate.detach().reshape(1, -1).to(router_weight.dtype)])
+        self.register_buffer("router_ext", w.contiguous())
+
+    @torch.no_grad()
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        shape = hidden_states.shape
+        h = hidden_states.reshape(-1, self.hidden_dim).contiguous()
+        rt = self.runtime
+        wr = self.router_ext if self.router_ext.dtype == h.dtype else self.router_ext.to(h.dtype)
+        pol = rt.policy
+        want_levels = not (pol.mode == "hi" and not pol.protect_layers)
+        _, w, idx, level, skip = ops.router(h, wr, self.top_k, self.norm_topk_prob, None,
+                                            pol.to_c(self.layer) if want_levels else None, want_probs=False,
+                                            shared_level=self.shared_level)
+        if want_levels and rt.votes(self.layer) and h.shape[0] > 1:
+            ops.levels_vote(idx, level, skip, self.num_experts + 1, pol.hi_vote)
+        hook = rt.capture_hook
+        if hook is not None:
+            out = hook(self, h, idx, w)
+        else:
+            rt._table(self.layer)
+            out = ops.experts_forward(rt._ctables[self.layer], h, idx, w, level, skip, miss=rt.miss)
+        return out.reshape(shape)
+
+    def extra_repr(self) -> str:
+        return (f"moe_layer={self.layer}, experts={self.num_experts} + shared (folded), "
+                f"precisions={self.runtime.precisions}")
+
+
 def iter_moe_blocks(model: nn.Module):
     """(layer index, MoE block) for blocks holding 3-D experts and a router `gate` (as
     moelab/loader.py:53-65 finds them)."""
@@ -224,10 +289,26 @@ def iter_moe_blocks(model: nn.Module):
             li += 1
 
 
+def _shared_mlp(blk: nn.Module, inter: int):
+    """(gate_up [2I, H], down [H, I]) of a block's shared expert when it can be folded (a SwiGLU MLP
+    with the routed experts' intermediate size and a one-row sigmoid gate), else None."""
+    se, sg = getattr(blk, "shared_expert", None), getattr(blk, "shared_expert_gate", None)
+    if se is None or sg is None or not all(hasattr(se, n) for n in ("gate_proj", "up_proj", "down_proj")):
+        return None
+    if se.gate_proj.weight.shape[0] != inter or sg.weight.shape[0] != 1:
+        return None
+    require_silu(se.act_fn)
+    return torch.cat([se.gate_proj.weight, se.up_proj.weight]), se.down_proj.weight
+
+
 def install(model: nn.Module, precisions: list[str], policy: PolicySpec | None = None, group_size: int = 64,
-            device=None, swap_router: bool = True) -> B200Runtime:
+            device=None, swap_router: bool = True, fold_shared: bool = False) -> B200Runtime:
     """Quantise every MoE block's experts into moelab records on the device, make them resident,
-    and swap ``experts`` (and optionally ``gate``) for the B200 modules (moelab/loader.py:211-223)."""
+    and swap ``experts`` (and optionally ``gate``) for the B200 modules (moelab/loader.py:211-223).
+
+    fold_shared: blocks with a Qwen3-Next shared expert of the routed experts' size are replaced
+    whole by B200MoeBlock, the shared MLP quantised like the routed experts (every precision) and
+    held as expert E; its pair always takes the most precise record (level 0)."""
     blocks = list(iter_moe_blocks(model))
     if not blocks:
         raise ValueError("no MoE block with 3-D experts found")
@@ -235,10 +316,14 @@ def install(model: nn.Module, precisions: list[str], policy: PolicySpec | None =
     E, two_i, H = ex0.gate_up_proj.shape
     I = two_i // 2
     dev = torch.device(device) if device is not None else ex0.gate_up_proj.device
+    fold = fold_shared and all(_shared_mlp(b, I) is not None for _, b in blocks)
+    if fold_shared and not fold:
+        raise ValueError("fold_shared: a block has no shared expert of the routed experts' size to fold")
     lays = {p: record_layout(p, H, I, group_size) for p in precisions}
-    rt = B200Runtime(precisions, lays, E, dev, policy, layers=range(len(blocks)))
+    rt = B200Runtime(precisions, lays, E + (1 if fold else 0), dev, policy, layers=range(len(blocks)))
     from .format import encode_record
 
+    parents = {id(m): (parent, name) for parent in model.modules() for name, m in parent.named_children()}
     for li, blk in blocks:
         ex = blk.experts
         require_silu(ex.act_fn)
@@ -247,6 +332,16 @@ def install(model: nn.Module, precisions: list[str], policy: PolicySpec | None =
             dn = ex.down_proj[e].detach().to(dev, torch.float32)
             for p in precisions:
                 rt.add_record(li, e, p, encode_record(lays[p], gu, dn))
+        if fold:
+            gu, dn = _shared_mlp(blk, I)
+            for p in precisions:
+                rt.add_record(li, E, p, encode_record(lays[p], gu.detach().to(dev, torch.float32),
+                                                      dn.detach().to(dev, torch.float32)))
+            new = B200MoeBlock(rt, li, blk.gate.weight.to(dev), blk.shared_expert_gate.weight.to(dev), blk.gate.top_k,
+                               bool(getattr(blk.gate, "norm_topk_prob", False)))
+            parent, name = parents[id(blk)]
+            setattr(parent, name, new)
+            continue
         blk.experts = B200Experts(rt, li, ex.act_fn, E)
         if swap_router:
             blk.gate = B200Router.from_module(blk.gate).to(dev)

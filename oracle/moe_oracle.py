@@ -374,6 +374,33 @@ def threshold_levels(w: np.ndarray, thr: float):
     return np.where(w >= np.float32(thr), 0, 2).astype(np.uint8), np.zeros(w.shape, bool)
 
 
+def expert_vote(idx: np.ndarray, level: np.ndarray, skip: np.ndarray | None, E: int, hi_vote: float = 0.5):
+    """Per-expert precision vote of the reference's T > 1 path (moelab/policy.py:148-154
+    `expert_level`, applied per expert in moelab/runtime.py:476-488 `_decide_general`).
+
+    Over the kept (not skipped) pairs of expert e (n of them), the expert's level is the most
+    precise level L in (0, 1) with #(pair levels <= L) >= (hi_vote - 1e-9) * n, else 2; the
+    comparison is the reference's Python (double) arithmetic. Returns (vote [E] int8, -1 where the
+    expert has no kept pair; levels [T, k] uint8 with every kept pair set to its expert's vote,
+    skipped pairs unchanged)."""
+    e = np.asarray(idx, np.int64).reshape(-1)
+    lv = np.asarray(level, np.int64).reshape(-1)
+    keep = np.ones(e.shape, bool) if skip is None else ~np.asarray(skip, bool).reshape(-1)
+    vote = np.full(E, -1, np.int8)
+    for x in np.unique(e[keep]):
+        sel = lv[keep & (e == x)]
+        n = sel.size
+        v = 2
+        for L in (0, 1):
+            if int((sel <= L).sum()) >= (float(hi_vote) - 1e-9) * n:
+                v = L
+                break
+        vote[x] = v
+    out = lv.copy()
+    out[keep] = vote[e[keep]]
+    return vote, out.reshape(np.asarray(level).shape).astype(np.uint8)
+
+
 def level_to_slot(level: int, n_prec: int) -> int:
     """Level -> index into the store's precision list, most precise first (moelab/policy.py:188-192)."""
     if n_prec >= 3:

@@ -91,6 +91,12 @@ class CpuOps:
         part.copy_(torch.from_numpy(y))
         return part
 
+    def vote(self, idx, level, skip, num_experts, hi_vote):
+        _, lv = O.expert_vote(idx.numpy(), level.numpy(), None if skip is None else skip.numpy().astype(bool),
+                              num_experts, hi_vote)
+        level.copy_(torch.from_numpy(lv))
+        return level
+
     def combine(self, parts, out, add=False):
         acc = torch.zeros(parts.shape[1:], dtype=torch.float32)
         for g in range(parts.shape[0]):

@@ -52,7 +52,7 @@ def _tokens(rank: int, wr):
     return x, idx.astype(np.int64), w.astype(np.float32), level.astype(np.uint8), skip.astype(np.uint8)
 
 
-def _worker(rank: int, world: int, port: int, q):
+def _worker(rank: int, world: int, port: int, q, vote: bool = False):
     sys.path[:0] = [str(ROOT), str(ROOT / "moe-offload-lab_b200")]
     import torch.distributed as dist
 
@@ -66,11 +66,27 @@ def _worker(rank: int, world: int, port: int, q):
         lo, hi = ep.partition(E, world, rank)
         own = [[r if lo <= e < hi else None for e, r in enumerate(rs)] for rs in recs]
         rt = ep_util.CpuRuntime(E, lays, own, 2)
+        if vote:  # the per-expert vote, taken over every rank's tokens after the gather
+            from types import SimpleNamespace
+
+            rt.policy = SimpleNamespace(hi_vote=0.5)
+            rt.votes = lambda layer: True
         par = ep.ExpertParallel(rt, ops=ep_util.CpuOps())
         x, idx, w, level, skip = _tokens(rank, wr)
+        if vote:  # three per-pair levels to vote on
+            level = O.hobbit_levels(w, t1=0.4, t_mid=0.7)[0].astype(np.uint8)
         xt = torch.from_numpy(x).half()
         out = par.run_layer(0, xt, torch.from_numpy(idx), torch.from_numpy(w), torch.from_numpy(level),
                             torch.from_numpy(skip))
+        if vote:
+            allt = [_tokens(r, wr) for r in range(world)]
+            all_idx = np.concatenate([a[1] for a in allt])
+            all_lvl = np.concatenate([O.hobbit_levels(a[2], t1=0.4, t_mid=0.7)[0] for a in allt]).astype(np.uint8)
+            all_skip = np.concatenate([a[4] for a in allt]).astype(bool)
+            cat = [all_idx, all_lvl]
+            _, lv_all = O.expert_vote(all_idx, all_lvl, all_skip, E, 0.5)
+            assert not np.array_equal(lv_all, cat[1])  # the vote moves some pairs
+            level = lv_all[rank * T:(rank + 1) * T]
         slot = np.vectorize(lambda v: O.level_to_slot(int(v), 2))(level.astype(np.int64))
         ref = O.moe_layer(x, idx, w, slot, skip.astype(bool), recs, lays, E)
         err = O.max_rel_err(out.float().numpy(), ref)
@@ -80,12 +96,12 @@ def _worker(rank: int, world: int, port: int, q):
         q.put((rank, None, None, repr(exc)))
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_ep_gloo_matches_single_process(world):
+@pytest.mark.parametrize("world,vote", [(2, False), (3, False), (2, True)])
+def test_ep_gloo_matches_single_process(world, vote):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, vote)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}

@@ -30,7 +30,7 @@ from gpu_util import TOL, act_np, layer_records
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("path", ["gemv", "gemm", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "gemm", "decode", "ws"])
 def test_out_of_range_expert_sets_status_and_is_dropped(cuda_dev, path):
     H, I, E, k, T = 2048, 512, 16, 4, 6
     lays, recs = layer_records(["int4"], H, I, E, seed=12, device=cuda_dev, std=0.02)
@@ -51,8 +51,8 @@ def test_out_of_range_expert_sets_status_and_is_dropped(cuda_dev, path):
     try:
         out = ops.experts_forward(table, x, idx, wv, level, skip, miss=rt.miss, ws=ws)
     except _lib.MoeB200Error as exc:
-        if path == "decode" and exc.code == _lib.ERR_UNSUPPORTED:
-            pytest.skip("layout not taken by the fused decode kernel")
+        if path in ("decode", "ws") and exc.code == _lib.ERR_UNSUPPORTED:
+            pytest.skip(f"layout not taken by the {path} path")
         raise
     finally:
         ops.set_path("auto")

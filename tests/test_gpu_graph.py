@@ -97,7 +97,7 @@ def _capture(step):
     return g
 
 
-@pytest.mark.parametrize("path", ["gemv", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "decode", "ws"])
 @pytest.mark.parametrize("T", [1, 64])
 def test_captured_step_replays_match_oracle(cuda_dev, path, T):
     ops.set_path(path)
@@ -116,7 +116,7 @@ def test_captured_step_replays_match_oracle(cuda_dev, path, T):
         ops.set_path("auto")
 
 
-@pytest.mark.parametrize("path", ["gemv", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "decode", "ws"])
 def test_graph_survives_workspace_growth(cuda_dev, path):
     # capture at T=8, grow the cached workspaces with an eager T=64 layer, replay the T=8 graph
     ops.set_path(path)

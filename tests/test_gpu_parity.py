@@ -180,6 +180,58 @@ def test_dispatch_matches_reference_decide_general(cuda_dev, golden, golden_meta
         assert np.array_equal(d["pos_e"].cpu().numpy()[:n] // m["k"], golden[f"dsp/{case}/tok"])
 
 
+@pytest.mark.parametrize("T,k,E", [(1, 8, 64), (37, 4, 16), (256, 10, 512), (2048, 8, 128)])
+def test_levels_vote_matches_oracle(cuda_dev, T, k, E):
+    g = np.random.default_rng(T * 7 + E)
+    idx = np.stack([g.choice(E, k, replace=False) for _ in range(T)]).astype(np.int64)
+    lvl = g.integers(0, 3, (T, k)).astype(np.uint8)
+    skip = g.random((T, k)) < 0.1
+    for hv in (0.5, 0.3, 1.0):
+        _, ref = O.expert_vote(idx, lvl, skip, E, hv)
+        level = torch.from_numpy(lvl.copy()).to(cuda_dev)
+        ops.levels_vote(torch.from_numpy(idx).to(cuda_dev), level, torch.from_numpy(skip.astype(np.uint8)).to(cuda_dev),
+                        E, hv)
+        assert np.array_equal(level.cpu().numpy(), ref), hv
+
+
+def test_levels_vote_matches_reference_goldens(cuda_dev, golden, golden_meta):
+    for case in ("d1", "d2", "d3"):
+        m = golden_meta["cases"][f"dsp/{case}"]
+        idx, skip, lvl = golden[f"dsp/{case}/idx"], golden[f"dsp/{case}/skip"], golden[f"dsp/{case}/lvl"]
+        level = torch.from_numpy(lvl.astype(np.uint8)).to(cuda_dev)
+        ops.levels_vote(torch.from_numpy(idx).to(cuda_dev), level, torch.from_numpy(skip.astype(np.uint8)).to(cuda_dev),
+                        m["E"], 0.5)
+        got = level.cpu().numpy()
+        experts = golden[f"dsp/{case}/experts"]
+        keep = ~skip.astype(bool)
+        for e, prec in zip(experts, golden[f"dsp/{case}/vote_prec"]):
+            sel = keep & (idx == e)
+            assert set(O.level_to_slot(int(v), 3) for v in got[sel]) == {int(prec)}, (case, e)
+
+
+def test_layer_with_per_expert_vote_matches_oracle(cuda_dev):
+    H, I, E, k, T = 2048, 512, 32, 8, 48
+    precs = ["fp16", "int8", "int4"]
+    lays, recs = layer_records(precs, H, I, E, seed=41, device=cuda_dev, std=0.02)
+    pol = ops.PolicySpec("hobbit", t1=0.5, t_mid=0.8, hi_vote=0.5)
+    rt = B200Runtime(precs, lays, E, cuda_dev, pol, layers=[0])
+    for p in precs:
+        for e in range(E):
+            rt.add_record(0, e, p, recs[p][e])
+    g = torch.Generator(device=cuda_dev).manual_seed(8)
+    x = torch.randn(T, H, generator=g, device=cuda_dev).half()
+    wv, idx = torch.topk(torch.randn(T, E, generator=g, device=cuda_dev).softmax(-1), k, dim=-1)
+    out = rt.run_layer(0, x, idx, wv, torch.nn.SiLU())
+    lv0, sk0 = O.hobbit_levels(wv.cpu().numpy(), t1=0.5, t_mid=0.8)
+    _, lv = O.expert_vote(idx.cpu().numpy(), lv0, sk0, E, 0.5)
+    slot = np.vectorize(lambda v: O.level_to_slot(int(v), 3))(lv.astype(np.int64))
+    recs_np = [[b.cpu().numpy() for b in recs[p]] for p in precs]
+    ref = O.moe_layer(act_np(x), idx.cpu().numpy(), wv.cpu().numpy(), slot, sk0, recs_np, [lays[p] for p in precs], E)
+    assert O.max_rel_err(act_np(out), ref) < TOL
+    # the vote changed some pairs' precision (otherwise this test proves nothing)
+    assert not np.array_equal(lv, lv0)
+
+
 # -- the experts module: whole MoE layer ------------------------------------------------------------------------
 LAYER_CASES = [
     # (name, H, I, E, k, T, precs, policy, act)
@@ -200,14 +252,14 @@ def _run_on_path(path, fn):
     try:
         return fn()
     except _lib.MoeB200Error as exc:
-        if path == "decode" and exc.code == _lib.ERR_UNSUPPORTED:
-            pytest.skip("layout not taken by the fused decode kernel")
+        if path in ("decode", "ws") and exc.code == _lib.ERR_UNSUPPORTED:
+            pytest.skip(f"layout not taken by the {path} path")
         raise
     finally:
         ops.set_path("auto")
 
 
-@pytest.mark.parametrize("path", ["gemv", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "decode", "ws"])
 @pytest.mark.parametrize("case", LAYER_CASES, ids=[c[0] for c in LAYER_CASES])
 def test_experts_forward_matches_oracle(cuda_dev, case, path):
     name, H, I, E, k, T, precs, pol, act = case
@@ -234,7 +286,7 @@ def test_experts_forward_matches_oracle(cuda_dev, case, path):
     assert int(rt.miss.item()) == 0
 
 
-@pytest.mark.parametrize("path", ["gemv", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "decode", "ws"])
 def test_calls_in_a_row_reuse_the_workspace(cuda_dev, path):
     # The GEMV job counters and the split-K arrival counters (decode kernel: unit claims, per-item
     # and per-row-block counters) live in the workspace and are zeroed by the kernel that writes each
@@ -286,7 +338,7 @@ def test_missing_expert_counted_and_skipped(cuda_dev):
     assert O.max_rel_err(act_np(out), ref) < TOL
 
 
-@pytest.mark.parametrize("path", ["gemv", "decode"])
+@pytest.mark.parametrize("path", ["gemv", "decode", "ws"])
 def test_every_pair_skipped_gives_zero_output(cuda_dev, path):
     # no work item at all: the output must still be written (zeros), on every path
     H, I, E, k, T = 2048, 512, 16, 4, 3

@@ -154,6 +154,35 @@ def test_dispatch_matches_reference_decide_general(golden, golden_meta, case):
     assert np.array_equal(w[d["pos_e"]], golden[f"dsp/{case}/w_sorted"])
 
 
+@pytest.mark.parametrize("case", ["d1", "d2", "d3"])
+def test_expert_vote_matches_reference_decide_general(golden, golden_meta, case):
+    # the reference votes one precision per expert (hi_vote 0.5) over its 3-precision store
+    m = golden_meta["cases"][f"dsp/{case}"]
+    idx, skip, lvl = golden[f"dsp/{case}/idx"], golden[f"dsp/{case}/skip"], golden[f"dsp/{case}/lvl"]
+    vote, per_pair = O.expert_vote(idx, lvl, skip, m["E"], 0.5)
+    experts = golden[f"dsp/{case}/experts"]
+    assert np.array_equal(np.nonzero(vote >= 0)[0], experts)
+    got = [O.level_to_slot(int(v), 3) for v in vote[experts]]
+    assert got == golden[f"dsp/{case}/vote_prec"].tolist()
+    keep = ~skip.astype(bool)
+    assert np.array_equal(per_pair[keep], vote[idx[keep]].astype(np.uint8))
+    assert np.array_equal(per_pair[~keep], lvl.astype(np.uint8)[~keep])
+
+
+def test_expert_vote_known_answers():
+    # expert 0: levels 0, 0, 2 -> 2 of 3 at <= 0 >= 1.5 -> 0; expert 1: 1, 2 -> 1 of 2 at <= 1 -> 1;
+    # expert 2: 2, 2, 0 (last skipped) -> 2; expert 3: no pair -> -1
+    idx = np.array([[0, 1, 2], [0, 1, 2], [0, 2, 2]])
+    lvl = np.array([[0, 1, 2], [0, 2, 2], [2, 2, 0]])
+    skip = np.array([[0, 0, 0], [0, 0, 0], [0, 0, 1]], bool)
+    vote, per_pair = O.expert_vote(idx, lvl, skip, 4, 0.5)
+    assert vote.tolist() == [0, 1, 2, -1]
+    assert per_pair.tolist() == [[0, 1, 2], [0, 1, 2], [0, 2, 0]]
+    # hi_vote 1.0: every pair of the expert must ask for the level
+    vote, _ = O.expert_vote(idx, lvl, skip, 4, 1.0)
+    assert vote.tolist() == [2, 2, 2, -1]
+
+
 # -- router -----------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("case", ["olmoe_f32", "qwen3_f32", "olmoe_bf16"])
 def test_router_matches_transformers(golden, golden_meta, case):
