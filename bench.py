@@ -78,6 +78,9 @@ def parse():
                     help="expert-parallel dispatch/combine (N > 1): peer memory over NVLink or NCCL collectives")
     ap.add_argument("--policy", default=None, choices=["hi", "lo"],
                     help="--ncu mode: every pair at the most precise (hi) or least precise (lo) record")
+    ap.add_argument("--ep-extra", default="c3,c3p,c4",
+                    help="configurations also run expert-parallel when --gpus > 1 (c3: T=1/GPU decode; c3p: "
+                         "4096 tokens split over the ranks; c4: 256 tokens/GPU with cold uploads)")
     ap.add_argument("--extra", default="c0,c2,c3,c3p,c4,dense",
                     help="single-layer configs (and the dense int8 GEMV) measured beside the headline")
     return ap.parse_args()
@@ -494,11 +497,32 @@ def phase_times(step, reps: int = 5, flush_l2: bool = False):
     return up.value / reps, dn.value / reps
 
 
-def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: dict) -> dict:
+def ep_phase_split(stack, step, reps: int, world: int) -> dict:
+    """Expert-parallel layers: milliseconds per layer of dispatch (pack + all_gather + unpack),
+    experts, the partial-sum all_to_all and the combine, from CUDA events of eager steps (host launch
+    gaps included), max over ranks."""
+    stack.ep.timing = []
+    for _ in range(reps):
+        step()
+    ph = stack.ep.phase_ms()
+    n = max(1, len(stack.ep.timing))
+    stack.ep.timing = None
+    out = {}
+    for key in ("dispatch", "experts", "combine_exchange", "combine"):
+        out[key] = max_over_ranks(ph[key] / n, world)
+    out["timing"] = "eager steps, CUDA events per phase, per layer, max over ranks"
+    return out
+
+
+def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: dict, T: int | None = None,
+                   exchange: str = "nccl") -> dict:
     """Tokens/s of one MoE layer of `cfg` (CUDA-graph replay, inputs resident) and the roofline of
-    its expert kernels: HBM bytes for decode, tensor flops for prefill (tcgen05 path)."""
-    stack = Stack(cfg, dev, seed=1)
-    T = cfg["T"]
+    its expert kernels: HBM bytes for decode, tensor flops for prefill (tcgen05 path). With world > 1
+    the layer runs expert-parallel (T tokens per rank) and the line carries the per-phase split and
+    layer 0's parity against the single-GPU layer."""
+    ep = world > 1
+    stack = Stack(cfg, dev, seed=1, ep=ep, exchange=exchange)
+    T = cfg["T"] if T is None else T
     L = cfg["layers"]
     step = stack.make_device_step(T)
     stack.xs[0].copy_(torch.randn(T, cfg["H"], device=dev).to(stack.act))
@@ -506,6 +530,21 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
     g, ms = time_graph(step, steps, warmup, world, flush_l2=True)
     del g
     ms = max_over_ranks(ms, world)
+    if ep:
+        err = stack.ep_layer0_error()
+        phases = ep_phase_split(stack, step, 3, world)
+        out = {"workload": cfg["name"], "T_per_gpu": T, "n_gpus": world, "layers": L,
+               "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": ms, "ms_per_layer": ms / L,
+               "parallelism": f"ep{world} (NCCL all_gather + all_to_all)", "ep_max_rel_err": err,
+               "ep_phase_ms_per_layer": phases,
+               "layer_precisions": [lp[0] for lp in cfg["layer_precs"]] if cfg.get("layer_precs") else cfg["precs"],
+               "shared_expert": "run beside the routed experts on every rank for its own tokens"
+               if cfg.get("shared") else False,
+               "l2": "evicted (256 MB write) before every timed replay"}
+        stack.ep.close()
+        del stack
+        torch.cuda.empty_cache()
+        return out
     rb = stack.routing_bytes()
     up_ms, dn_ms = phase_times(step, flush_l2=True)
     pairs = rb["pairs"] + rb.get("shared_pairs", 0)
@@ -578,21 +617,27 @@ def measure_dense(dev, steps: int, warmup: int, peaks: dict) -> dict:
             "timing": "CUDA graph replay of one call (weights 103 MB > L2), CUDA events"}
 
 
-def measure_cold(cfg: dict, dev, steps: int, warmup: int) -> dict:
+def measure_cold(cfg: dict, dev, steps: int, warmup: int, world: int = 1) -> dict:
     """Config 4: every step routes T tokens, uploads the routed cold records from pinned host memory
     on a copy stream while the resident pairs run, then runs the uploaded pairs. Eager steps (one
-    routing read-back per layer, as the reference), CUDA events around the steps."""
+    routing read-back per layer, as the reference), CUDA events around the steps. With world > 1 the
+    layer runs expert-parallel (T tokens per rank, NCCL exchange): each rank holds and uploads only the
+    cold records of its own expert block, from the gathered routing of every rank."""
     from moeb200 import ops
     from moeb200.cold import ColdExperts
 
-    stack = Stack(cfg, dev, seed=2)
+    ep = world > 1
+    stack = Stack(cfg, dev, seed=2, ep=ep, exchange="nccl")
     E, T, k = cfg["E"], cfg["T"], cfg["k"]
     g = torch.Generator().manual_seed(4)
     cold_set = sorted(torch.randperm(E, generator=g)[: int(round(cfg["cold_frac"] * E))].tolist())
-    cold = ColdExperts(stack.rt, {p: len(cold_set) for p in cfg["precs"]})
-    for e in cold_set:
+    owned = [e for e in cold_set if stack.e_lo <= e < stack.e_hi]
+    cold = ColdExperts(stack.rt, {p: max(1, len(owned)) for p in cfg["precs"]})
+    for e in owned:
         for p in cfg["precs"]:
             cold.add_cold(0, e, p, stack.rt._records[(0, e, p)].cpu())
+    if ep:
+        stack.ep.cold = cold
     torch.cuda.empty_cache()
     b = dict(w=torch.empty(T, k, device=dev), idx=torch.empty(T, k, dtype=torch.int64, device=dev),
              level=torch.empty(T, k, dtype=torch.uint8, device=dev), skip=torch.empty(T, k, dtype=torch.uint8, device=dev))
@@ -603,11 +648,15 @@ def measure_cold(cfg: dict, dev, steps: int, warmup: int) -> dict:
     def step():
         cold.reset()  # nothing stays cached: the cold records are uploaded again every step
         ops.router(x, stack.wr[0], k, cfg["renorm"], stack.bias, pol, want_probs=False, out=b)
-        cold.run_layer(0, x, b["idx"], b["w"], b["level"], b["skip"], out)
+        if ep:
+            stack.ep.run_layer(0, x, b["idx"], b["w"], b["level"], b["skip"], out=out)
+        else:
+            cold.run_layer(0, x, b["idx"], b["w"], b["level"], b["skip"], out)
 
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    barrier(world)
     up0, by0 = cold.uploads, cold.uploaded_bytes
     a, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
@@ -615,17 +664,27 @@ def measure_cold(cfg: dict, dev, steps: int, warmup: int) -> dict:
         step()
     e_.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(e_) / steps
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(e_) / steps, world)
     ups = (cold.uploads - up0) / steps
     byts = (cold.uploaded_bytes - by0) / steps
     peak = h2d_peak_gbs(dev)
-    gbs = byts / (ms / 1e3) / 1e9
-    res = {"workload": "c4", "T": T, "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "cold_experts": len(cold_set),
-           "uploads_per_step": ups, "upload_bytes_per_step": byts, "miss": int(stack.rt.miss.item()),
+    gbs = byts / (ms / 1e3) / 1e9  # this rank's upload rate (every GPU has its own host link)
+    res = {"workload": "c4", "T": T, "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": ms,
+           "cold_experts": len(cold_set), "uploads_per_step": ups, "upload_bytes_per_step": byts,
+           "miss": int(stack.rt.miss.item()),
            "roofline": {"bound": "h2d", "kernel": "cold-record uploads (cudaMemcpyAsync on a copy stream)",
                         "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                         "peak_kind": "measured pinned H2D copy, 256 MiB"},
-           "timing": "eager steps (routing read back per layer), CUDA events"}
+           "timing": "eager steps (routing read back per layer), CUDA events" + (", max over ranks" if ep else "")}
+    if ep:
+        res.update({"T_per_gpu": T, "n_gpus": world, "cold_experts_this_rank": len(owned),
+                    "parallelism": f"ep{world} (NCCL all_gather + all_to_all; each rank uploads its own block's "
+                                   "routed cold records)",
+                    "uploads_per_step_rank0": ups, "upload_bytes_per_step_rank0": byts})
+        res.pop("uploads_per_step")
+        res.pop("upload_bytes_per_step")
+        stack.ep.close()
     del stack, cold
     torch.cuda.empty_cache()
     return res
@@ -789,6 +848,8 @@ def main():
     del graph
     # expert-parallel runs: the last replay's layer 0 against the single-GPU layer (outside timing)
     ep_err = stack.ep_layer0_error() if world > 1 else None
+    # expert-parallel runs: per-phase split of the headline layers (eager steps, outside the timed region)
+    ep_phases = ep_phase_split(stack, step, 2, world) if world > 1 else None
 
     # roofline of the dominant kernel (gate/up GEMV) from CUDA events on its stream
     try:
@@ -864,6 +925,17 @@ def main():
                "sample": sample}
 
     extra = {}
+    if world > 1:
+        for name in [c for c in args.ep_extra.split(",") if c]:
+            cfgx = CONFIGS[name]
+            if cfgx.get("cold_frac"):
+                extra[name] = measure_cold(cfgx, dev, max(5, args.steps // 2), 3, world)
+            elif name == "c3p":  # prefill: the 4096 tokens split over the ranks (strong scaling)
+                extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks,
+                                             T=max(1, cfgx["T"] // world))
+                extra[name]["scaling"] = "strong (4096 tokens in total)"
+            else:
+                extra[name] = measure_single(cfgx, dev, max(5, args.steps // 2), 3, world, peaks)
     for name in [c for c in args.extra.split(",") if c and world == 1]:
         if name == "dense":
             extra[name] = measure_dense(dev, max(20, args.steps), 5, peaks)
@@ -897,6 +969,7 @@ def main():
             "sweep": sweep,
             "missing_pairs": miss,
             "ep_max_rel_err": ep_err,
+            "ep_phase_ms_per_layer": ep_phases,
             "extra_configs": extra,
             "records_per_step": rb["records"], "pairs_per_step": rb["pairs"],
         }

@@ -672,7 +672,8 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   // two-launch grouped GEMV on every decode workload of the build's configs so far
   const bool decode = !gemm && g_path == 3;
   // warp-streamed GEMV: items of <= 8 pairs; x rows are staged with 16-byte bulk copies
-  const bool ws_ok = ws_supported(ex->layout, P, act_type, H, I, 8) && reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  const bool ws_ok = ws_supported(ex->layout, P, act_type, H, I, 8) && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                     ex->tma_base != 0 && ex->tma_base % 4096 == 0;
   if (g_path == 4 && !ws_ok)
     return fail(MOEB200_ERR_UNSUPPORTED, "warp-streamed GEMV: these record layouts, shapes or the x alignment are "
                                          "not supported");
@@ -770,6 +771,7 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   gp.job_next = fw.hdr->job_next;
   for (int p = 0; p < P; ++p) gp.lay[p] = to_dev(ex->layout[p]);
   gp.zero_acc = 1;
+  gp.tma_base = ex->tma_base;
   return run_expert_phases(gp, ex->layout, P, act_type, (int)max_items, n, nt, s, part ? nullptr : out, /*add=*/0,
                            gemm, streamed);
 }

@@ -57,6 +57,7 @@ struct GemvParams {
   int32_t pre_slices;   // split slices in pre (the up phase splits K at most this many ways; 0 = kMaxKSplit)
   int32_t* job_next;    // [2] job counters of the up and down launches, zeroed by the kernel that wrote
                         // the items (dispatch, table items, shared gate)
+  int64_t tma_base;     // warp-streamed GEMV: base of its weight tensor maps (moeb200_expert_table.tma_base)
 };
 
 // Geometry shared by host and device.
@@ -125,7 +126,8 @@ cudaError_t launch_decode(const DecodeParams& p, const moeb200_layout* lays, int
                           cudaStream_t s);
 
 // Warp-streamed grouped GEMV (gemv_ws.cu): items of at most 8 pairs; int4 / int8 records with
-// 64-column groups, or float records of the activation type; H and I multiples of 512.
+// 64-column groups, or float records of the activation type; H and I multiples of 512; records on
+// 4096-byte multiples above GemvParams::tma_base (row pitches dividing 4096 and the field offsets).
 bool ws_supported(const moeb200_layout* lays, int nlay, int act_type, int H, int I, int max_item_pairs);
 cudaError_t launch_ws_phases(GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int max_items,
                              cudaStream_t s);

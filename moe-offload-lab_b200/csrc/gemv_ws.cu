@@ -11,14 +11,17 @@
 // phase time is set by how soon every SM has its bytes in flight. Plain loads cannot do that: the
 // misses an SM can hold outstanding cap it near 11 GB/s at these latencies (measured: 1.6 TB/s for
 // the whole chip with 128 KB of loads issued per SM). Here every warp streams its own weight rows
-// with 1-D bulk copies (the copy engine, no per-SM miss limit) into two 5.3 KB shared-memory slots
-// of its own -- the next chunk always in flight while it multiplies the current one -- so each SM
-// keeps up to 128 KB of records in flight with no producer warp, tensor map or cross-warp
-// hand-off. A chunk is 256 bytes of each of the warp's 16 rows; each row lands at a pitch of 256
-// bytes plus an offset chosen so that the fragment reads of the warp's rows fall in different
-// banks. Its groups are multiplied in a fully unrolled sequence (every shared-memory offset a
-// constant), and a CTA runs 16 warps when their slots fit beside the activation rows (8 else),
-// so each scheduler has 4 warps' independent dequantise-and-multiply chains to interleave.
+// through the copy engine into two 5 KB shared-memory slots of its own -- the next chunk always in
+// flight while it multiplies the current one -- so each SM keeps up to 128 KB of records in flight
+// with no producer warp or cross-warp hand-off. A chunk is 256 bytes of each of the warp's 16 rows,
+// moved as 2-D TMA boxes of 128 bytes x 8 (gate/up) or 16 (down) rows from a tensor map of all
+// memory above the expert table's tma_base (records lie on row multiples above it, so no map is
+// built per record) -- four or two tensor loads per chunk plus one or two bulk copies of the tile's
+// whole scale rows, where per-row 1-D copies took 32: the copy engine's per-request cost, not DRAM,
+// bounded that version. The boxes land 128-byte swizzled, so the fragment reads of the warp's rows
+// fall in different banks. A chunk's groups are multiplied in a fully unrolled sequence, and a CTA
+// runs 16 warps when their slots fit beside the activation rows (8 else), so each scheduler has 4
+// warps' independent dequantise-and-multiply chains to interleave.
 //
 // Fragment layout. A warp owns one 16-row mma.sync m16n8k16 tile: up = 8 gate rows (tile rows
 // 0..7) and the matching 8 up rows (tile rows 8..15), so gate and up of one intermediate row land
@@ -26,8 +29,10 @@
 // in 64-column groups; in a group, lane (g, t) holds columns 16t..16t+15 of its rows g and g+8
 // (int4: 8 bytes per row, int8: 16, 16-bit floats: 32), so every mma sums columns of one scale
 // group: the exact integer products of the group are summed in fp32 and the group's partial is
-// scaled once (as gemv.cu does). The item's activation rows (B fragments) are staged in shared
-// memory with bulk copies, double-buffered across work units.
+// scaled once (as gemv.cu does). In a slot, byte b of box row r lies at
+// (b / 128) * SS + r * 128 + (((b / 16) % 8) ^ (r % 8)) * 16 + b % 16, SS = 1 KB (8-row boxes) or 2 KB
+// (16 rows); rows g and g + 8 share r % 8 = g. The item's activation rows (B fragments) are staged
+// in shared memory with bulk copies, double-buffered across work units.
 //
 // Work. A CTA (one per SM) takes units = (item, row block, all K): its warps split the
 // row block into 16-row tiles and, when a call has few items, K into ks parts (warp w: tile w / ks,
@@ -35,6 +40,7 @@
 // every run). The down kernel issues its first weight copies before it waits for the gate/up
 // kernel (only h comes from it), so its first DRAM round trip overlaps the gate/up tail.
 #include "gemv.cuh"
+#include "tma.cuh"
 
 namespace moeb200 {
 
@@ -43,29 +49,41 @@ namespace {
 constexpr int kWsMaxWarps = 16;
 constexpr int kWsMaxTok = 8;      // pairs of one item: one mma column block
 constexpr int kWsSegBytes = 256;  // weight bytes of one row per chunk
-constexpr int kWsScaleArea = 16 * 16;
-constexpr int kWsSlotBytes = 16 * (kWsSegBytes + 64) + kWsScaleArea;  // 5376: largest pitch + scales
+constexpr int kWsWBytes = 16 * kWsSegBytes;  // the chunk's 16 rows: two 128-byte segments of swizzled boxes
+// bytes above tma_base that the weight tensor maps cover (every record of a process lies well within)
+constexpr int64_t kWsSpan = 1ll << 40;
 
 enum WsKind : int { kWsI4 = 0, kWsI8 = 1, kWsF = 2 };
 
-// Per kind: NG = 64-column groups of one chunk (256 weight bytes per row), LB = bytes of one group
-// row per lane, PITCH = bytes between two rows of a slot (the rows a quarter- or half-warp reads at
-// one column offset fall in different banks), SB = scale bytes per row per chunk.
+// Per kind: NG = 64-column groups of one chunk (256 weight bytes per row).
 template <int KIND>
 struct WsGeo;
 template <>
 struct WsGeo<kWsI4> {
-  static constexpr int NG = 8, LB = 8, PITCH = kWsSegBytes + 32, SB = 16;
+  static constexpr int NG = 8;
 };
 template <>
 struct WsGeo<kWsI8> {
-  // a chunk uses 4 groups' scales; the 16-byte aligned 8 groups holding them are copied (bulk
-  // copies move multiples of 16 bytes) and read at the chunk's offset in them
-  static constexpr int NG = 4, LB = 16, PITCH = kWsSegBytes + 64, SB = 16;
+  static constexpr int NG = 4;
 };
 template <>
 struct WsGeo<kWsF> {
-  static constexpr int NG = 2, LB = 32, PITCH = kWsSegBytes + 16;
+  static constexpr int NG = 2;
+};
+
+// A slot of a phase with K columns: the chunk's weight boxes, then the 16 rows' whole scale rows
+// (16 * K / 64 * 2 bytes), rounded up to 1 KB so that every slot's boxes start on a 1024-byte
+// boundary (the period of the 128-byte swizzle).
+__host__ __device__ inline int ws_slot_bytes(int K) { return kWsWBytes + ((K / 2 + 1023) / 1024) * 1024; }
+// rows of the weight tensor map of a field with rows of rowb bytes
+__host__ __device__ inline int64_t ws_map_rows(int64_t rowb) {
+  return kWsSpan / rowb < 0x7fffffffll ? kWsSpan / rowb : 0x7fffffffll;
+}
+
+// Tensor maps of the weight fields, per precision slot and phase (0 gate/up, 1 down): uint8 [rows][row
+// bytes] views of the memory above tma_base, boxes of 128 bytes x 8 (gate/up) or 16 (down) rows.
+struct alignas(64) WsMaps {
+  CUtensorMap m[4][2];
 };
 
 __device__ __forceinline__ int ws_kind(int wtype) {
@@ -88,22 +106,26 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
 __device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
 __device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 
-// One chunk (NG groups, every offset a constant) of the lane's rows g and g+8 from its slot: wsl =
-// slot address; xs = shared address of the lane's token row at the chunk's first column plus 32t;
-// xon = the lane's token exists.
+// One chunk (NG groups, unrolled) of the lane's rows g and g+8: ra / rb = shared address of the
+// rows' first segment in the slot's boxes, ss = bytes between two segments of a row, sa / sb = the
+// rows' scales of the chunk's first group, xs = shared address of the lane's token row at the
+// chunk's first column plus 32t; xon = the lane's token exists.
 template <typename AT, int KIND>
-__device__ __forceinline__ void ws_chunk(uint32_t wsl, uint32_t xs, bool xon, int g, int t, uint32_t soff,
-                                         float (&tot)[4]) {
+__device__ __forceinline__ void ws_chunk(uint32_t ra, uint32_t rb, uint32_t ss, uint32_t sa, uint32_t sb, uint32_t xs,
+                                         bool xon, int g, int t, float (&tot)[4]) {
   using G = WsGeo<KIND>;
-  const uint32_t r0 = wsl + (uint32_t)(g * G::PITCH) + (uint32_t)(t * G::LB);
-  const uint32_t r1 = r0 + 8u * G::PITCH;
   if constexpr (KIND == kWsI4) {
     // the 8 groups' scales of both rows: 16 bytes per row
-    const uint4 sg = lds128(wsl + 16u * G::PITCH + g * G::SB), su = lds128(wsl + 16u * G::PITCH + (8 + g) * G::SB);
+    const uint4 sg = lds128(sa), su = lds128(sb);
     const uint32_t sgw[4] = {sg.x, sg.y, sg.z, sg.w}, suw[4] = {su.x, su.y, su.z, su.w};
+    // the lane's 8 bytes of group j: segment j / 4, 16-byte unit (2 (j % 4) + t / 2) ^ g
+    uint32_t uo[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) uo[jj] = ((uint32_t)((2 * jj + (t >> 1)) ^ g) << 4) + 8u * (t & 1);
 #pragma unroll
     for (int j = 0; j < G::NG; ++j) {
-      const uint2 wg = lds64(r0 + j * 32), wu = lds64(r1 + j * 32);
+      const uint32_t off = (uint32_t)(j >> 2) * ss + uo[j & 3];
+      const uint2 wg = lds64(ra + off), wu = lds64(rb + off);
       uint4 X0 = make_uint4(0, 0, 0, 0), X1 = X0;
       if (xon) {
         X0 = lds128(xs + j * 128);
@@ -134,12 +156,15 @@ __device__ __forceinline__ void ws_chunk(uint32_t wsl, uint32_t xs, bool xon, in
       tot[3] = fmaf(s1, d[3], tot[3]);
     }
   } else if constexpr (KIND == kWsI8) {
-    const uint2 sg = lds64(wsl + 16u * G::PITCH + g * G::SB + soff);
-    const uint2 su = lds64(wsl + 16u * G::PITCH + (8 + g) * G::SB + soff);
+    // the 4 groups' scales of both rows: 8 bytes per row
+    const uint2 sg = lds64(sa), su = lds64(sb);
     const uint32_t sgw[2] = {sg.x, sg.y}, suw[2] = {su.x, su.y};
+    // the lane's 16 bytes of group j: segment j / 2, 16-byte unit (4 (j % 2) + t) ^ g
+    const uint32_t uo[2] = {(uint32_t)(t ^ g) << 4, (uint32_t)((4 + t) ^ g) << 4};
 #pragma unroll
     for (int j = 0; j < G::NG; ++j) {
-      const uint4 wg = lds128(r0 + j * 64), wu = lds128(r1 + j * 64);
+      const uint32_t off = (uint32_t)(j >> 1) * ss + uo[j & 1];
+      const uint4 wg = lds128(ra + off), wu = lds128(rb + off);
       uint4 X0 = make_uint4(0, 0, 0, 0), X1 = X0;
       if (xon) {
         X0 = lds128(xs + j * 128);
@@ -167,17 +192,20 @@ __device__ __forceinline__ void ws_chunk(uint32_t wsl, uint32_t xs, bool xon, in
       tot[3] = fmaf(s1, d[3], tot[3]);
     }
   } else {
+    // the lane's 32 bytes of group j: segment j's 16-byte units 2t ^ g and (2t + 1) ^ g
+    const uint32_t u0 = (uint32_t)((2 * t) ^ g) << 4, u1 = (uint32_t)((2 * t + 1) ^ g) << 4;
 #pragma unroll
     for (int j = 0; j < G::NG; ++j) {
-      const uint4 g0 = lds128(r0 + j * 128), g1 = lds128(r0 + j * 128 + 16);
-      const uint4 u0 = lds128(r1 + j * 128), u1 = lds128(r1 + j * 128 + 16);
+      const uint32_t so = (uint32_t)j * ss;
+      const uint4 g0 = lds128(ra + so + u0), g1 = lds128(ra + so + u1);
+      const uint4 v0 = lds128(rb + so + u0), v1 = lds128(rb + so + u1);
       uint4 X0 = make_uint4(0, 0, 0, 0), X1 = X0;
       if (xon) {
         X0 = lds128(xs + j * 128);
         X1 = lds128(xs + j * 128 + 16);
       }
       const uint32_t w0[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const uint32_t w1[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      const uint32_t w1[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       const uint32_t xw[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
@@ -195,8 +223,19 @@ struct WsUnit {
   int r0;       // first row of the warp's tile (up: first gate row)
   int k0, kc;   // the warp's K part
   int nch;      // chunks in the part
+  int row0;     // the phase's weight field's first row in the tensor maps' row coordinates
   bool live;    // a well-formed item in which the tile has rows
 };
+
+// First row of a field at q in the row coordinates of a map with rows of rowb bytes above tma_base
+// (nrows of the field must fit), or -1: records lie on 4096-byte multiples above tma_base and the
+// row pitches divide 4096 and the field offsets, so -1 means a record the runtime did not place.
+__device__ __forceinline__ int ws_row0(int64_t q, int64_t tma_base, int64_t rowb, int64_t nrows) {
+  const int64_t dq = q - tma_base;
+  if (dq < 0 || dq % rowb) return -1;
+  const int64_t r = dq / rowb;
+  return r + nrows <= ws_map_rows(rowb) ? (int)r : -1;
+}
 
 template <bool UP>
 __device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, int rb, int ks, int nw, int warp) {
@@ -211,47 +250,61 @@ __device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, i
   u.kc = K / ks;
   u.k0 = (warp % ks) * u.kc;
   u.nch = u.kc / ws_cc(u.kind);
+  const int64_t rowb = (int64_t)K * (u.kind == kWsI4 ? 4 : u.kind == kWsI8 ? 8 : 16) / 8;
+  u.row0 = ws_row0(UP ? it.p_guq : it.p_dnq, p.tma_base, rowb, UP ? 2 * p.I : p.H);
   return u;
 }
 
-// The warp issues the bulk copies of chunk c of its unit into its slot: lanes 0..15 the 16 weight
-// row segments, lanes 16..31 their scale segments (integer records).
+// The warp issues chunk c of its unit into its slot: lanes 0..3 (gate/up: 128-byte segment k of the
+// 8 gate rows and of the 8 up rows) or 0..1 (down: segment k of the 16 rows) one TMA box each; the
+// next lanes one bulk copy each of the tile's whole scale rows (integer records).
 template <bool UP>
-__device__ __forceinline__ void ws_issue(const GemvParams& p, const WsUnit& u, int c, uint8_t* slot, uint64_t* bar,
-                                         int lane) {
+__device__ __forceinline__ void ws_issue(const GemvParams& p, const WsMaps& tm, const WsUnit& u, int c, uint8_t* slot,
+                                         uint64_t* bar, int lane) {
   const int K = UP ? p.H : p.I;
   const int kind = u.kind;
   const int col0 = u.k0 + c * ws_cc(kind);
   const int wbits = kind == kWsI4 ? 4 : kind == kWsI8 ? 8 : 16;
-  const int pitch = kind == kWsI4 ? WsGeo<kWsI4>::PITCH : kind == kWsI8 ? WsGeo<kWsI8>::PITCH : WsGeo<kWsF>::PITCH;
-  const int sb = kind == kWsI4 ? WsGeo<kWsI4>::SB : kind == kWsI8 ? WsGeo<kWsI8>::SB : 0;
-  if (lane == 0) mbar_arrive_expect_tx(bar, 16 * kWsSegBytes + 16 * sb);
+  const uint32_t srow = kind != kWsF ? (uint32_t)(K / 64) * 2u : 0u;
+  if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kWsWBytes + 16u * srow);
   __syncwarp();
-  const int rr = lane & 15;
-  const int row = UP ? (rr < 8 ? u.r0 + rr : p.I + u.r0 + rr - 8) : u.r0 + rr;
-  if (lane < 16) {
-    const uint8_t* q = reinterpret_cast<const uint8_t*>(UP ? u.it.p_guq : u.it.p_dnq);
-    const int64_t rstride = (int64_t)K * wbits / 8;
-    bulk_g2s(slot + rr * pitch, q + row * rstride + (int64_t)col0 * wbits / 8, kWsSegBytes, bar);
-  } else if (sb) {
-    // the 16-byte aligned run of 8 groups holding the chunk's groups (int8: 4 of them)
-    const uint8_t* s = reinterpret_cast<const uint8_t*>(UP ? u.it.p_gus : u.it.p_dns);
-    bulk_g2s(slot + 16 * pitch + rr * sb, s + (int64_t)row * (K / 64 * 2) + (col0 / 64 & ~7) * 2, sb, bar);
+  const uint64_t map = reinterpret_cast<uint64_t>(&tm.m[u.it.slot][UP ? 0 : 1]);
+  const uint32_t w = smem_u32(slot);
+  const int x0 = col0 * wbits / 8;  // the chunk's first byte of a row
+  const uint8_t* sc = reinterpret_cast<const uint8_t*>(UP ? u.it.p_gus : u.it.p_dns);
+  if (UP) {
+    if (lane < 4) {
+      const int k = lane & 1, half = lane >> 1;  // half 0: gate rows, 1: up rows
+      tma2d(w + 2048u * half + 1024u * k, map, x0 + 128 * k, u.row0 + half * p.I + u.r0, bar);
+    } else if (lane < 6 && srow) {
+      const int half = lane - 4;
+      bulk_g2s(slot + kWsWBytes + 8u * srow * half, sc + (int64_t)(half * p.I + u.r0) * srow, 8u * srow, bar);
+    }
+  } else {
+    if (lane < 2) {
+      tma2d(w + 2048u * lane, map, x0 + 128 * lane, u.row0 + u.r0, bar);
+    } else if (lane == 2 && srow) {
+      bulk_g2s(slot + kWsWBytes, sc + (int64_t)u.r0 * srow, 16u * srow, bar);
+    }
   }
 }
 
-// One phase, NW warps. Shared memory: activation rows [2][xrows][K + 8] (16-bit), weight slots
-// [NW][2], part sums [NW * 32] float4, mbarriers: 2 activation buffers, 2 per warp.
+// One phase, NW warps. Shared memory (from a 1024-byte boundary): weight slots [NW][2], activation
+// rows [2][xrows][K + 8] (16-bit), part sums [NW * 32] float4, mbarriers: 2 activation buffers, 2 per
+// warp.
 template <typename AT, bool UP, int NW>
-__global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int ks, int xrows) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, const __grid_constant__ WsMaps tm, int ks,
+                                                        int xrows) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int K = UP ? p.H : p.I;
   const int xstride = K * 2 + 16;  // odd multiple of 16 bytes: the token rows fall in different banks
-  uint8_t* xbuf = smem;
-  uint8_t* slots = smem + 2 * xrows * xstride;
-  float4* part = reinterpret_cast<float4*>(slots + NW * 2 * kWsSlotBytes);
+  const int slot_bytes = ws_slot_bytes(K);
+  uint8_t* slots = smem;
+  uint8_t* xbuf = smem + NW * 2 * slot_bytes;
+  float4* part = reinterpret_cast<float4*>(xbuf + 2 * xrows * xstride);
   uint64_t* xfull = reinterpret_cast<uint64_t*>(part + 32 * NW);
   uint64_t* wfull = xfull + 2;  // [warp][2]
   if (threadIdx.x == 0) {
@@ -259,7 +312,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int 
     fence_mbar_init();
   }
   __syncthreads();
-  uint8_t* myslot[2] = {slots + (warp * 2) * kWsSlotBytes, slots + (warp * 2 + 1) * kWsSlotBytes};
+  uint8_t* myslot[2] = {slots + (warp * 2) * slot_bytes, slots + (warp * 2 + 1) * slot_bytes};
 
   const int rows = UP ? p.I : p.H;
   const int rb_rows = (UP ? 8 : 16) * (NW / ks);
@@ -282,6 +335,10 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int 
       return true;
     }
     u = ws_unit<UP>(p, it, cu % upi, ks, NW, warp);
+    if (u.live && u.row0 < 0) {  // a record off the tensor maps' rows: flagged, its unit skipped
+      if (lane == 0) atomicExch(p.status, kDevBadIndex);
+      u.live = false;
+    }
     return true;
   };
   // issue the next chunk of the stream (skipping units where the warp has no rows)
@@ -292,7 +349,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int 
       ivalid = load_unit(icu, iu);
     }
     if (!ivalid) return;
-    ws_issue<UP>(p, iu, ic, myslot[n_issued & 1], &wfull[warp * 2 + (n_issued & 1)], lane);
+    ws_issue<UP>(p, tm, iu, ic, myslot[n_issued & 1], &wfull[warp * 2 + (n_issued & 1)], lane);
     ++n_issued;
     ++ic;
   };
@@ -364,10 +421,19 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int 
         if (landed && xready) {
           const uint32_t wsl = smem_u32(myslot[sl]);
           const uint32_t xc = xs + (uint32_t)(c * cc * 2);
-          const uint32_t soff = (uint32_t)(((u.k0 + c * cc) / 64 & 7) * 2);  // int8: 0 or 8
-          if (u.kind == kWsI4) ws_chunk<AT, kWsI4>(wsl, xc, xon, g, t, 0u, tot);
-          else if (u.kind == kWsI8) ws_chunk<AT, kWsI8>(wsl, xc, xon, g, t, soff, tot);
-          else ws_chunk<AT, kWsF>(wsl, xc, xon, g, t, 0u, tot);
+          // rows g and g+8: gate/up = row g of the gate boxes and of the up boxes (8 rows, segments
+          // 1 KB apart); down = rows g and g+8 of the 16-row boxes (segments 2 KB apart)
+          const uint32_t ra = wsl + (uint32_t)g * 128u;
+          const uint32_t rb = UP ? wsl + 2048u + (uint32_t)g * 128u : wsl + (uint32_t)(g + 8) * 128u;
+          const uint32_t ss = UP ? 1024u : 2048u;
+          // the rows' scales of the chunk's first group (whole scale rows follow the boxes)
+          const uint32_t srow = (uint32_t)(K / 64) * 2u;
+          const uint32_t g0 = (uint32_t)((u.k0 + c * cc) / 64) * 2u;
+          const uint32_t sa = wsl + kWsWBytes + (uint32_t)g * srow + g0;
+          const uint32_t sb = wsl + kWsWBytes + (uint32_t)(g + 8) * srow + g0;
+          if (u.kind == kWsI4) ws_chunk<AT, kWsI4>(ra, rb, ss, sa, sb, xc, xon, g, t, tot);
+          else if (u.kind == kWsI8) ws_chunk<AT, kWsI8>(ra, rb, ss, sa, sb, xc, xon, g, t, tot);
+          else ws_chunk<AT, kWsF>(ra, rb, ss, sa, sb, xc, xon, g, t, tot);
         }
         // every lane is done with the slot before the copy that reuses it is issued
         __syncwarp();
@@ -415,24 +481,26 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, int 
 }
 
 size_t ws_smem(int K, int nw, int xrows) {
-  return (size_t)2 * xrows * (K * 2 + 16) + (size_t)nw * 2 * kWsSlotBytes + (size_t)nw * 32 * 16 + (2 + 2 * nw) * 8;
+  return 1024 /* alignment of the slots */ + (size_t)nw * 2 * ws_slot_bytes(K) + (size_t)2 * xrows * (K * 2 + 16) +
+         (size_t)nw * 32 * 16 + (2 + 2 * nw) * 8;
 }
 
 // Warps of a CTA: 16 when their slots fit beside the activation rows, else 8.
 int ws_warps(int K, int xrows) { return ws_smem(K, 16, xrows) <= 227 * 1024 ? 16 : 8; }
 
 template <typename AT, bool UP, int NW>
-cudaError_t ws_launch_nw(const GemvParams& p, int ks, int xrows, int grid, cudaStream_t s) {
+cudaError_t ws_launch_nw(const GemvParams& p, const WsMaps& tm, int ks, int xrows, int grid, cudaStream_t s) {
   const int K = UP ? p.H : p.I;
   const size_t smem = ws_smem(K, NW, xrows);
   cudaError_t e = cudaFuncSetAttribute(ws_kernel<AT, UP, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_chained(ws_kernel<AT, UP, NW>, dim3(grid), dim3(32 * NW), smem, s, p, ks, xrows);
+  return launch_chained(ws_kernel<AT, UP, NW>, dim3(grid), dim3(32 * NW), smem, s, p, tm, ks, xrows);
 }
 
 template <typename AT, bool UP>
-cudaError_t ws_launch(const GemvParams& p, int nw, int ks, int xrows, int grid, cudaStream_t s) {
-  return nw == 16 ? ws_launch_nw<AT, UP, 16>(p, ks, xrows, grid, s) : ws_launch_nw<AT, UP, 8>(p, ks, xrows, grid, s);
+cudaError_t ws_launch(const GemvParams& p, const WsMaps& tm, int nw, int ks, int xrows, int grid, cudaStream_t s) {
+  return nw == 16 ? ws_launch_nw<AT, UP, 16>(p, tm, ks, xrows, grid, s)
+                  : ws_launch_nw<AT, UP, 8>(p, tm, ks, xrows, grid, s);
 }
 
 // K parts of a phase: the fewest (1, 2, 4, ...) whose units give every SM work, keeping every part
@@ -463,16 +531,19 @@ bool ws_supported(const moeb200_layout* lays, int nlay, int act_type, int H, int
     } else if (L.wtype != act_type) {
       return false;  // float records are read as the activation type
     }
-    // every field 16-byte aligned inside the record (bulk copies)
-    if (L.off_gu_q % 16 || L.off_dn_q % 16 || (isint && (L.off_gu_s % 16 || L.off_dn_s % 16))) return false;
+    // scale fields 16-byte aligned inside the record (bulk copies)
+    if (isint && (L.off_gu_s % 16 || L.off_dn_s % 16)) return false;
+    // tensor-map rows: records lie on 4096-byte multiples above the maps' base, so the row pitches
+    // must divide 4096 and the weight field offsets
+    const int bits = gemv_wbits(L.wtype);
+    const int rb_up = H * bits / 8, rb_dn = I * bits / 8;
+    if (4096 % rb_up || 4096 % rb_dn || L.off_gu_q % rb_up || L.off_dn_q % rb_dn) return false;
   }
   return ws_smem(std::max(H, I), 8, kWsMaxTok) <= 227 * 1024;
 }
 
 cudaError_t launch_ws_phases(GemvParams& p, const moeb200_layout* lays, int nlay, int act_type, int max_items,
                              cudaStream_t s) {
-  (void)lays;
-  (void)nlay;
   const int sms = num_sms_cached();
   const int xrows = std::min(kWsMaxTok, p.T);  // an item holds at most this many pairs
   const int nw_up = ws_warps(p.H, xrows), nw_dn = ws_warps(p.I, xrows);
@@ -484,15 +555,25 @@ cudaError_t launch_ws_phases(GemvParams& p, const moeb200_layout* lays, int nlay
   const int grid_up = (int)std::max<int64_t>(1, std::min<int64_t>(sms, cu_up));
   const int grid_dn = (int)std::max<int64_t>(1, std::min<int64_t>(sms, cu_dn));
   p.ksplit_up = p.ksplit_dn = 1;
+  if (p.tma_base == 0 || p.tma_base % 4096) return cudaErrorInvalidValue;
+  WsMaps tm{};
+  for (int i = 0; i < nlay && i < 4; ++i) {
+    const int bits = gemv_wbits(lays[i].wtype);
+    const int rb_up = p.H * bits / 8, rb_dn = p.I * bits / 8;
+    cudaError_t e = tma_rows2d_map(&tm.m[i][0], (uint64_t)p.tma_base, rb_up, ws_map_rows(rb_up), 8);
+    if (e != cudaSuccess) return e;
+    e = tma_rows2d_map(&tm.m[i][1], (uint64_t)p.tma_base, rb_dn, ws_map_rows(rb_dn), 16);
+    if (e != cudaSuccess) return e;
+  }
   cudaError_t e = trace_mark(0, s);
   if (e != cudaSuccess) return e;
-  e = act_type == MOEB200_BF16 ? ws_launch<__nv_bfloat16, true>(p, nw_up, ks_up, xrows, grid_up, s)
-                               : ws_launch<__half, true>(p, nw_up, ks_up, xrows, grid_up, s);
+  e = act_type == MOEB200_BF16 ? ws_launch<__nv_bfloat16, true>(p, tm, nw_up, ks_up, xrows, grid_up, s)
+                               : ws_launch<__half, true>(p, tm, nw_up, ks_up, xrows, grid_up, s);
   if (e != cudaSuccess) return e;
   e = trace_mark(1, s);
   if (e != cudaSuccess) return e;
-  e = act_type == MOEB200_BF16 ? ws_launch<__nv_bfloat16, false>(p, nw_dn, ks_dn, xrows, grid_dn, s)
-                               : ws_launch<__half, false>(p, nw_dn, ks_dn, xrows, grid_dn, s);
+  e = act_type == MOEB200_BF16 ? ws_launch<__nv_bfloat16, false>(p, tm, nw_dn, ks_dn, xrows, grid_dn, s)
+                               : ws_launch<__half, false>(p, tm, nw_dn, ks_dn, xrows, grid_dn, s);
   if (e != cudaSuccess) return e;
   return trace_mark(2, s);
 }

@@ -81,6 +81,35 @@ cudaError_t tma_rows3d_map(CUtensorMap* out, uint64_t base, int row_bytes, int b
   return cudaSuccess;
 }
 
+cudaError_t tma_rows2d_map(CUtensorMap* out, uint64_t base, int row_bytes, int64_t rows, int box_rows) {
+  static std::mutex mu;
+  static std::map<std::tuple<uint64_t, int, int64_t, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if (row_bytes < 128 || row_bytes % 128 || box_rows < 1 || box_rows > 256 || rows < box_rows || rows > 0x7fffffffll)
+    return cudaErrorInvalidValue;
+  const auto key = std::make_tuple(base, row_bytes, rows, box_rows);
+  auto f = cache.find(key);
+  if (f != cache.end()) {
+    *out = f->second;
+    return cudaSuccess;
+  }
+  auto encode = encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, reinterpret_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (cache.size() > 256) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return cudaSuccess;
+}
+
 cudaError_t tma_rows16_map(CUtensorMap* out, const void* base, int cols, int rows, int box_rows, int act_type) {
   auto encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;

@@ -49,6 +49,12 @@ cudaError_t tma_weight_template(CUtensorMap* out, int row_bytes, int rows, int b
 // segment-major in shared memory with 128-byte swizzle. Cached per (base, row_bytes, box_rows).
 cudaError_t tma_rows3d_map(CUtensorMap* out, uint64_t base, int row_bytes, int box_rows);
 
+// Host: 2-D uint8 tensor map [rows][row_bytes] of the memory from `base` on (row_bytes a multiple of
+// 128), boxes of 128 bytes x box_rows rows with 128-byte swizzle. Records that lie on row_bytes
+// multiples above `base` are read through the row coordinate, so no map is built per record. Cached
+// per (base, row_bytes, rows, box_rows).
+cudaError_t tma_rows2d_map(CUtensorMap* out, uint64_t base, int row_bytes, int64_t rows, int box_rows);
+
 // Host: tensor map of a row-major 16-bit matrix [rows][cols] at `base`, boxes of 64 columns x
 // box_rows with 128-byte swizzle (the K-major operand layout of the tensor cores).
 cudaError_t tma_rows16_map(CUtensorMap* out, const void* base, int cols, int rows, int box_rows, int act_type);

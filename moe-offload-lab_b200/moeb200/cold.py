@@ -5,9 +5,10 @@ to the device on a dedicated copy stream and records an event, `_ready` makes th
 wait on it before use (moelab/runtime.py:310-333), and the host pool lends pinned slots and only
 reuses a slot after the event of its last use (moelab/hostpool.py:52-196).
 
-Per layer, `ColdExperts.run_layer`:
+Per layer, `ColdExperts.run_layer` (or `run_part` for the experts [e_lo, e_hi) of one rank of an
+expert-parallel group, over the gathered tokens of every rank, writing an fp32 partial sum):
   1. reads the routing back once (the reference reads it back too, moelab/runtime.py:505) and
-     lists the (expert, precision) records that are routed but only held on the host;
+     lists the (expert, precision) records in range that are routed but only held on the host;
   2. assigns each one a device slot (least recently used first, never a slot that this layer needs)
      and issues one cudaMemcpyAsync per record on the copy stream; a reused slot's copy first waits
      on the event that ended its previous use; one event marks the end of the uploads;
@@ -137,6 +138,19 @@ class ColdExperts:
     @torch.no_grad()
     def run_layer(self, layer: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, level: torch.Tensor | None,
                   skip: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+        """out[T, H] = the layer over every expert, uploading the routed cold records first."""
+        return self._run(layer, x, idx, w, level, skip, 0, self.rt.num_experts, out=out)
+
+    @torch.no_grad()
+    def run_part(self, layer: int, e_lo: int, e_hi: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+                 level: torch.Tensor | None, skip: torch.Tensor | None, part: torch.Tensor) -> torch.Tensor:
+        """part[T, H] fp32 = the pairs routed to experts [e_lo, e_hi) (one rank's block under expert
+        parallelism: the tokens are every rank's), uploading the block's routed cold records first."""
+        return self._run(layer, x, idx, w, level, skip, e_lo, e_hi, part=part)
+
+    def _run(self, layer: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, level: torch.Tensor | None,
+             skip: torch.Tensor | None, e_lo: int, e_hi: int, out: torch.Tensor | None = None,
+             part: torch.Tensor | None = None) -> torch.Tensor:
         rt = self.rt
         T, k = idx.shape
         P = rt.n_prec
@@ -154,13 +168,17 @@ class ColdExperts:
         slot = np.minimum(lv_h, P - 1) if P >= 3 else np.where(lv_h == 0, 0, P - 1)
         code = idx_h.astype(np.int64) * P + slot
         cold_code = self._cold_codes(layer, rt.num_experts, P)
-        cold_pair = np.isin(code, cold_code) & ~sk_h
+        cold_pair = np.isin(code, cold_code) & ~sk_h & (idx_h >= e_lo) & (idx_h < e_hi)
         needed: dict[str, list] = {p: [] for p in self.plans}
         for c in np.unique(code[cold_pair]).tolist():
             e, sl = divmod(int(c), P)
             needed[rt.precisions[sl]].append((layer, e, rt.precisions[sl]))
         cold_pair = torch.from_numpy(cold_pair)
         if not cold_pair.any():
+            if part is not None:
+                rt._table(layer)
+                return ops.experts_forward_part(rt._ctables[layer], e_lo, e_hi, x, idx, w, level, skip, part=part,
+                                                miss=rt.miss)
             return rt.run_layer(layer, x, idx, w, level=level, skip=skip, out=out)
         E = rt.num_experts
         writes: dict[int, list[tuple[int, int]]] = {}
@@ -196,13 +214,14 @@ class ColdExperts:
         ct = rt._ctables[layer]
         # hot pairs run while the uploads are in flight (the cold pairs' table entries are written on
         # the copy stream and only read after the compute stream has waited on `done`)
-        ops.experts_forward_part(ct, 0, rt.num_experts, x, idx, w, level, base | mask, part=parts[0], miss=rt.miss)
+        ops.experts_forward_part(ct, e_lo, e_hi, x, idx, w, level, base | mask, part=parts[0], miss=rt.miss)
         cur.wait_event(done)
-        ops.experts_forward_part(ct, 0, rt.num_experts, x, idx, w, level, base | (1 - mask), part=parts[1],
-                                 miss=rt.miss)
+        ops.experts_forward_part(ct, e_lo, e_hi, x, idx, w, level, base | (1 - mask), part=parts[1], miss=rt.miss)
         for prec, s in used:
             ev = torch.cuda.Event()
             ev.record(cur)
             self.last_use[(prec, s)] = ev
+        if part is not None:
+            return ops.combine_parts(parts, part)
         ops.combine_parts(parts, out)
         return out

@@ -26,6 +26,11 @@ Two exchanges implement dispatch and combine:
         per layer than NCCL's small collectives), so it is opt-in.
 Every rank must call with the same T (a rank with fewer tokens pads with rows whose skip flags are
 set).
+
+Cold experts (records held in pinned host memory, uploaded when routed) work under the "nccl"
+exchange: attach a ColdExperts of this rank's runtime as `ExpertParallel.cold`; each rank then reads
+the gathered routing back, uploads only the routed cold records of its own block and runs its
+block's pairs as a resident pass and an uploaded pass.
 """
 
 from __future__ import annotations
@@ -198,6 +203,10 @@ class ExpertParallel:
         self._bufs: dict[tuple, _Bufs] = {}
         self._peers: dict[tuple, PeerExchange] = {}
         self.failed: str | None = None  # the first failed collective, once one failed
+        self.cold = None  # optional ColdExperts of this rank's runtime ("nccl" exchange)
+        # phase timing: when a list, every run_layer appends (pack + all_gather + unpack, experts,
+        # all_to_all, combine) CUDA event pairs recorded on the current stream (eager calls only)
+        self.timing: list | None = None
 
     def _collective(self, phase: str, fn, *args) -> None:
         """Run one collective of the exchange; a failure (peer error, exit or timeout) marks the group
@@ -260,18 +269,53 @@ class ExpertParallel:
         if out is None:
             out = torch.empty_like(x2)
         if self.exchange == "p2p":
+            if self.cold is not None:
+                raise ValueError("cold experts under expert parallelism need the 'nccl' exchange")
             self._run_p2p(layer, x2, idx, w, level, skip, b, out.view(T, H), votes)
             return out.view_as(x)
+        ev = self._events(5) if self.timing is not None else None
+        if ev:
+            ev[0].record()
         self.ops.pack(x2, idx, w, level, skip, b.rows)
         self._collective("dispatch all_gather", dist.all_gather_into_tensor, b.rows_all, b.rows)
         self.ops.unpack(b.rows_all, H, k, x2.dtype, b.x_all, b.idx_all, b.w_all, b.level_all, b.skip_all)
         if votes and self.world * T > 1:
             self.ops.vote(b.idx_all, b.level_all, b.skip_all, self.runtime.num_experts, self.runtime.policy.hi_vote)
-        self.ops.local(self.runtime, layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all,
-                       b.skip_all, b.part)
+        if ev:
+            ev[1].record()
+        if self.cold is not None:
+            self.cold.run_part(layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all, b.skip_all,
+                               b.part)
+        else:
+            self.ops.local(self.runtime, layer, self.e_lo, self.e_hi, b.x_all, b.idx_all, b.w_all, b.level_all,
+                           b.skip_all, b.part)
+        if ev:
+            ev[2].record()
         self._collective("combine all_to_all", dist.all_to_all_single, b.recv, b.part)
+        if ev:
+            ev[3].record()
         self.ops.combine(b.recv.view(self.world, T, H), out.view(T, H))
+        if ev:
+            ev[4].record()
+            self.timing.append(ev)
         return out.view_as(x)
+
+    @staticmethod
+    def _events(n: int) -> list:
+        return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+    def phase_ms(self) -> dict:
+        """Per-phase milliseconds summed over the calls recorded in `timing` (synchronises):
+        dispatch = pack + all_gather + unpack (+ vote), experts, combine_exchange = the all_to_all of
+        the partial sums, combine = the rank-order add and cast."""
+        torch.cuda.synchronize()
+        tot = {"dispatch": 0.0, "experts": 0.0, "combine_exchange": 0.0, "combine": 0.0}
+        for ev in self.timing or []:
+            tot["dispatch"] += ev[0].elapsed_time(ev[1])
+            tot["experts"] += ev[1].elapsed_time(ev[2])
+            tot["combine_exchange"] += ev[2].elapsed_time(ev[3])
+            tot["combine"] += ev[3].elapsed_time(ev[4])
+        return tot
 
     def _run_p2p(self, layer, x2, idx, w, level, skip, b: _Bufs, out, votes: bool = False) -> None:
         from . import _lib

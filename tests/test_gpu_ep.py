@@ -113,7 +113,7 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p", "nccl_cold"])
 def test_expert_parallel_two_ranks(tmp_path, exchange):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=f"{ROOT}:{ROOT / 'moe-offload-lab_b200'}")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
@@ -128,3 +128,5 @@ def test_expert_parallel_two_ranks(tmp_path, exchange):
         assert res["err_single"] < 4e-3, res
         assert res["err_repeat"] < 4e-3, res  # the second call reuses the exchange buffers
         assert res["miss"] == 0 and res["status"] == 0, res
+        if exchange == "nccl_cold":
+            assert res["uploads"] > 0, res
