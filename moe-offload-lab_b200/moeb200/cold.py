@@ -5,6 +5,13 @@ to the device on a dedicated copy stream and records an event, `_ready` makes th
 wait on it before use (moelab/runtime.py:310-333), and the host pool lends pinned slots and only
 reuses a slot after the event of its last use (moelab/hostpool.py:52-196).
 
+A cold record is held either in pinned host memory (`add_cold`) or only on disk in an expert store
+(`add_stored`, with a moeb200.store.RecordStore and a moeb200.hostpool.PinnedPool): a stored record
+that is routed is read by the store's reader threads into a pool slot while the resident pairs
+compute, then copied to its device slot on the copy stream; the pool slot goes back with the copy's
+event and is reused only after it fired and the pool advanced a layer (moelab's store-to-device
+path: ExpertStore.read, store.py:423-445, into HostPool slots, hostpool.py:140-170).
+
 Per layer, `ColdExperts.run_layer` (or `run_part` for the experts [e_lo, e_hi) of one rank of an
 expert-parallel group, over the gathered tokens of every rank, writing an fp32 partial sum):
   1. reads the routing back once (the reference reads it back too, moelab/runtime.py:505) and
@@ -79,9 +86,12 @@ class SlotPlan:
 class ColdExperts:
     """Host-held records of a B200Runtime, uploaded into `slots[prec]` device slots on demand."""
 
-    def __init__(self, runtime, slots: dict[str, int]):
+    def __init__(self, runtime, slots: dict[str, int], store=None, pool=None):
         self.rt = runtime
         self.dev = runtime.device
+        self.store = store  # RecordStore of the records added with add_stored
+        self.pool = pool    # PinnedPool the stored records are read into
+        self.disk: set[tuple] = set()
         self.copy_stream = torch.cuda.Stream(self.dev)
         self.host: dict[tuple, torch.Tensor] = {}
         self.plans = {p: SlotPlan(n) for p, n in slots.items()}
@@ -107,12 +117,25 @@ class ColdExperts:
         self._codes.pop(layer, None)
         self.rt.remove_record(layer, expert, prec)
 
+    def add_stored(self, layer: int, expert: int, prec: str) -> None:
+        """Register a record that stays on disk in the store (read when routed)."""
+        if self.store is None or self.pool is None:
+            raise ValueError("stored cold records need a store and a pinned pool")
+        if prec not in self.plans:
+            raise ValueError(f"no device slots for precision {prec}")
+        if self.store.record_bytes(prec) != self.rt.layouts[prec]["record_bytes"]:
+            raise ValueError("the store's record size does not match the precision's layout")
+        self.disk.add((layer, expert, prec))
+        self.host.pop((layer, expert, prec), None)
+        self._codes.pop(layer, None)
+        self.rt.remove_record(layer, expert, prec)
+
     def _cold_codes(self, layer: int, E: int, P: int) -> np.ndarray:
         """expert * P + slot of every host-held record of `layer` (cached per layer)."""
         c = self._codes.get(layer)
         if c is None:
-            c = np.array(sorted(e * P + self.rt.precisions.index(p) for (l_, e, p) in self.host if l_ == layer),
-                         np.int64)
+            keys = set(self.host) | self.disk
+            c = np.array(sorted(e * P + self.rt.precisions.index(p) for (l_, e, p) in keys if l_ == layer), np.int64)
             self._codes[layer] = c
         return c
 
@@ -184,7 +207,9 @@ class ColdExperts:
         writes: dict[int, list[tuple[int, int]]] = {}
         cur = torch.cuda.current_stream(self.dev)
         self.copy_stream.wait_stream(cur)  # the routing and any earlier table writes come first
-        used = []
+        if self.pool is not None:
+            self.pool.advance()  # a new layer: pool slots released by earlier layers may be reused
+        used, disk = [], []
         with torch.cuda.stream(self.copy_stream):
             for prec, keys in needed.items():
                 if not keys:
@@ -193,28 +218,44 @@ class ColdExperts:
                 used += [(prec, s) for s in slot_of.values()]
                 for key, s, old in uploads:
                     ev = self.last_use.get((prec, s))
-                    if ev is not None:
-                        self.copy_stream.wait_event(ev)  # quarantine: the slot's last reader is done
-                    self.buf[prec][s].copy_(self.host[key], non_blocking=True)
-                    self.uploaded_bytes += self.host[key].numel()
-                    self.uploads += 1
+                    if key in self.host:
+                        if ev is not None:
+                            self.copy_stream.wait_event(ev)  # quarantine: the slot's last reader is done
+                        self.buf[prec][s].copy_(self.host[key], non_blocking=True)
+                        self.uploaded_bytes += self.host[key].numel()
+                        self.uploads += 1
+                    else:  # on disk: read on a store thread into a pool slot, copied once it is there
+                        hb = self.pool.acquire(prec)
+                        disk.append((key, prec, s, ev, hb, self.store.read_async(key[0], key[1], prec, hb)))
                     if old is not None:
                         ol, oe, op = old
                         writes.setdefault(ol, []).append((rt.precisions.index(op) * E + oe, 0))
                 for (l_, e, p_), s in slot_of.items():
                     writes.setdefault(layer, []).append((rt.precisions.index(p_) * E + e, self.buf[p_][s].data_ptr()))
+        mask = cold_pair.to(self.dev, non_blocking=True).to(torch.uint8)
+        base = skip if skip is not None else torch.zeros(T, k, dtype=torch.uint8, device=self.dev)
+        parts = torch.empty(2, T, x.shape[-1], dtype=torch.float32, device=self.dev)
+        ct = rt._ctables[layer]
+        # hot pairs run while the uploads (and the disk reads) are in flight: the cold pairs' table
+        # entries are written on the copy stream and only read after the compute stream has waited on
+        # `done`; the hot pass reads no entry of a cold key
+        ops.experts_forward_part(ct, e_lo, e_hi, x, idx, w, level, base | mask, part=parts[0], miss=rt.miss)
+        with torch.cuda.stream(self.copy_stream):
+            for key, prec, s, ev, hb, fut in disk:
+                fut.result()  # the record is in the pool slot
+                if ev is not None:
+                    self.copy_stream.wait_event(ev)
+                self.buf[prec][s].copy_(hb, non_blocking=True)
+                copied = torch.cuda.Event()
+                copied.record(self.copy_stream)
+                self.pool.release(hb, copied)  # reusable after this copy and a layer advance
+                self.uploaded_bytes += hb.numel()
+                self.uploads += 1
             # one indexed store per table; its entries are distinct (an evicted key is never one that
             # this layer needs, and each slot holds one key)
             self._write_table(writes)
             done = torch.cuda.Event()
             done.record(self.copy_stream)
-        mask = cold_pair.to(self.dev, non_blocking=True).to(torch.uint8)
-        base = skip if skip is not None else torch.zeros(T, k, dtype=torch.uint8, device=self.dev)
-        parts = torch.empty(2, T, x.shape[-1], dtype=torch.float32, device=self.dev)
-        ct = rt._ctables[layer]
-        # hot pairs run while the uploads are in flight (the cold pairs' table entries are written on
-        # the copy stream and only read after the compute stream has waited on `done`)
-        ops.experts_forward_part(ct, e_lo, e_hi, x, idx, w, level, base | mask, part=parts[0], miss=rt.miss)
         cur.wait_event(done)
         ops.experts_forward_part(ct, e_lo, e_hi, x, idx, w, level, base | (1 - mask), part=parts[1], miss=rt.miss)
         for prec, s in used:
