@@ -554,7 +554,7 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
            "shared_expert": ("folded into the routed launches (expert E, one more pair per token)"
                              if stack.shared_fused else bool(cfg.get("shared"))),
            "l2": "evicted (256 MB write) before every timed replay and every traced call"}
-    prefill = T * cfg["k"] >= 16 * cfg["E"]
+    prefill = T * cfg["k"] >= 40 * cfg["E"]  # the automatic path's GEMM switch (40 pairs per expert)
     if prefill:
         flops = 6.0 * cfg["H"] * cfg["I"] * pairs
         tf = flops / ((up_ms + dn_ms) / 1e3) / 1e12
