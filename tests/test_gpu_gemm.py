@@ -38,6 +38,10 @@ CASES = [
     ("int8_gs16_bf16", 512, 256, 8, 2, 80, ["int8"], dict(mode="lo"), "bf16", False, False, 16),
     ("int8_gs128_int4_fp16", 1024, 512, 16, 4, 200, ["int8", "int4"], dict(mode="hobbit", t1=0.6), "fp16", True,
      False, 128),
+    # items of more than 128 pairs: the weight tile feeds two token halves (two B stages, two MMAs)
+    ("fp16_items_of_200", 512, 256, 4, 2, 400, ["fp16"], dict(mode="hi"), "fp16", False, False),
+    ("int8_items_of_256_bf16", 512, 256, 4, 2, 512, ["int8"], dict(mode="lo"), "bf16", False, False),
+    ("int4_items_130_to_250", 1024, 256, 6, 3, 400, ["int4"], dict(mode="lo"), "fp16", False, False),
 ]
 
 
