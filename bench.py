@@ -566,7 +566,8 @@ def measure_single(cfg: dict, dev, steps: int, warmup: int, world: int, peaks: d
         byts = rb["up_total"] + rb["down_total"]
         gbs = byts / ((up_ms + dn_ms) / 1e3) / 1e9
         peak = peaks.get("hbm_gbs", 6650.0)
-        kname = "fused decode kernel (one launch)" if path_used() == 3 else "grouped GEMV (up + down)"
+        kname = {3: "fused decode kernel (one launch)", 4: "warp-streamed grouped GEMV (up + down)"}.get(
+            path_used(), "grouped GEMV (up + down)")
         out["roofline"] = {"bound": "hbm", "kernel": kname, "achieved": gbs, "peak": peak,
                            "unit": "GB/s", "frac": gbs / peak, "bytes_per_step": byts, "up_ms": up_ms,
                            "down_ms": dn_ms}
