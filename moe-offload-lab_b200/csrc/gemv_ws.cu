@@ -50,8 +50,6 @@ constexpr int kWsMaxWarps = 16;
 constexpr int kWsMaxTok = 8;      // pairs of one item: one mma column block
 constexpr int kWsSegBytes = 256;  // weight bytes of one row per chunk
 constexpr int kWsWBytes = 16 * kWsSegBytes;  // the chunk's 16 rows: two 128-byte segments of swizzled boxes
-// bytes above tma_base that the weight tensor maps cover (every record of a process lies well within)
-constexpr int64_t kWsSpan = 1ll << 40;
 
 enum WsKind : int { kWsI4 = 0, kWsI8 = 1, kWsF = 2 };
 
@@ -75,10 +73,6 @@ struct WsGeo<kWsF> {
 // (16 * K / 64 * 2 bytes), rounded up to 1 KB so that every slot's boxes start on a 1024-byte
 // boundary (the period of the 128-byte swizzle).
 __host__ __device__ inline int ws_slot_bytes(int K) { return kWsWBytes + ((K / 2 + 1023) / 1024) * 1024; }
-// rows of the weight tensor map of a field with rows of rowb bytes
-__host__ __device__ inline int64_t ws_map_rows(int64_t rowb) {
-  return kWsSpan / rowb < 0x7fffffffll ? kWsSpan / rowb : 0x7fffffffll;
-}
 
 // Tensor maps of the weight fields, per precision slot and phase (0 gate/up, 1 down): uint8 [rows][row
 // bytes] views of the memory above tma_base, boxes of 128 bytes x 8 (gate/up) or 16 (down) rows.
@@ -227,15 +221,6 @@ struct WsUnit {
   bool live;    // a well-formed item in which the tile has rows
 };
 
-// First row of a field at q in the row coordinates of a map with rows of rowb bytes above tma_base
-// (nrows of the field must fit), or -1: records lie on 4096-byte multiples above tma_base and the
-// row pitches divide 4096 and the field offsets, so -1 means a record the runtime did not place.
-__device__ __forceinline__ int ws_row0(int64_t q, int64_t tma_base, int64_t rowb, int64_t nrows) {
-  const int64_t dq = q - tma_base;
-  if (dq < 0 || dq % rowb) return -1;
-  const int64_t r = dq / rowb;
-  return r + nrows <= ws_map_rows(rowb) ? (int)r : -1;
-}
 
 template <bool UP>
 __device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, int rb, int ks, int nw, int warp) {
@@ -251,7 +236,9 @@ __device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, i
   u.k0 = (warp % ks) * u.kc;
   u.nch = u.kc / ws_cc(u.kind);
   const int64_t rowb = (int64_t)K * (u.kind == kWsI4 ? 4 : u.kind == kWsI8 ? 8 : 16) / 8;
-  u.row0 = ws_row0(UP ? it.p_guq : it.p_dnq, p.tma_base, rowb, UP ? 2 * p.I : p.H);
+  // records lie on 4096-byte multiples above tma_base and the row pitches divide 4096 and the field
+  // offsets, so -1 means a record the runtime did not place
+  u.row0 = row_map_first(UP ? it.p_guq : it.p_dnq, p.tma_base, rowb, UP ? 2 * p.I : p.H);
   return u;
 }
 
@@ -560,9 +547,9 @@ cudaError_t launch_ws_phases(GemvParams& p, const moeb200_layout* lays, int nlay
   for (int i = 0; i < nlay && i < 4; ++i) {
     const int bits = gemv_wbits(lays[i].wtype);
     const int rb_up = p.H * bits / 8, rb_dn = p.I * bits / 8;
-    cudaError_t e = tma_rows2d_map(&tm.m[i][0], (uint64_t)p.tma_base, rb_up, ws_map_rows(rb_up), 8);
+    cudaError_t e = tma_rows2d_map(&tm.m[i][0], (uint64_t)p.tma_base, rb_up, row_map_rows(rb_up), 8);
     if (e != cudaSuccess) return e;
-    e = tma_rows2d_map(&tm.m[i][1], (uint64_t)p.tma_base, rb_dn, ws_map_rows(rb_dn), 16);
+    e = tma_rows2d_map(&tm.m[i][1], (uint64_t)p.tma_base, rb_dn, row_map_rows(rb_dn), 16);
     if (e != cudaSuccess) return e;
   }
   cudaError_t e = trace_mark(0, s);

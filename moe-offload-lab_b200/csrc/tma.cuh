@@ -39,6 +39,22 @@ __device__ __forceinline__ void retarget_tmap(const CUtensorMap& tmpl, uint32_t 
   __syncwarp();
 }
 
+// Row maps: a 2-D map of all memory from a base on (rows of rowb bytes) reads every record that lies
+// on a multiple of rowb above the base through the row coordinate. They cover kRowMapSpan bytes (every
+// record of a process lies well within) and at most 2^31 - 1 rows (int32 coordinates).
+constexpr int64_t kRowMapSpan = 1ll << 40;
+__host__ __device__ inline int64_t row_map_rows(int64_t rowb) {
+  return kRowMapSpan / rowb < 0x7fffffffll ? kRowMapSpan / rowb : 0x7fffffffll;
+}
+// First row of a field at q in a row map with rows of rowb bytes above base (nrows of the field must
+// fit), or -1 for a field that is not on a row of the map.
+__device__ __forceinline__ int row_map_first(int64_t q, int64_t base, int64_t rowb, int64_t nrows) {
+  const int64_t dq = q - base;
+  if (dq < 0 || dq % rowb) return -1;
+  const int64_t r = dq / rowb;
+  return r + nrows <= row_map_rows(rowb) ? (int)r : -1;
+}
+
 // Host: tensor-map template of a weight field, uint8 [rows][row_bytes] read in boxes of 128 bytes x
 // box_rows with 128-byte swizzle. The address is a placeholder (16-byte aligned device memory): the
 // kernels swap in each record's address. Cached per shape.
