@@ -50,9 +50,19 @@ __host__ __device__ inline int64_t row_map_rows(int64_t rowb) {
 // fit), or -1 for a field that is not on a row of the map.
 __device__ __forceinline__ int row_map_first(int64_t q, int64_t base, int64_t rowb, int64_t nrows) {
   const int64_t dq = q - base;
-  if (dq < 0 || dq % rowb) return -1;
-  const int64_t r = dq / rowb;
-  return r + nrows <= row_map_rows(rowb) ? (int)r : -1;
+  if (dq < 0) return -1;
+  int64_t r, rows;
+  if ((rowb & (rowb - 1)) == 0) {  // a power-of-two pitch (every pitch dividing 4096): shifts, no divisions
+    const int sh = __ffsll(rowb) - 1;
+    if (dq & (rowb - 1)) return -1;
+    r = dq >> sh;
+    rows = (kRowMapSpan >> sh) < 0x7fffffffll ? (kRowMapSpan >> sh) : 0x7fffffffll;
+  } else {
+    if (dq % rowb) return -1;
+    r = dq / rowb;
+    rows = row_map_rows(rowb);
+  }
+  return r + nrows <= rows ? (int)r : -1;
 }
 
 // Host: tensor-map template of a weight field, uint8 [rows][row_bytes] read in boxes of 128 bytes x
