@@ -86,6 +86,21 @@ __device__ __forceinline__ int ws_kind(int wtype) {
 __device__ __forceinline__ int ws_cc(int kind) {  // columns of one chunk
   return 64 * (kind == kWsI4 ? WsGeo<kWsI4>::NG : kind == kWsI8 ? WsGeo<kWsI8>::NG : WsGeo<kWsF>::NG);
 }
+__device__ __forceinline__ int ws_cc_log2(int kind) {  // log2 of ws_cc (512, 256, 128 columns)
+  return kind == kWsI4 ? 9 : kind == kWsI8 ? 8 : 7;
+}
+
+// n / d for 0 <= n and d >= 1 without an integer division sequence on the units' critical path:
+// for n < 2^22 the float quotient n * (1/d) (reciprocal correctly rounded) is within one of n / d, so
+// one remainder check makes it exact; larger n take the integer division.
+__device__ __forceinline__ int small_div(int n, int d, float inv) {
+  if (n >= (1 << 22)) return n / d;
+  int q = __float2int_rz(__int2float_rn(n) * inv);
+  const int r = n - q * d;
+  if (r < 0) --q;
+  else if (r >= d) ++q;
+  return q;
+}
 
 __device__ __forceinline__ uint2 lds64(uint32_t a) {
   uint2 v;
@@ -223,18 +238,19 @@ struct WsUnit {
 
 
 template <bool UP>
-__device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, int rb, int ks, int nw, int warp) {
+// ksl = log2 of the K parts (a power of two)
+__device__ __forceinline__ WsUnit ws_unit(const GemvParams& p, const Item& it, int rb, int ksl, int nw, int warp) {
   WsUnit u;
   u.it = it;
   u.kind = ws_kind(p.lay[it.slot].wtype);
   const int K = UP ? p.H : p.I;
   const int rows = UP ? p.I : p.H;
   const int rpt = UP ? 8 : 16;
-  u.r0 = (rb * (nw / ks) + warp / ks) * rpt;
+  u.r0 = (rb * (nw >> ksl) + (warp >> ksl)) * rpt;
   u.live = u.r0 < rows;
-  u.kc = K / ks;
-  u.k0 = (warp % ks) * u.kc;
-  u.nch = u.kc / ws_cc(u.kind);
+  u.kc = K >> ksl;
+  u.k0 = (warp & ((1 << ksl) - 1)) * u.kc;
+  u.nch = u.kc >> ws_cc_log2(u.kind);
   const int64_t rowb = (int64_t)K * (u.kind == kWsI4 ? 4 : u.kind == kWsI8 ? 8 : 16) / 8;
   // records lie on 4096-byte multiples above tma_base and the row pitches divide 4096 and the field
   // offsets, so -1 means a record the runtime did not place
@@ -302,8 +318,11 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
   uint8_t* myslot[2] = {slots + (warp * 2) * slot_bytes, slots + (warp * 2 + 1) * slot_bytes};
 
   const int rows = UP ? p.I : p.H;
-  const int rb_rows = (UP ? 8 : 16) * (NW / ks);
+  const int ksl = __ffs(ks) - 1;  // the K parts are a power of two
+  const int rb_rows = (UP ? 8 : 16) * (NW >> ksl);
   const int upi = (rows + rb_rows - 1) / rb_rows;  // units per item
+  // reciprocals for the per-unit quotients (small_div)
+  const float inv_upi = __frcp_rn((float)upi), inv_k = __frcp_rn((float)p.k);
 
   // the warp's chunk stream: units cu = blockIdx.x, +gridDim.x, ...; chunks of the warp's K part
   int n_items = 0;
@@ -316,12 +335,13 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
   auto load_unit = [&](int cu, WsUnit& u) -> bool {
     u.live = false;
     if (cu >= n_items * upi) return false;
-    const Item it = p.items[cu / upi];
+    const int item = small_div(cu, upi, inv_upi);
+    const Item it = p.items[item];
     if (it.ntok < 1 || it.ntok > xrows || it.slot < 0 || it.slot > 3) {
       if (lane == 0) atomicExch(p.status, kDevBadIndex);
       return true;
     }
-    u = ws_unit<UP>(p, it, cu % upi, ks, NW, warp);
+    u = ws_unit<UP>(p, it, cu - item * upi, ksl, NW, warp);
     if (u.live && u.row0 < 0) {  // a record off the tensor maps' rows: flagged, its unit skipped
       if (lane == 0) atomicExch(p.status, kDevBadIndex);
       u.live = false;
@@ -363,7 +383,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
 
   // activation rows of unit ordinal n into buffer n & 1 (thread 0)
   auto stage = [&](int cu, uint32_t n) {
-    const Item it = p.items[cu / upi];
+    const Item it = p.items[small_div(cu, upi, inv_upi)];
     uint64_t* bar = &xfull[n & 1];
     if (it.ntok < 1 || it.ntok > xrows) {  // flagged by load_unit; complete the phase empty
       mbar_arrive_expect_tx(bar, 0);
@@ -375,7 +395,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
     mbar_arrive_expect_tx(bar, rowb * it.ntok);
     uint8_t* dst = xbuf + (n & 1) * xrows * xstride;
     for (int j = 0; j < it.ntok; ++j) {
-      const uint8_t* src = UP ? static_cast<const uint8_t*>(p.x) + (int64_t)(p.pos[it.start + j] / p.k) * rowb
+      const uint8_t* src = UP ? static_cast<const uint8_t*>(p.x) + (int64_t)small_div(p.pos[it.start + j], p.k, inv_k) * rowb
                               : static_cast<const uint8_t*>(p.h) + (int64_t)(it.start + j) * rowb;
       bulk_g2s(dst + j * xstride, src, rowb, bar);
     }
@@ -431,7 +451,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
     if (ks > 1) {
       part[threadIdx.x] = make_float4(tot[0], tot[1], tot[2], tot[3]);
       __syncthreads();
-      if (warp % ks == 0) {
+      if ((warp & (ks - 1)) == 0) {
         for (int q = 1; q < ks; ++q) {
           const float4 v = part[threadIdx.x + 32 * q];
           tot[0] += v.x;
@@ -441,7 +461,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
         }
       }
     }
-    if (valid && warp % ks == 0 && ok) {
+    if (valid && (warp & (ks - 1)) == 0 && ok) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int tk = 2 * t + e;
@@ -451,7 +471,7 @@ __global__ void __launch_bounds__(32 * NW, 1) ws_kernel(const GemvParams p, cons
           static_cast<AT*>(p.h)[(int64_t)j * p.I + u.r0 + g] = from_f32<AT>(silu_mul(tot[e], tot[2 + e]));
         } else {
           const int pos = p.pos[j];
-          float* arow = p.acc + (int64_t)(pos / p.k) * p.H + u.r0;
+          float* arow = p.acc + (int64_t)small_div(pos, p.k, inv_k) * p.H + u.r0;
           const float wv = p.wflat[pos];
           red_add_f32(arow + g, wv * tot[e]);
           red_add_f32(arow + 8 + g, wv * tot[2 + e]);
