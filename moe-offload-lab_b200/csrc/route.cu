@@ -322,15 +322,25 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     idx[(int64_t)t * kk + k] = E;
   }
   if (with_levels) {
-    __syncwarp();
-    if (lane == 0) {
-      float wl[32];
-      for (int j = 0; j < k; ++j) wl[j] = w[(int64_t)t * kk + j];
-      token_levels(wl, k, pol, level + (int64_t)t * kk, skip ? skip + (int64_t)t * kk : nullptr);
-      if (shared_level >= 0) {
-        level[(int64_t)t * kk + k] = (uint8_t)shared_level;
-        if (skip) skip[(int64_t)t * kk + k] = 0;
+    if (pol.mode != 2) {
+      // hi / lo / threshold: a pair's level depends on its own weight only, which lane j holds
+      if (lane < k) {
+        level[(int64_t)t * kk + lane] = pol.mode == 0 ? 0 : pol.mode == 1 ? 2 : (wsel >= pol.thr ? 0 : 2);
+        if (skip) skip[(int64_t)t * kk + lane] = 0;
       }
+    } else {
+      // HOBBIT ranks the token's pairs: lane 0 gathers the k weights from their lanes (no read-back
+      // from global memory) and runs the serial rule
+      float wl[32];
+      for (int j = 0; j < k; ++j) {
+        const float v = __shfl_sync(0xffffffffu, wsel, j);
+        if (lane == 0) wl[j] = v;
+      }
+      if (lane == 0) token_levels(wl, k, pol, level + (int64_t)t * kk, skip ? skip + (int64_t)t * kk : nullptr);
+    }
+    if (shared_level >= 0 && lane == 0) {
+      level[(int64_t)t * kk + k] = (uint8_t)shared_level;
+      if (skip) skip[(int64_t)t * kk + k] = 0;
     }
   }
 }
