@@ -59,7 +59,9 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const AT* __restrict
     for (int q = 0; q < RT; ++q) acc[r][q] = 0.f;
   // raw 16-byte words of the step, converted element by element (a tile of RE x RT keeps RE + RT
   // words, not RE * 8 converted floats, in registers)
-#pragma unroll 2
+  // small tiles: eight column steps' loads in flight at once (a 2,048-column row in one L2 round trip)
+  constexpr int kUnroll = RE * RT <= 4 ? 8 : 2;
+#pragma unroll kUnroll
   for (int c = lane * 8; c < H; c += 256) {
     uint4 wv[RE], xv[RT];
 #pragma unroll
@@ -471,8 +473,22 @@ __device__ int32_t block_exclusive_scan(int32_t (&v)[PER], int32_t* sh_warp) {
 // With cnt_k/cnt_e (a single dispatch block whose counts are in shared memory) the totals are read
 // there and the first positions are also left in offk_s/offe_s; otherwise the per-block counts in
 // global memory are turned into per-(block, key) prefixes on the way.
+constexpr int kKeysPerThread = kMaxKeys / 1024;  // slot-major keys of each thread of a 1024-thread block
+
+// Record address of each of the thread's slot-major keys m = slot * E + expert (the table's own
+// index; 0 = not resident or no table), loaded first so that the load overlaps the pair loads
+__device__ __forceinline__ void load_key_records(const DispatchParams& p, int64_t (&rec)[kKeysPerThread]) {
+  const int keys = p.E * p.P;
+#pragma unroll
+  for (int i = 0; i < kKeysPerThread; ++i) {
+    const int m = threadIdx.x * kKeysPerThread + i;
+    rec[i] = (p.items != nullptr && p.table != nullptr && m < keys) ? p.table[m] : 0;
+  }
+}
+
+// rec_pre: the thread's key records from load_key_records
 __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const int32_t* cnt_e, int32_t* offk_s,
-                            int32_t* offe_s, int32_t* sh_warp) {
+                            int32_t* offe_s, int32_t* sh_warp, const int64_t (&rec_pre)[kKeysPerThread]) {
   __shared__ int32_t tot_s[kMaxKeys];    // pairs per key
   __shared__ int32_t offk_sh[kMaxKeys];  // first sorted position per key
   const int keys = p.E * p.P;
@@ -480,7 +496,7 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
   if (tid == 0 && p.miss) *p.miss = 0;
   for (int i = tid; i < p.zero_n; i += blockDim.x) p.zero_cnt[i] = 0;
   __syncthreads();
-  constexpr int PER = kMaxKeys / 1024;
+  constexpr int PER = kKeysPerThread;
   int32_t tot_k[PER], tot_e[PER], nit[PER];
   int64_t rec_i[PER];  // record address of each of the thread's slot-major keys (loaded once)
 #pragma unroll
@@ -539,7 +555,7 @@ __device__ void finish_keys(const DispatchParams& p, const int32_t* cnt_k, const
       const int sl = m / p.E, ex = m % p.E;
       const int32_t run = tot_s[ex * p.P + sl];
       if (run > 0) {
-        rec = p.table ? p.table[(int64_t)sl * p.E + ex] : 0;
+        rec = p.table ? rec_pre[i] : 0;  // p.table[sl * E + ex]
         if (rec != 0 || !p.table) ni = (run + p.nt - 1) / p.nt;
         else if (p.miss) atomicAdd(p.miss, run);
       }
@@ -623,7 +639,9 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchParams p) {
   __shared__ int32_t sh_warp[32];
   chain_wait();
   chain_release();
-  finish_keys(p, nullptr, nullptr, nullptr, nullptr, sh_warp);
+  int64_t rec[kKeysPerThread];
+  load_key_records(p, rec);
+  finish_keys(p, nullptr, nullptr, nullptr, nullptr, sh_warp, rec);
 }
 
 // D1+D2+D3 in one block of 1024 threads when all pairs fit one dispatch block (T*k <= kDispBlock):
@@ -636,6 +654,8 @@ __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) 
   __shared__ int32_t sh_warp[32];
   chain_wait();
   chain_release();
+  int64_t rec[kKeysPerThread];
+  load_key_records(p, rec);
   const int keys = p.E * p.P;
   int32_t* cnt_k = sh;                 // [keys]
   int32_t* cnt_e = cnt_k + keys;       // [E]
@@ -655,7 +675,7 @@ __global__ void __launch_bounds__(1024) dispatch_fused_kernel(DispatchParams p) 
     se = atomicAdd(&cnt_e[e], 1);
   }
   __syncthreads();
-  finish_keys(p, cnt_k, cnt_e, offk, offe, sh_warp);
+  finish_keys(p, cnt_k, cnt_e, offk, offe, sh_warp, rec);
   __syncthreads();
   if (key >= 0) {
     bk_s[offk[key] + sk] = tid;
