@@ -682,9 +682,10 @@ int experts_forward_impl(const moeb200_expert_table* ex, int32_t e_lo, int32_t e
   if (g_path == 4 && !ws_ok)
     return fail(MOEB200_ERR_UNSUPPORTED, "warp-streamed GEMV: these record layouts, shapes or the x alignment are "
                                          "not supported");
-  // automatic path: the warp-streamed GEMV for single-token calls (measured, 16 layers of config 1:
-  // 1,323 against 1,189 tokens/s at T = 1, even at T = 2 and 4, 12 % behind at T = 8)
-  const bool streamed = !gemm && !decode && (g_path == 4 || (g_path == 0 && T == 1 && ws_ok));
+  // automatic path: the warp-streamed GEMV for calls of up to 8 tokens (measured, 16 layers of
+  // config 1, against the CTA-pipeline GEMV: T = 2 2,440 / 2,100 tokens/s, T = 4 3,649 / 3,414,
+  // T = 8 5,449 / 5,434)
+  const bool streamed = !gemm && !decode && (g_path == 4 || (g_path == 0 && T <= 8 && ws_ok));
   // (the warp-streamed GEMV stages at most min(8, T) activation rows per item)
   const int nt = gemm ? 128 : decode ? 8 : streamed ? std::min(8, T) : g_item_tokens ? g_item_tokens : (T >= 64 ? 16 : 8);
   g_last_path = gemm ? 2 : decode ? 3 : streamed ? 4 : 1;
