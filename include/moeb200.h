@@ -91,8 +91,8 @@ int moeb200_last_error(char* buf, size_t n);
 int moeb200_num_sms(void);
 
 /* Expert-product path of the following moeb200_experts_forward calls on the calling thread
- * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 16*E, else the two-launch
- * grouped GEMV), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128), 3 = the fused
+ * (no reference counterpart): 0 = automatic (tcgen05 GEMM when T*k >= 40*E; else the warp-streamed
+ * GEMV of path 4 for T <= 8 where it applies, else the two-launch grouped GEMV), 1 = grouped GEMV, 2 = tcgen05 GEMM (needs H and I multiples of 128), 3 = the fused
  * one-launch decode kernel (int4/int8 records with group size 64 or float records of the activation
  * type, H and I multiples of 64 up to 2048, a table with tma_base; refused with
  * MOEB200_ERR_UNSUPPORTED where it does not apply), 4 = the warp-streamed grouped GEMV (items of at
