@@ -7,8 +7,8 @@ host, with no GPU involved:
   PeerFailure after the process group's short timeout.
 
 In both cases the surviving rank's ExpertParallel then refuses the next layer at once (no further
-collective is entered). The reference runs on one GPU and has no exchange to fail (SURVEY: moelab
-switches to its torch path on a kernel exception, runtime.py:346-348)."""
+collective is entered). The reference runs on one GPU and has no exchange to fail (moelab switches
+to its torch path on a kernel exception, moelab/runtime.py:346-348)."""
 
 from __future__ import annotations
 
